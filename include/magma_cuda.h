@@ -1,0 +1,285 @@
+/*
+ * magma_cuda.h — C ABI of libmagma_cuda.so, the sm_100a (B200) execution
+ * backend for the fused ops that Magma's LazyTensor graph emits for a
+ * training step: LayerNorm fwd/bwd, causal attention fwd/bwd, the Linear
+ * contraction (GEMM), the generic Adam update, and the glue ops on the same
+ * graphs (embedding, softmax cross-entropy, GELU/ReLU, bias gradient,
+ * dtype conversion).
+ *
+ * Conventions follow Magma's PJRT C shim
+ * (Sources/CXLARuntime/include/PJRTSimpleWrapper.h):
+ *   - every entry point returns a status code whose values are those of
+ *     SW_PJRT_Error_Code (PJRTSimpleWrapper.h:32-50);
+ *   - dtypes use the values of SW_PJRT_Buffer_Type (PJRTSimpleWrapper.h:52-71),
+ *     so F32 = 10 and BF16 = 12 on both sides of the boundary;
+ *   - a failing call records a message in thread-local storage, read with
+ *     magma_get_last_error_message() and cleared with
+ *     magma_clear_last_error_message() (PJRTSimpleWrapper.h:86-99);
+ *   - buffers are plain device pointers owned by the caller, who allocates
+ *     and frees them (as with PJRT_CreateBuffer / PJRT_DestroyBuffer,
+ *     PJRTSimpleWrapper.h:174-232). Outputs are written into caller-provided
+ *     buffers. Ops that need scratch memory take a caller-provided workspace
+ *     and export a *_workspace_size query; the library never allocates device
+ *     memory on an op path;
+ *   - every op is asynchronous on the `stream` argument (a cudaStream_t passed
+ *     as void*; NULL is the legacy default stream). Calls on distinct streams
+ *     from distinct threads are independent.
+ *
+ * Layouts are row-major. Integer sizes are int64_t; strides are in elements.
+ */
+#ifndef MAGMA_CUDA_H_
+#define MAGMA_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MAGMA_API __attribute__((visibility("default")))
+#else
+#define MAGMA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes: values of SW_PJRT_Error_Code (PJRTSimpleWrapper.h:32-50) */
+typedef int32_t magma_status_t;
+#define MAGMA_OK 0
+#define MAGMA_CANCELLED 1
+#define MAGMA_UNKNOWN 2
+#define MAGMA_INVALID_ARGUMENT 3
+#define MAGMA_DEADLINE_EXCEEDED 4
+#define MAGMA_NOT_FOUND 5
+#define MAGMA_RESOURCE_EXHAUSTED 8
+#define MAGMA_FAILED_PRECONDITION 9
+#define MAGMA_OUT_OF_RANGE 11
+#define MAGMA_UNIMPLEMENTED 12
+#define MAGMA_INTERNAL 13
+#define MAGMA_UNAVAILABLE 14
+
+/* ---- dtypes: values of SW_PJRT_Buffer_Type (PJRTSimpleWrapper.h:52-71) */
+typedef int32_t magma_dtype_t;
+#define MAGMA_DTYPE_S32 3
+#define MAGMA_DTYPE_S64 4
+#define MAGMA_DTYPE_F32 10
+#define MAGMA_DTYPE_BF16 12
+
+/* ---- GEMM epilogues (fused into the contraction's store) */
+#define MAGMA_EPI_NONE 0          /* c = acc                                   */
+#define MAGMA_EPI_BIAS 1          /* c = acc + bias[col]                       */
+#define MAGMA_EPI_BIAS_GELU 2     /* aux_out = acc + bias; c = gelu(aux_out)   */
+#define MAGMA_EPI_BIAS_RESIDUAL 3 /* c = aux_in + (acc + bias[col]); aux_in f32 */
+#define MAGMA_EPI_DGELU 4         /* c = acc * gelu'(aux_in)                   */
+#define MAGMA_EPI_ACCUMULATE 5    /* c = c + acc  (c must be f32)              */
+#define MAGMA_EPI_BIAS_RELU 6     /* aux_out = acc + bias; c = relu(aux_out)   */
+#define MAGMA_EPI_DRELU 7         /* c = acc * (aux_in > 0)                    */
+
+/* ---- errors (PJRTSimpleWrapper.h:86-99) ------------------------------------ */
+
+/* Message of the most recent failure on the calling thread, or NULL. */
+MAGMA_API const char* magma_get_last_error_message(void);
+/* Clears the calling thread's last error message. */
+MAGMA_API void magma_clear_last_error_message(void);
+/* ABI version of this header (major*10000 + minor*100 + patch). */
+MAGMA_API int32_t magma_abi_version(void);
+
+/* ---- runtime: device, streams, memory (the PJRTClient/PJRTBuffer surface of
+ *      Sources/XLARuntime/XLARuntime.swift:407-923, without XLA) ------------- */
+
+MAGMA_API magma_status_t magma_device_count(int32_t* count);
+/* Makes `device_ordinal` current on the calling thread and checks that it is an
+ * sm_100 device; records the device's SM count for grid sizing. */
+MAGMA_API magma_status_t magma_init(int32_t device_ordinal);
+MAGMA_API magma_status_t magma_stream_create(void** stream);
+MAGMA_API magma_status_t magma_stream_destroy(void* stream);
+MAGMA_API magma_status_t magma_stream_synchronize(void* stream);
+MAGMA_API magma_status_t magma_malloc(void** ptr, size_t bytes);
+MAGMA_API magma_status_t magma_free(void* ptr);
+/* Asynchronous copies on `stream`; synchronize the stream before reading. */
+MAGMA_API magma_status_t magma_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+MAGMA_API magma_status_t magma_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+MAGMA_API magma_status_t magma_memset(void* dst, int32_t value, size_t bytes, void* stream);
+/* Synchronizes `stream`, then reads and clears the device-side error word
+ * that kernels with bounded waits set when a wait times out. Returns
+ * MAGMA_DEADLINE_EXCEEDED (and the kernel's code in *code) if one did. */
+MAGMA_API magma_status_t magma_device_error_check(void* stream, int32_t* code);
+
+/* ---- LayerNorm ---------------------------------------------------------------
+ * Replaces nn.LayerNorm.forward (Sources/Core/Module.swift:2754-2791) and the
+ * GPT block's layerNorm (Benchmarks/GPT2Shakespeare/Sources/main.swift:364-375):
+ *   mean = sum(x)/D; var = sum((x-mean)^2)/D; std = sqrt(var + eps);
+ *   y = ((x - mean) / std) * gamma + beta.
+ * x [rows, dim] in x_dtype (F32|BF16); y in y_dtype (F32|BF16); gamma, beta,
+ * mean[rows], rstd[rows] = 1/std are F32. */
+MAGMA_API magma_status_t magma_layernorm_fwd(const void* x, const float* gamma, const float* beta,
+                                   void* y, float* mean, float* rstd,
+                                   int64_t rows, int64_t dim, float eps,
+                                   magma_dtype_t x_dtype, magma_dtype_t y_dtype,
+                                   void* stream);
+
+/* Bytes of workspace magma_layernorm_bwd needs for (rows, dim). */
+MAGMA_API size_t magma_layernorm_bwd_workspace_size(int64_t rows, int64_t dim);
+
+/* Replaces the autodiff chain of the LayerNorm above (vjpDivide, vjpSqrt,
+ * vjpMeanDims, vjpMultiply/vjpAdd with sumAlongBroadcastDims:
+ * Sources/Core/Autodiff.swift:57-94,221-257,351-370, Optimizer.swift:627-633):
+ *   dx = rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy*gamma;
+ *   dgamma = sum_rows dy*xhat; dbeta = sum_rows dy (fixed summation order).
+ * accumulate_dx != 0 adds into dx (dx must then be F32); accumulate_params != 0
+ * adds into dgamma/dbeta. */
+MAGMA_API magma_status_t magma_layernorm_bwd(const void* dy, const void* x, const float* gamma,
+                                   const float* mean, const float* rstd,
+                                   void* dx, float* dgamma, float* dbeta,
+                                   int64_t rows, int64_t dim,
+                                   magma_dtype_t dy_dtype, magma_dtype_t x_dtype,
+                                   magma_dtype_t dx_dtype,
+                                   int32_t accumulate_dx, int32_t accumulate_params,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Linear contraction (GEMM) ------------------------------------------------
+ * Replaces Tensor.matmul -> stablehlo.dot (Sources/Core/Tensor.swift:1102-1121,
+ * Sources/StableHLO/Builder/MLIRBuilder.swift:372-378) as used by value Linear
+ * (ValueLayers.swift:38-41, x.W + b), nn.Linear (Module.swift:266-300,
+ * x.W^T + b), the GPT linear (main.swift:353-362), and their VJPs
+ * (Autodiff.swift:177-191): c[m,n] = sum_k opA[m,k] * opB[k,n], then the
+ * epilogue.
+ *   trans_a = 0: A stored [m, k] (lda >= k); 1: A stored [k, m] (lda >= m).
+ *   trans_b = 0: B stored [k, n] (ldb >= n); 1: B stored [n, k] (ldb >= k).
+ *   c stored [m, n] (ldc >= n). ab_dtype F32 or BF16; BF16 runs on the tcgen05
+ *   tensor cores with F32 accumulation, F32 runs an F32 FFMA kernel.
+ *   c_dtype F32 or BF16. bias is F32 [n]. aux_in / aux_out are [m, n] with
+ *   leading dimension ldc: aux_in F32 for BIAS_RESIDUAL, else c_dtype-typed
+ *   pre-activations; aux_out has c_dtype.
+ * BF16 operands need 16-byte aligned base pointers and leading dimensions that
+ * are multiples of 8 elements (TMA). */
+MAGMA_API size_t magma_gemm_workspace_size(int64_t m, int64_t n, int64_t k, magma_dtype_t ab_dtype);
+MAGMA_API magma_status_t magma_gemm(const void* a, const void* b, void* c,
+                          int64_t m, int64_t n, int64_t k,
+                          int64_t lda, int64_t ldb, int64_t ldc,
+                          int32_t trans_a, int32_t trans_b,
+                          magma_dtype_t ab_dtype, magma_dtype_t c_dtype,
+                          int32_t epilogue, const float* bias,
+                          const void* aux_in, void* aux_out,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- causal scaled-dot-product attention -----------------------------------
+ * Replaces nn.scaledDotProductAttention (Module.swift:2408-2441) and the GPT
+ * block's attention (main.swift:467-481): S = (Q K^T) * scale, masked entries
+ * (key > query when causal) set to -1e9 (main.swift:793-801), P = softmax(S),
+ * O = P V. Q, K, V, O have logical shape [batch, heads, seq, head_dim]; element
+ * (b, h, s, d) lives at base + b*strides[0] + h*strides[1] + s*strides[2] + d.
+ * qkv_strides applies to Q, K and V; o_strides to O and dO (and dQ/dK/dV use
+ * qkv_strides). lse [batch, heads, seq] F32 receives the row log-sum-exp of the
+ * scaled, masked scores. dtype F32 or BF16; head_dim 64 (BF16) or <= 128 (F32). */
+MAGMA_API magma_status_t magma_attention_fwd(const void* q, const void* k, const void* v,
+                                   void* o, float* lse,
+                                   int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                                   const int64_t* qkv_strides, const int64_t* o_strides,
+                                   float scale, int32_t causal, magma_dtype_t dtype,
+                                   void* stream);
+
+MAGMA_API size_t magma_attention_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq,
+                                          int64_t head_dim, magma_dtype_t dtype);
+
+/* Replaces the attention VJP chain (vjpBatchedMatmul Autodiff.swift:309-317,
+ * vjpSoftmax :379-386, the scale multiply VJP :76-82, mask add VJP): with
+ * P recomputed from lse, dV = P^T dO; dP = dO V^T; dS = P * (dP - rowsum(dO*O));
+ * dQ = scale * dS K; dK = scale * dS^T Q. */
+MAGMA_API magma_status_t magma_attention_bwd(const void* q, const void* k, const void* v,
+                                   const void* o, const void* d_o, const float* lse,
+                                   void* dq, void* dk, void* dv,
+                                   int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                                   const int64_t* qkv_strides, const int64_t* o_strides,
+                                   float scale, int32_t causal, magma_dtype_t dtype,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Adam -----------------------------------------------------------------
+ * Replaces optim.Adam.step (Sources/Core/Optimizer.swift:354-412) and the value
+ * Adam.update (Sources/Core/TangentOptimizer.swift:99-135), element-wise over a
+ * flat F32 arena, in the reference's op order:
+ *   g = grad * grad_scale;
+ *   if weight_decay: p = p - p * (lr*weight_decay);
+ *   m = m*beta1 + g*(1-beta1);  v = v*beta2 + (g*g)*(1-beta2);
+ *   p = p - (m/bc1) / (sqrt(v/bc2) + eps) * lr,  bc_i = 1 - beta_i^step (F32).
+ * step counts from 1. If shadow_bf16 is non-NULL the updated parameters are
+ * also written there rounded to BF16 (round-to-nearest-even). */
+MAGMA_API magma_status_t magma_adam_step(float* params, const float* grads, float* m, float* v,
+                               void* shadow_bf16, int64_t n,
+                               float lr, float beta1, float beta2, float eps,
+                               float weight_decay, int64_t step, float grad_scale,
+                               void* stream);
+
+/* Same update over `count` separate tensors in one launch (multi-tensor apply);
+ * the pointer and size arrays are host arrays. */
+MAGMA_API magma_status_t magma_adam_step_multi(float* const* params, const float* const* grads,
+                                     float* const* m, float* const* v,
+                                     const int64_t* sizes, int32_t count,
+                                     float lr, float beta1, float beta2, float eps,
+                                     float weight_decay, int64_t step, float grad_scale,
+                                     void* stream);
+
+/* ---- glue ops on the same graphs ------------------------------------------ */
+
+/* Token + position embedding gather (Sources/Core/Data.swift:856-886, GPT
+ * main.swift:454-458): out[b*seq+s, :] = wte[tokens[b*seq+s], :] + wpe[s, :].
+ * wte [vocab, dim], wpe [>=seq, dim], out [batch*seq, dim]; all F32.
+ * Out-of-range token ids are an error recorded in the device error word. */
+MAGMA_API magma_status_t magma_embedding_fwd(const int32_t* tokens, const float* wte, const float* wpe,
+                                   float* out, int64_t batch, int64_t seq, int64_t dim,
+                                   int64_t vocab, void* stream);
+
+/* Embedding VJP (the one-hot matmul of Data.swift:890-907, as a scatter-add):
+ * dwte[tokens[r], :] += dout[r, :]; dwpe[s, :] += sum_b dout[b*seq+s, :].
+ * Both accumulate into their outputs (F32). dwpe may be NULL. */
+MAGMA_API magma_status_t magma_embedding_bwd(const int32_t* tokens, const float* dout,
+                                   float* dwte, float* dwpe,
+                                   int64_t batch, int64_t seq, int64_t dim, int64_t vocab,
+                                   void* stream);
+
+/* Softmax cross-entropy with class-index targets, forward and backward in one
+ * pass (main.swift:412-433, Loss.swift:627-699): for each row r of logits
+ * [rows, classes] (leading dimension ld), losses[r] = logsumexp(row) -
+ * row[targets[r]], and the row is overwritten in place with
+ * grad_scale * (softmax(row) - onehot(targets[r])); columns in [classes, ld)
+ * are set to zero. dtype F32 or BF16 (F32 math). */
+MAGMA_API magma_status_t magma_cross_entropy_fwd_bwd(void* logits, const int32_t* targets, float* losses,
+                                           int64_t rows, int64_t classes, int64_t ld,
+                                           float grad_scale, magma_dtype_t dtype, void* stream);
+
+/* Deterministic sum of n F32 values into out[0] (e.g. the mean loss with
+ * scale = 1/n). */
+MAGMA_API magma_status_t magma_reduce_sum(const float* x, float* out, int64_t n, float scale, void* stream);
+
+/* GELU (tanh form, StableHLOEmitter.swift:804-816) and its VJP
+ * (Autodiff.swift:401-418), element-wise; dtype F32 or BF16. */
+MAGMA_API magma_status_t magma_gelu_fwd(const void* x, void* y, int64_t n, magma_dtype_t dtype, void* stream);
+MAGMA_API magma_status_t magma_gelu_bwd(const void* x, const void* dy, void* dx, int64_t n,
+                              magma_dtype_t dtype, void* stream);
+/* ReLU (Tensor.swift:1386) and its VJP (Autodiff.swift:119-135). */
+MAGMA_API magma_status_t magma_relu_fwd(const void* x, void* y, int64_t n, magma_dtype_t dtype, void* stream);
+MAGMA_API magma_status_t magma_relu_bwd(const void* x, const void* dy, void* dx, int64_t n,
+                              magma_dtype_t dtype, void* stream);
+
+/* Bias gradient: dbias[c] (+)= sum_r dy[r, c] over dy [rows, cols] (leading
+ * dimension ld) in a fixed order (sumAlongBroadcastDims, Autodiff.swift:221-257).
+ * dy F32 or BF16; dbias F32. */
+MAGMA_API size_t magma_bias_grad_workspace_size(int64_t rows, int64_t cols);
+MAGMA_API magma_status_t magma_bias_grad(const void* dy, float* dbias, int64_t rows, int64_t cols,
+                               int64_t ld, magma_dtype_t dtype, int32_t accumulate,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* dtype conversion (Tensor.swift:2069-2130; F32 -> BF16 rounds to nearest even
+ * as LazyTensor.swift:1511-1516 does). */
+MAGMA_API magma_status_t magma_convert(const void* src, void* dst, int64_t n,
+                             magma_dtype_t src_dtype, magma_dtype_t dst_dtype, void* stream);
+
+/* y = y * alpha (F32), e.g. the 1/n of allReduceMean (MLIRBuilder.swift:923-929)
+ * applied after a sum all-reduce. */
+MAGMA_API magma_status_t magma_scale(float* y, int64_t n, float alpha, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* MAGMA_CUDA_H_ */

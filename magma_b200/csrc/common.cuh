@@ -1,0 +1,154 @@
+// Shared helpers for libmagma_cuda.so: status/last-error plumbing, dtype
+// traits, BF16 packing, warp reductions and the device-side error word.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/magma_cuda.h"
+
+namespace magma {
+
+// Records a printf-style message as the calling thread's last error and
+// returns `code` (the PJRT shim's "copy the message, return the code" rule,
+// PJRTSimpleWrapper.h:86-99).
+magma_status_t fail(magma_status_t code, const char* fmt, ...);
+
+// Maps a CUDA runtime error to a status + message; MAGMA_OK if err == success.
+magma_status_t cuda_status(cudaError_t err, const char* what);
+
+// Checks the launch that just happened on this thread.
+inline magma_status_t check_launch(const char* what) {
+  return cuda_status(cudaGetLastError(), what);
+}
+
+// SM count of the current device (cached per device ordinal).
+int num_sms();
+
+// Device address of the error word that bounded waits set on timeout
+// (one per device, found once per device with cudaGetSymbolAddress).
+int* device_error_word();
+
+// Error codes kernels write into the device error word.
+enum DeviceErrorCode : int {
+  kDevErrNone = 0,
+  kDevErrWaitTimeout = 1,   // an mbarrier/flag wait exceeded its iteration cap
+  kDevErrBadIndex = 2,      // a token id / target outside [0, vocab)
+};
+
+inline size_t dtype_size(magma_dtype_t t) {
+  switch (t) {
+    case MAGMA_DTYPE_F32: return 4;
+    case MAGMA_DTYPE_BF16: return 2;
+    case MAGMA_DTYPE_S32: return 4;
+    case MAGMA_DTYPE_S64: return 8;
+    default: return 0;
+  }
+}
+
+inline bool is_float_dtype(magma_dtype_t t) {
+  return t == MAGMA_DTYPE_F32 || t == MAGMA_DTYPE_BF16;
+}
+
+inline const char* dtype_name(magma_dtype_t t) {
+  switch (t) {
+    case MAGMA_DTYPE_F32: return "F32";
+    case MAGMA_DTYPE_BF16: return "BF16";
+    case MAGMA_DTYPE_S32: return "S32";
+    case MAGMA_DTYPE_S64: return "S64";
+    default: return "UNSUPPORTED";
+  }
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- element load/store as F32 -------------------------------------------
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// Loads 8 consecutive elements (16 B for BF16, 32 B for F32) as F32.
+// The address must be aligned to the vector size.
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+// Records the first device-side error (later errors keep the first code).
+__device__ __forceinline__ void set_device_error(int* word, int code) {
+  if (word != nullptr) atomicCAS(word, 0, code);
+}
+
+// GELU, tanh form, in the op order of StableHLOEmitter.swift:804-816:
+//   x3 = x*(x*x); inner = x + 0.044715*x3; t = tanh(0.7978845608*inner);
+//   y = 0.5*(x*(1+t)).
+__device__ __forceinline__ float gelu_f(float x) {
+  float x3 = __fmul_rn(x, __fmul_rn(x, x));
+  float inner = __fadd_rn(x, __fmul_rn(0.044715f, x3));
+  float t = tanhf(__fmul_rn(0.7978845608f, inner));
+  return __fmul_rn(0.5f, __fmul_rn(x, __fadd_rn(1.0f, t)));
+}
+// GELU derivative, Autodiff.swift:401-418:
+//   u = c*(x + a*x^3); t = tanh(u); u' = c*(1 + 3a*x^2);
+//   g' = 0.5*(1+t) + 0.5*x*(1-t*t)*u'.
+__device__ __forceinline__ float gelu_grad_f(float x) {
+  const float c = 0.7978845608f, a = 0.044715f;
+  float x2 = __fmul_rn(x, x);
+  float u = __fmul_rn(c, __fadd_rn(x, __fmul_rn(a, __fmul_rn(x2, x))));
+  float t = tanhf(u);
+  float up = __fmul_rn(c, __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f, a), x2)));
+  float left = __fmul_rn(0.5f, __fadd_rn(1.0f, t));
+  float right = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, x), __fsub_rn(1.0f, __fmul_rn(t, t))), up);
+  return __fadd_rn(left, right);
+}
+
+}  // namespace magma
+
+// Argument-check helper used at the top of every entry point.
+#define MAGMA_REQUIRE(cond, ...)                                   \
+  do {                                                             \
+    if (!(cond)) return ::magma::fail(MAGMA_INVALID_ARGUMENT, __VA_ARGS__); \
+  } while (0)

@@ -1,0 +1,564 @@
+// The Linear contraction: c = opA(a) . opB(b) with a fused epilogue.
+//
+// Replaces Tensor.matmul -> stablehlo.dot (Sources/Core/Tensor.swift:1102-1121,
+// Sources/StableHLO/Builder/MLIRBuilder.swift:372-378) as emitted by the value
+// Linear (ValueLayers.swift:38-41), nn.Linear (Module.swift:266-300), the GPT
+// linear (main.swift:353-362) and the matmul VJP (Autodiff.swift:177-191). The
+// transposes that the reference materialises in the graph become operand
+// majorness here (no transpose kernels), and the bias add / activation /
+// residual add / activation VJP that follow the dot are fused into the store.
+//
+// BF16 path: a persistent, warp-specialised tcgen05 kernel.
+//   warp 0      TMA producer: 128x64 A and BNx64 B tiles, 128-byte swizzle,
+//               into a STAGES-deep shared-memory ring (full/empty mbarriers);
+//   warp 1      TMEM allocator and MMA issuer: one thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) into one
+//               of two TMEM accumulators (2 x BN columns) and commits;
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = row), fused
+//               epilogue math, 16-byte global stores; the accumulator is handed
+//               back to the MMA warp so the next tile's MMAs overlap this store.
+// Operands may be K-major or MN-major (instruction-descriptor bits 15/16),
+// which covers x.W^T (forward), dY.W (input gradient) and X^T.dY (weight
+// gradient) without copies.
+//
+// F32 path: a register-blocked FFMA kernel (128x128 tile, 8x8 per thread).
+// It is the fp32-accurate contraction for the fp32 configurations (the tensor
+// cores' TF32 would miss a 1e-4 relative tolerance) and the path for shapes
+// TMA cannot describe.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace magma {
+namespace {
+
+struct EpiArgs {
+  int epi;
+  const float* bias;
+  const void* aux_in;
+  void* aux_out;
+  int64_t ldc;
+};
+
+template <typename TC>
+__device__ __forceinline__ float epi_value(const EpiArgs& e, const TC* C, int64_t off, int64_t col,
+                                           float acc) {
+  switch (e.epi) {
+    case MAGMA_EPI_NONE:
+      return acc;
+    case MAGMA_EPI_BIAS:
+      return e.bias ? __fadd_rn(acc, e.bias[col]) : acc;
+    case MAGMA_EPI_BIAS_GELU: {
+      float pre = e.bias ? __fadd_rn(acc, e.bias[col]) : acc;
+      static_cast<TC*>(e.aux_out)[off] = from_f32<TC>(pre);
+      return gelu_f(pre);
+    }
+    case MAGMA_EPI_BIAS_RESIDUAL: {
+      float t = e.bias ? __fadd_rn(acc, e.bias[col]) : acc;
+      return __fadd_rn(static_cast<const float*>(e.aux_in)[off], t);
+    }
+    case MAGMA_EPI_DGELU:
+      return __fmul_rn(acc, gelu_grad_f(to_f32(static_cast<const TC*>(e.aux_in)[off])));
+    case MAGMA_EPI_ACCUMULATE:
+      return __fadd_rn(to_f32(C[off]), acc);
+    case MAGMA_EPI_BIAS_RELU: {
+      float pre = e.bias ? __fadd_rn(acc, e.bias[col]) : acc;
+      static_cast<TC*>(e.aux_out)[off] = from_f32<TC>(pre);
+      return fmaxf(pre, 0.f);
+    }
+    case MAGMA_EPI_DRELU:
+      return to_f32(static_cast<const TC*>(e.aux_in)[off]) > 0.f ? acc : 0.f;
+    default:
+      return acc;
+  }
+}
+
+// ============================== F32 FFMA kernel ==============================
+constexpr int kSimtBM = 128, kSimtBN = 128, kSimtBK = 8;
+
+template <typename TA, typename TC, bool TA_T, bool TB_T>
+__global__ void __launch_bounds__(256)
+gemm_simt_kernel(const TA* __restrict__ A, const TA* __restrict__ B, TC* __restrict__ C,
+                 int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, EpiArgs e) {
+  __shared__ float As[2][kSimtBK][kSimtBM + 4];
+  __shared__ float Bs[2][kSimtBK][kSimtBN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * kSimtBM, n0 = (int64_t)blockIdx.x * kSimtBN;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  float ra[4], rb[4];
+  auto load_tiles = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int idx = tid + i * 256;
+      int mm, kk;
+      if (!TA_T) { mm = idx >> 3; kk = idx & 7; } else { kk = idx >> 7; mm = idx & 127; }
+      int64_t gm = m0 + mm, gk = k0 + kk;
+      ra[i] = (gm < M && gk < K) ? to_f32(TA_T ? A[gk * lda + gm] : A[gm * lda + gk]) : 0.f;
+      int nn;
+      if (!TB_T) { kk = idx >> 7; nn = idx & 127; } else { nn = idx >> 3; kk = idx & 7; }
+      int64_t gn = n0 + nn;
+      gk = k0 + kk;
+      rb[i] = (gn < N && gk < K) ? to_f32(TB_T ? B[gn * ldb + gk] : B[gk * ldb + gn]) : 0.f;
+    }
+  };
+  auto store_tiles = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int idx = tid + i * 256;
+      int mm, kk;
+      if (!TA_T) { mm = idx >> 3; kk = idx & 7; } else { kk = idx >> 7; mm = idx & 127; }
+      As[buf][kk][mm] = ra[i];
+      int nn;
+      if (!TB_T) { kk = idx >> 7; nn = idx & 127; } else { nn = idx >> 3; kk = idx & 7; }
+      Bs[buf][kk][nn] = rb[i];
+    }
+  };
+  const int64_t ktiles = (K + kSimtBK - 1) / kSimtBK;
+  if (ktiles > 0) {
+    load_tiles(0);
+    store_tiles(0);
+  }
+  __syncthreads();
+  for (int64_t kt = 0; kt < ktiles; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < ktiles) load_tiles((kt + 1) * kSimtBK);
+#pragma unroll
+    for (int k = 0; k < kSimtBK; ++k) {
+      float a[8], b[8];
+      float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
+      float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
+      float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
+      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+      a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+      b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (kt + 1 < ktiles) store_tiles(buf ^ 1);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int64_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (row >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int64_t col = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      if (col >= N) continue;
+      int64_t off = row * e.ldc + col;
+      C[off] = from_f32<TC>(epi_value<TC>(e, C, off, col, acc[i][j]));
+    }
+  }
+}
+
+// ============================ tcgen05 BF16 kernel ============================
+constexpr int kBM = 128, kBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct TcCfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  // full[S], empty[S], tfull[2], tempty[2], done -> 8 B each; then TMEM slot.
+  static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
+  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  static constexpr int kTmemCols = 2 * BN;
+};
+
+struct TcArgs {
+  int64_t M, N, K;
+  void* C;
+  EpiArgs e;
+  int* err;
+  int vec_ok;  // C/aux pointers 16-B aligned and ldc % 8 == 0: 8-wide vector stores
+};
+
+// Stores 8 consecutive columns (col .. col+7) of one row with the epilogue.
+template <typename TC>
+__device__ __forceinline__ void epi_store8(const TcArgs& a, int64_t row, int64_t col,
+                                           const float (&v)[8], bool vec_ok) {
+  TC* C = static_cast<TC*>(a.C);
+  const int64_t off = row * a.e.ldc + col;
+  if (vec_ok && col + 8 <= a.N) {
+    float o[8];
+    const int epi = a.e.epi;
+    if (epi == MAGMA_EPI_NONE) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[i];
+    } else if (epi == MAGMA_EPI_BIAS || epi == MAGMA_EPI_BIAS_GELU || epi == MAGMA_EPI_BIAS_RELU ||
+               epi == MAGMA_EPI_BIAS_RESIDUAL) {
+      float pre[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pre[i] = a.e.bias ? __fadd_rn(v[i], a.e.bias[col + i]) : v[i];
+      if (epi == MAGMA_EPI_BIAS) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = pre[i];
+      } else if (epi == MAGMA_EPI_BIAS_RESIDUAL) {
+        float r[8];
+        load8(static_cast<const float*>(a.e.aux_in) + off, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(r[i], pre[i]);
+      } else {
+        store8(static_cast<TC*>(a.e.aux_out) + off, pre);
+        if (epi == MAGMA_EPI_BIAS_GELU) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = gelu_f(pre[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = fmaxf(pre[i], 0.f);
+        }
+      }
+    } else if (epi == MAGMA_EPI_DGELU || epi == MAGMA_EPI_DRELU) {
+      float x[8];
+      load8(static_cast<const TC*>(a.e.aux_in) + off, x);
+      if (epi == MAGMA_EPI_DGELU) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[i], gelu_grad_f(x[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = x[i] > 0.f ? v[i] : 0.f;
+      }
+    } else {  // ACCUMULATE
+      float c[8];
+      load8(C + off, c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(c[i], v[i]);
+    }
+    store8(C + off, o);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (col + i < a.N)
+        C[off + i] = from_f32<TC>(epi_value<TC>(a.e, C, off + i, col + i, v[i]));
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, typename TC>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               TcArgs args) {
+  using Cfg = TcCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = sm100::smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw);
+  const uint32_t bars = base + Cfg::kBarOffset;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (S + s); };
+  auto tfull_bar = [&](int a) { return bars + 8u * (2 * S + a); };
+  auto tempty_bar = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
+  const uint32_t done_bar = bars + 8u * (2 * S + 4);
+  const uint32_t tmem_slot = bars + 8u * (2 * S + 5);
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(base_ptr + Cfg::kBarOffset + 8 * (2 * S + 5));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t M = args.M, N = args.N, K = args.K;
+  const int tiles_m = (int)((M + kBM - 1) / kBM);
+  const int tiles_n = (int)((N + BN - 1) / BN);
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (int)((K + kBK - 1) / kBK);
+
+  if (threadIdx.x == 0) {
+    sm100::prefetch_tensormap(&tmA);
+    sm100::prefetch_tensormap(&tmB);
+    for (int s = 0; s < S; ++s) {
+      sm100::mbar_init(full_bar(s), 1);
+      sm100::mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(tfull_bar(a), 1);
+      sm100::mbar_init(tempty_bar(a), 4);
+    }
+    sm100::mbar_init(done_bar, 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr);
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------- TMA producer ----------------------------
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * kBM;
+      const int n0 = (tile / tiles_m) * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!sm100::mbar_wait(empty_bar(stage), phase ^ 1u, args.err)) { ok = false; break; }
+        const uint32_t sa = base + stage * Cfg::kStageBytes;
+        const uint32_t sb = sa + Cfg::kABytes;
+        sm100::mbar_expect_tx(full_bar(stage), Cfg::kStageBytes);
+        if (!A_MN) {
+          sm100::tma_load_2d(sa, &tmA, kb * kBK, m0, full_bar(stage));
+        } else {
+#pragma unroll
+          for (int j = 0; j < kBM / 64; ++j)
+            sm100::tma_load_2d(sa + j * 8192, &tmA, m0 + j * 64, kb * kBK, full_bar(stage));
+        }
+        if (!B_MN) {
+          sm100::tma_load_2d(sb, &tmB, kb * kBK, n0, full_bar(stage));
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            sm100::tma_load_2d(sb + j * 8192, &tmB, n0 + j * 64, kb * kBK, full_bar(stage));
+        }
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // Re-acquire every slot: all loads issued above have been consumed (and
+    // the MMAs reading them completed) before this thread leaves.
+    for (int i = 0; i < S && ok; ++i) {
+      if (!sm100::mbar_wait(empty_bar(stage), phase ^ 1u, args.err)) ok = false;
+      if (++stage == S) { stage = 0; phase ^= 1u; }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ----------------------------- MMA issuer -----------------------------
+    constexpr uint32_t idesc = sm100::idesc_bf16_f32(kBM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      if (!sm100::mbar_wait(tempty_bar(acc), acc_phase ^ 1u, args.err)) { ok = false; break; }
+      sm100::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!sm100::mbar_wait(full_bar(stage), phase, args.err)) { ok = false; break; }
+        sm100::tc_fence_after();
+        const uint32_t sa = base + stage * Cfg::kStageBytes;
+        const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          // K-major: step 16 elements (32 B) inside the 128-B swizzle atom.
+          // MN-major: step 16 K-rows (16 x 128 B) = two 1024-B atom rows.
+          const uint64_t adesc =
+              A_MN ? sm100::smem_desc_sw128(sa + kk * 2048, 8192, 1024)
+                   : sm100::smem_desc_sw128(sa + kk * 32, 16, 1024);
+          const uint64_t bdesc =
+              B_MN ? sm100::smem_desc_sw128(sb + kk * 2048, 8192, 1024)
+                   : sm100::smem_desc_sw128(sb + kk * 32, 16, 1024);
+          sm100::mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+        sm100::mma_commit(empty_bar(stage));
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+      sm100::mma_commit(tfull_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    // Wait for every MMA this thread issued before TMEM is released.
+    sm100::mma_commit(done_bar);
+    sm100::mbar_wait(done_bar, 0, args.err);
+  } else if (warp >= 2) {
+    // ------------------------------ epilogue ------------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const bool vec_ok = args.vec_ok != 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * kBM;
+      const int n0 = (tile / tiles_m) * BN;
+      if (!sm100::mbar_wait(tfull_bar(acc), acc_phase, args.err)) break;
+      sm100::tc_fence_after();
+      const int64_t row = (int64_t)m0 + q * 32 + lane;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        sm100::tmem_ld32(taddr + c0, r);
+        sm100::tmem_wait_ld();
+        if (row < M && n0 + c0 < N) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[g * 8 + i]);
+            const int64_t col = (int64_t)n0 + c0 + g * 8;
+            if (col < N) epi_store8<TC>(args, row, col, v, vec_ok);
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, typename TC>
+magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                         int64_t lda, int64_t ldb, const TcArgs& args, cudaStream_t stream) {
+  using Cfg = TcCfg<BN>;
+  CUtensorMap ta, tb;
+  magma_status_t st;
+  if (!A_MN)
+    st = encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, K, M, lda * 2, 64, kBM,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    st = encode_tensor_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a, M, K, lda * 2, 64, 64,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  if (!B_MN)
+    st = encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, ldb * 2, 64, BN,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    st = encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, N, K, ldb * 2, 64, 64,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, TC>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (magma_status_t s2 = cuda_status(
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes),
+            "cudaFuncSetAttribute(gemm)"))
+      return s2;
+    attr_set[dev] = true;
+  }
+  const int64_t tiles = ceil_div(M, kBM) * ceil_div(N, BN);
+  int grid = num_sms();
+  if (tiles < grid) grid = (int)tiles;
+  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, args);
+  return check_launch("gemm_tcgen05");
+}
+
+template <int BN, typename TC>
+magma_status_t dispatch_major(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                              int64_t lda, int64_t ldb, int ta, int tb, const TcArgs& args,
+                              cudaStream_t s) {
+  const bool a_mn = ta != 0;   // A stored [K, M]
+  const bool b_mn = tb == 0;   // B stored [K, N]
+  if (!a_mn && !b_mn) return launch_tc<BN, false, false, TC>(a, b, M, N, K, lda, ldb, args, s);
+  if (!a_mn && b_mn) return launch_tc<BN, false, true, TC>(a, b, M, N, K, lda, ldb, args, s);
+  if (a_mn && !b_mn) return launch_tc<BN, true, false, TC>(a, b, M, N, K, lda, ldb, args, s);
+  return launch_tc<BN, true, true, TC>(a, b, M, N, K, lda, ldb, args, s);
+}
+
+// Picks BN by wave quantisation over the SMs: BN=256 halves the shared-memory
+// operand traffic per FLOP, BN=128 fills the SMs better when tiles are few.
+int choose_bn(int64_t M, int64_t N) {
+  const int sms = num_sms();
+  const int64_t t256 = ceil_div(M, kBM) * ceil_div(N, 256);
+  const int64_t t128 = ceil_div(M, kBM) * ceil_div(N, 128);
+  const double cost256 = (double)ceil_div(t256, sms) * 1.0;
+  const double cost128 = (double)ceil_div(t128, sms) * 0.5 * 1.15;
+  return cost128 < cost256 ? 128 : 256;
+}
+
+template <typename TA, typename TC>
+magma_status_t launch_simt(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K,
+                           int64_t lda, int64_t ldb, int ta, int tb, const EpiArgs& e,
+                           cudaStream_t s) {
+  dim3 grid((unsigned)ceil_div(N, kSimtBN), (unsigned)ceil_div(M, kSimtBM));
+  const TA* A = (const TA*)a;
+  const TA* B = (const TA*)b;
+  TC* C = (TC*)c;
+  if (!ta && !tb) gemm_simt_kernel<TA, TC, false, false><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
+  else if (!ta && tb) gemm_simt_kernel<TA, TC, false, true><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
+  else if (ta && !tb) gemm_simt_kernel<TA, TC, true, false><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
+  else gemm_simt_kernel<TA, TC, true, true><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
+  return check_launch("gemm_f32");
+}
+
+}  // namespace
+}  // namespace magma
+
+using namespace magma;
+
+extern "C" {
+
+size_t magma_gemm_workspace_size(int64_t m, int64_t n, int64_t k, magma_dtype_t ab_dtype) {
+  (void)m; (void)n; (void)k; (void)ab_dtype;
+  return 0;
+}
+
+magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
+                          int64_t lda, int64_t ldb, int64_t ldc, int32_t trans_a, int32_t trans_b,
+                          magma_dtype_t ab_dtype, magma_dtype_t c_dtype, int32_t epilogue,
+                          const float* bias, const void* aux_in, void* aux_out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  MAGMA_REQUIRE(m >= 0 && n >= 0 && k >= 0, "magma_gemm: negative size");
+  MAGMA_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31),
+                "magma_gemm: dimension exceeds 2^31");
+  MAGMA_REQUIRE(is_float_dtype(ab_dtype) && is_float_dtype(c_dtype),
+                "magma_gemm: unsupported dtypes ab=%s c=%s", dtype_name(ab_dtype),
+                dtype_name(c_dtype));
+  MAGMA_REQUIRE(epilogue >= MAGMA_EPI_NONE && epilogue <= MAGMA_EPI_DRELU,
+                "magma_gemm: unknown epilogue %d", epilogue);
+  MAGMA_REQUIRE(lda >= (trans_a ? m : k) && ldb >= (trans_b ? k : n) && ldc >= n,
+                "magma_gemm: leading dimensions too small (lda=%lld ldb=%lld ldc=%lld)",
+                (long long)lda, (long long)ldb, (long long)ldc);
+  if (m == 0 || n == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(c != nullptr && (k == 0 || (a != nullptr && b != nullptr)),
+                "magma_gemm: NULL operand");
+  MAGMA_REQUIRE(epilogue != MAGMA_EPI_ACCUMULATE || c_dtype == MAGMA_DTYPE_F32,
+                "magma_gemm: ACCUMULATE needs an F32 output");
+  MAGMA_REQUIRE(epilogue != MAGMA_EPI_BIAS_RESIDUAL || aux_in != nullptr,
+                "magma_gemm: BIAS_RESIDUAL needs aux_in (F32 residual)");
+  MAGMA_REQUIRE((epilogue != MAGMA_EPI_DGELU && epilogue != MAGMA_EPI_DRELU) || aux_in != nullptr,
+                "magma_gemm: activation VJP epilogue needs aux_in (pre-activation)");
+  MAGMA_REQUIRE((epilogue != MAGMA_EPI_BIAS_GELU && epilogue != MAGMA_EPI_BIAS_RELU) ||
+                    aux_out != nullptr,
+                "magma_gemm: activation epilogue needs aux_out for the pre-activation");
+  cudaStream_t s = (cudaStream_t)stream;
+  EpiArgs e{epilogue, bias, aux_in, aux_out, ldc};
+  const bool c32 = c_dtype == MAGMA_DTYPE_F32;
+
+  const bool tc_ok = ab_dtype == MAGMA_DTYPE_BF16 && k > 0 && aligned16(a) && aligned16(b) &&
+                     (lda % 8) == 0 && (ldb % 8) == 0;
+  if (tc_ok) {
+    const int vec_ok = (ldc % 8) == 0 && aligned16(c) && (aux_in == nullptr || aligned16(aux_in)) &&
+                       (aux_out == nullptr || aligned16(aux_out));
+    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok};
+    const int bn = choose_bn(m, n);
+    if (bn == 256)
+      return c32 ? dispatch_major<256, float>(a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
+                 : dispatch_major<256, __nv_bfloat16>(a, b, m, n, k, lda, ldb, trans_a, trans_b,
+                                                      args, s);
+    return c32 ? dispatch_major<128, float>(a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
+               : dispatch_major<128, __nv_bfloat16>(a, b, m, n, k, lda, ldb, trans_a, trans_b,
+                                                    args, s);
+  }
+  if (ab_dtype == MAGMA_DTYPE_F32)
+    return c32 ? launch_simt<float, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e, s)
+               : launch_simt<float, __nv_bfloat16>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b,
+                                                   e, s);
+  return c32 ? launch_simt<__nv_bfloat16, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e, s)
+             : launch_simt<__nv_bfloat16, __nv_bfloat16>(a, b, c, m, n, k, lda, ldb, trans_a,
+                                                         trans_b, e, s);
+}
+
+}  // extern "C"

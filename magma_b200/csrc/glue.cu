@@ -1,0 +1,444 @@
+// Glue ops on the training graphs: embedding gather and its scatter-add VJP,
+// fused softmax cross-entropy forward+backward, GELU/ReLU and their VJPs,
+// bias gradient, deterministic sum, dtype conversion, scaling. All are
+// HBM-bound element/row kernels with 128-bit accesses where alignment allows.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace magma {
+namespace {
+
+int grid_for(int64_t work, int threads, int per_sm = 8) {
+  int64_t b = ceil_div(work > 0 ? work : 1, threads);
+  int64_t cap = (int64_t)per_sm * num_sms();
+  return (int)(b > cap ? cap : b);
+}
+
+// ---- embedding ---------------------------------------------------------------
+// Data.swift:856-886 (gather along axis 0) + GPT main.swift:454-458 (tok + pos).
+__global__ void embedding_fwd_kernel(const int32_t* __restrict__ tokens,
+                                     const float* __restrict__ wte, const float* __restrict__ wpe,
+                                     float* __restrict__ out, int64_t rows, int64_t seq, int dim,
+                                     int64_t vocab, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  for (int64_t r = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * warps) {
+    int32_t t = tokens[r];
+    if (t < 0 || t >= vocab) {
+      if (lane == 0) set_device_error(err, kDevErrBadIndex);
+      t = 0;
+    }
+    const float* te = wte + (int64_t)t * dim;
+    const float* pe = wpe ? wpe + (r % seq) * dim : nullptr;
+    float* o = out + r * dim;
+    for (int i = lane; i < dim; i += 32) o[i] = pe ? __fadd_rn(te[i], pe[i]) : te[i];
+  }
+}
+
+// Scatter-add of token rows: dwte[tokens[r]] += dout[r] (fp32 atomics; the sum
+// over rows sharing a token is order-independent up to rounding).
+__global__ void embedding_bwd_tok_kernel(const int32_t* __restrict__ tokens,
+                                         const float* __restrict__ dout, float* __restrict__ dwte,
+                                         int64_t rows, int dim, int64_t vocab, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  for (int64_t r = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * warps) {
+    int32_t t = tokens[r];
+    if (t < 0 || t >= vocab) {
+      if (lane == 0) set_device_error(err, kDevErrBadIndex);
+      continue;
+    }
+    const float* src = dout + r * dim;
+    float* dst = dwte + (int64_t)t * dim;
+    for (int i = lane; i < dim; i += 32) atomicAdd(dst + i, src[i]);
+  }
+}
+
+// dwpe[s, i] += sum_b dout[b*seq + s, i], summed in b order (deterministic).
+__global__ void embedding_bwd_pos_kernel(const float* __restrict__ dout, float* __restrict__ dwpe,
+                                         int64_t batch, int64_t seq, int dim) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t total = seq * dim;
+  for (; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+    int64_t s = idx / dim;
+    int i = (int)(idx % dim);
+    float acc = 0.f;
+    for (int64_t b = 0; b < batch; ++b) acc += dout[(b * seq + s) * dim + i];
+    dwpe[idx] += acc;
+  }
+}
+
+// ---- softmax cross-entropy, forward + backward -------------------------------
+// Loss.swift:627-660 / GPT main.swift:412-433: shifted = x - max;
+// lse = log(sum(exp(shifted))); loss = -(shifted[t] - lse);
+// d loss/d x = grad_scale * (softmax(x) - onehot(t)).
+template <typename T>
+__global__ void __launch_bounds__(1024)
+ce_block_kernel(T* __restrict__ logits, const int32_t* __restrict__ targets,
+                float* __restrict__ losses, int64_t rows, int classes, int64_t ld,
+                float grad_scale, int* err) {
+  __shared__ float red[32];
+  __shared__ float bcast;
+  const int tid = threadIdx.x;
+  const int nw = blockDim.x >> 5;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    T* row = logits + r * ld;
+    // pass 1: max
+    float mx = -INFINITY;
+    for (int i = tid; i < classes; i += blockDim.x) mx = fmaxf(mx, to_f32(row[i]));
+    mx = warp_max(mx);
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid < 32) {
+      float v = tid < nw ? red[tid] : -INFINITY;
+      v = warp_max(v);
+      if (tid == 0) bcast = v;
+    }
+    __syncthreads();
+    mx = bcast;
+    __syncthreads();
+    // pass 2: sum of exp(shifted)
+    float s = 0.f;
+    for (int i = tid; i < classes; i += blockDim.x) s += expf(to_f32(row[i]) - mx);
+    s = warp_sum(s);
+    if ((tid & 31) == 0) red[tid >> 5] = s;
+    __syncthreads();
+    if (tid < 32) {
+      float v = tid < nw ? red[tid] : 0.f;
+      v = warp_sum(v);
+      if (tid == 0) bcast = v;
+    }
+    __syncthreads();
+    const float sum = bcast;
+    const float lse = logf(sum);
+    int32_t t = targets[r];
+    const bool bad = t < 0 || t >= classes;
+    if (tid == 0) {
+      if (bad) set_device_error(err, kDevErrBadIndex);
+      float xt = bad ? mx : to_f32(row[t]);
+      losses[r] = -((xt - mx) - lse);
+    }
+    __syncthreads();  // row[t] read before it is overwritten
+    const float inv = 1.0f / sum;
+    for (int i = tid; i < (int)ld; i += blockDim.x) {
+      float g = 0.f;
+      if (i < classes) {
+        float p = expf(to_f32(row[i]) - mx) * inv;
+        g = grad_scale * (p - (i == t ? 1.f : 0.f));
+      }
+      row[i] = from_f32<T>(g);
+    }
+    __syncthreads();
+  }
+}
+
+// Small class counts: one warp per row.
+template <typename T>
+__global__ void ce_warp_kernel(T* __restrict__ logits, const int32_t* __restrict__ targets,
+                               float* __restrict__ losses, int64_t rows, int classes, int64_t ld,
+                               float grad_scale, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  for (int64_t r = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * warps) {
+    T* row = logits + r * ld;
+    float mx = -INFINITY;
+    for (int i = lane; i < classes; i += 32) mx = fmaxf(mx, to_f32(row[i]));
+    mx = warp_max(mx);
+    float s = 0.f;
+    for (int i = lane; i < classes; i += 32) s += expf(to_f32(row[i]) - mx);
+    s = warp_sum(s);
+    const float lse = logf(s);
+    int32_t t = targets[r];
+    const bool bad = t < 0 || t >= classes;
+    float xt = bad ? mx : to_f32(row[bad ? 0 : t]);
+    if (lane == 0) {
+      if (bad) set_device_error(err, kDevErrBadIndex);
+      losses[r] = -((xt - mx) - lse);
+    }
+    __syncwarp();
+    const float inv = 1.0f / s;
+    for (int i = lane; i < (int)ld; i += 32) {
+      float g = 0.f;
+      if (i < classes) {
+        float p = expf(to_f32(row[i]) - mx) * inv;
+        g = grad_scale * (p - (i == t ? 1.f : 0.f));
+      }
+      row[i] = from_f32<T>(g);
+    }
+  }
+}
+
+// Deterministic single-CTA sum: fixed per-thread strides, fixed tree.
+__global__ void __launch_bounds__(1024)
+reduce_sum_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n, float scale) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) out[0] = v * scale;
+  }
+}
+
+// ---- element-wise activations ------------------------------------------------
+enum class Act { GeluFwd, GeluBwd, ReluFwd, ReluBwd };
+
+template <typename T, Act A>
+__global__ void act_kernel(const T* __restrict__ x, const T* __restrict__ dy, T* __restrict__ y,
+                           int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float xv = to_f32(x[i]);
+    float r;
+    if constexpr (A == Act::GeluFwd) r = gelu_f(xv);
+    else if constexpr (A == Act::GeluBwd) r = __fmul_rn(to_f32(dy[i]), gelu_grad_f(xv));
+    else if constexpr (A == Act::ReluFwd) r = fmaxf(xv, 0.f);
+    else r = xv > 0.f ? to_f32(dy[i]) : 0.f;
+    y[i] = from_f32<T>(r);
+  }
+}
+
+template <Act A>
+magma_status_t launch_act(const void* x, const void* dy, void* y, int64_t n, magma_dtype_t dt,
+                          cudaStream_t s, const char* name) {
+  if (n == 0) return MAGMA_OK;
+  int g = grid_for(n, 256);
+  if (dt == MAGMA_DTYPE_F32)
+    act_kernel<float, A><<<g, 256, 0, s>>>((const float*)x, (const float*)dy, (float*)y, n);
+  else
+    act_kernel<__nv_bfloat16, A><<<g, 256, 0, s>>>((const __nv_bfloat16*)x,
+                                                   (const __nv_bfloat16*)dy, (__nv_bfloat16*)y, n);
+  return check_launch(name);
+}
+
+// ---- bias gradient -------------------------------------------------------------
+// Phase 1: CTA b sums rows [b*rpc, (b+1)*rpc) for 256 columns per CTA-column
+// (threads own columns: coalesced); phase 2 sums the partials in CTA order.
+constexpr int kBiasMaxRowBlocks = 256;
+
+template <typename T>
+__global__ void bias_grad_partial(const T* __restrict__ dy, float* __restrict__ part,
+                                  int64_t rows, int cols, int64_t ld, int64_t rows_per_block) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+  int64_t r1 = min(rows, r0 + rows_per_block);
+  float s = 0.f;
+  for (int64_t r = r0; r < r1; ++r) s += to_f32(dy[r * ld + c]);
+  part[(int64_t)blockIdx.y * cols + c] = s;
+}
+
+__global__ void bias_grad_final(const float* __restrict__ part, float* __restrict__ dbias,
+                                int nblocks, int cols, int accumulate) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += part[(int64_t)b * cols + c];
+  dbias[c] = accumulate ? dbias[c] + s : s;
+}
+
+int bias_row_blocks(int64_t rows) {
+  int64_t b = ceil_div(rows, 64);
+  return (int)(b > kBiasMaxRowBlocks ? kBiasMaxRowBlocks : (b < 1 ? 1 : b));
+}
+
+template <typename TS, typename TD>
+__global__ void convert_kernel(const TS* __restrict__ src, TD* __restrict__ dst, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    dst[i] = from_f32<TD>(to_f32(src[i]));
+}
+
+__global__ void scale_kernel(float* __restrict__ y, int64_t n, float alpha) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = __fmul_rn(y[i], alpha);
+}
+
+}  // namespace
+}  // namespace magma
+
+using namespace magma;
+
+extern "C" {
+
+magma_status_t magma_embedding_fwd(const int32_t* tokens, const float* wte, const float* wpe,
+                                   float* out, int64_t batch, int64_t seq, int64_t dim,
+                                   int64_t vocab, void* stream) {
+  MAGMA_REQUIRE(batch >= 0 && seq > 0 && dim > 0 && vocab > 0,
+                "magma_embedding_fwd: bad shape");
+  int64_t rows = batch * seq;
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(tokens && wte && out, "magma_embedding_fwd: NULL pointer");
+  int* err = device_error_word();
+  embedding_fwd_kernel<<<grid_for(rows, 8), 256, 0, (cudaStream_t)stream>>>(
+      tokens, wte, wpe, out, rows, seq, (int)dim, vocab, err);
+  return check_launch("embedding_fwd");
+}
+
+magma_status_t magma_embedding_bwd(const int32_t* tokens, const float* dout, float* dwte,
+                                   float* dwpe, int64_t batch, int64_t seq, int64_t dim,
+                                   int64_t vocab, void* stream) {
+  MAGMA_REQUIRE(batch >= 0 && seq > 0 && dim > 0 && vocab > 0,
+                "magma_embedding_bwd: bad shape");
+  int64_t rows = batch * seq;
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(tokens && dout && dwte, "magma_embedding_bwd: NULL pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  int* err = device_error_word();
+  embedding_bwd_tok_kernel<<<grid_for(rows, 8), 256, 0, s>>>(tokens, dout, dwte, rows, (int)dim,
+                                                             vocab, err);
+  if (magma_status_t st = check_launch("embedding_bwd_tok")) return st;
+  if (dwpe != nullptr) {
+    embedding_bwd_pos_kernel<<<grid_for(seq * dim, 256), 256, 0, s>>>(dout, dwpe, batch, seq,
+                                                                       (int)dim);
+    if (magma_status_t st = check_launch("embedding_bwd_pos")) return st;
+  }
+  return MAGMA_OK;
+}
+
+magma_status_t magma_cross_entropy_fwd_bwd(void* logits, const int32_t* targets, float* losses,
+                                           int64_t rows, int64_t classes, int64_t ld,
+                                           float grad_scale, magma_dtype_t dtype, void* stream) {
+  MAGMA_REQUIRE(rows >= 0 && classes > 0 && ld >= classes && classes < (1LL << 31),
+                "magma_cross_entropy_fwd_bwd: bad shape rows=%lld classes=%lld ld=%lld",
+                (long long)rows, (long long)classes, (long long)ld);
+  MAGMA_REQUIRE(is_float_dtype(dtype), "magma_cross_entropy_fwd_bwd: dtype must be F32 or BF16");
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(logits && targets && losses, "magma_cross_entropy_fwd_bwd: NULL pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  int* err = device_error_word();
+  if (classes <= 2048) {
+    int g = grid_for(rows, 8);
+    if (dtype == MAGMA_DTYPE_F32)
+      ce_warp_kernel<float><<<g, 256, 0, s>>>((float*)logits, targets, losses, rows, (int)classes,
+                                              ld, grad_scale, err);
+    else
+      ce_warp_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((__nv_bfloat16*)logits, targets, losses,
+                                                      rows, (int)classes, ld, grad_scale, err);
+  } else {
+    int64_t g = rows;
+    int64_t cap = 16LL * num_sms();
+    if (g > cap) g = cap;
+    if (dtype == MAGMA_DTYPE_F32)
+      ce_block_kernel<float><<<(int)g, 1024, 0, s>>>((float*)logits, targets, losses, rows,
+                                                     (int)classes, ld, grad_scale, err);
+    else
+      ce_block_kernel<__nv_bfloat16><<<(int)g, 1024, 0, s>>>(
+          (__nv_bfloat16*)logits, targets, losses, rows, (int)classes, ld, grad_scale, err);
+  }
+  return check_launch("cross_entropy_fwd_bwd");
+}
+
+magma_status_t magma_reduce_sum(const float* x, float* out, int64_t n, float scale, void* stream) {
+  MAGMA_REQUIRE(n >= 0, "magma_reduce_sum: negative size");
+  MAGMA_REQUIRE(out != nullptr && (n == 0 || x != nullptr), "magma_reduce_sum: NULL pointer");
+  reduce_sum_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, out, n, scale);
+  return check_launch("reduce_sum");
+}
+
+magma_status_t magma_gelu_fwd(const void* x, void* y, int64_t n, magma_dtype_t dtype,
+                              void* stream) {
+  MAGMA_REQUIRE(n >= 0 && is_float_dtype(dtype), "magma_gelu_fwd: bad arguments");
+  MAGMA_REQUIRE(n == 0 || (x && y), "magma_gelu_fwd: NULL pointer");
+  return launch_act<Act::GeluFwd>(x, nullptr, y, n, dtype, (cudaStream_t)stream, "gelu_fwd");
+}
+
+magma_status_t magma_gelu_bwd(const void* x, const void* dy, void* dx, int64_t n,
+                              magma_dtype_t dtype, void* stream) {
+  MAGMA_REQUIRE(n >= 0 && is_float_dtype(dtype), "magma_gelu_bwd: bad arguments");
+  MAGMA_REQUIRE(n == 0 || (x && dy && dx), "magma_gelu_bwd: NULL pointer");
+  return launch_act<Act::GeluBwd>(x, dy, dx, n, dtype, (cudaStream_t)stream, "gelu_bwd");
+}
+
+magma_status_t magma_relu_fwd(const void* x, void* y, int64_t n, magma_dtype_t dtype,
+                              void* stream) {
+  MAGMA_REQUIRE(n >= 0 && is_float_dtype(dtype), "magma_relu_fwd: bad arguments");
+  MAGMA_REQUIRE(n == 0 || (x && y), "magma_relu_fwd: NULL pointer");
+  return launch_act<Act::ReluFwd>(x, nullptr, y, n, dtype, (cudaStream_t)stream, "relu_fwd");
+}
+
+magma_status_t magma_relu_bwd(const void* x, const void* dy, void* dx, int64_t n,
+                              magma_dtype_t dtype, void* stream) {
+  MAGMA_REQUIRE(n >= 0 && is_float_dtype(dtype), "magma_relu_bwd: bad arguments");
+  MAGMA_REQUIRE(n == 0 || (x && dy && dx), "magma_relu_bwd: NULL pointer");
+  return launch_act<Act::ReluBwd>(x, dy, dx, n, dtype, (cudaStream_t)stream, "relu_bwd");
+}
+
+size_t magma_bias_grad_workspace_size(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return (size_t)bias_row_blocks(rows) * (size_t)cols * sizeof(float);
+}
+
+magma_status_t magma_bias_grad(const void* dy, float* dbias, int64_t rows, int64_t cols,
+                               int64_t ld, magma_dtype_t dtype, int32_t accumulate,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  MAGMA_REQUIRE(rows >= 0 && cols > 0 && ld >= cols && cols < (1LL << 31),
+                "magma_bias_grad: bad shape");
+  MAGMA_REQUIRE(is_float_dtype(dtype), "magma_bias_grad: dtype must be F32 or BF16");
+  MAGMA_REQUIRE(dbias != nullptr, "magma_bias_grad: NULL dbias");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (rows == 0) {
+    if (!accumulate) return magma_memset(dbias, 0, (size_t)cols * sizeof(float), stream);
+    return MAGMA_OK;
+  }
+  MAGMA_REQUIRE(dy != nullptr, "magma_bias_grad: NULL dy");
+  size_t need = magma_bias_grad_workspace_size(rows, cols);
+  MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+                "magma_bias_grad: workspace of %zu bytes needed, %zu given", need,
+                workspace_bytes);
+  int nb = bias_row_blocks(rows);
+  int64_t rpb = ceil_div(rows, nb);
+  dim3 grid((unsigned)ceil_div(cols, 256), (unsigned)nb);
+  float* part = (float*)workspace;
+  if (dtype == MAGMA_DTYPE_F32)
+    bias_grad_partial<float><<<grid, 256, 0, s>>>((const float*)dy, part, rows, (int)cols, ld, rpb);
+  else
+    bias_grad_partial<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part, rows,
+                                                          (int)cols, ld, rpb);
+  if (magma_status_t st = check_launch("bias_grad_partial")) return st;
+  bias_grad_final<<<(unsigned)ceil_div(cols, 256), 256, 0, s>>>(part, dbias, nb, (int)cols,
+                                                                accumulate);
+  return check_launch("bias_grad_final");
+}
+
+magma_status_t magma_convert(const void* src, void* dst, int64_t n, magma_dtype_t src_dtype,
+                             magma_dtype_t dst_dtype, void* stream) {
+  MAGMA_REQUIRE(n >= 0 && is_float_dtype(src_dtype) && is_float_dtype(dst_dtype),
+                "magma_convert: unsupported conversion %s -> %s", dtype_name(src_dtype),
+                dtype_name(dst_dtype));
+  if (n == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(src && dst, "magma_convert: NULL pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  int g = grid_for(n, 256);
+  if (src_dtype == MAGMA_DTYPE_F32 && dst_dtype == MAGMA_DTYPE_BF16)
+    convert_kernel<float, __nv_bfloat16><<<g, 256, 0, s>>>((const float*)src,
+                                                           (__nv_bfloat16*)dst, n);
+  else if (src_dtype == MAGMA_DTYPE_BF16 && dst_dtype == MAGMA_DTYPE_F32)
+    convert_kernel<__nv_bfloat16, float><<<g, 256, 0, s>>>((const __nv_bfloat16*)src,
+                                                           (float*)dst, n);
+  else if (src_dtype == MAGMA_DTYPE_F32)
+    convert_kernel<float, float><<<g, 256, 0, s>>>((const float*)src, (float*)dst, n);
+  else
+    convert_kernel<__nv_bfloat16, __nv_bfloat16><<<g, 256, 0, s>>>(
+        (const __nv_bfloat16*)src, (__nv_bfloat16*)dst, n);
+  return check_launch("convert");
+}
+
+magma_status_t magma_scale(float* y, int64_t n, float alpha, void* stream) {
+  MAGMA_REQUIRE(n >= 0, "magma_scale: negative size");
+  if (n == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(y != nullptr, "magma_scale: NULL pointer");
+  scale_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(y, n, alpha);
+  return check_launch("scale");
+}
+
+}  // extern "C"

@@ -1,0 +1,405 @@
+// LayerNorm forward and backward.
+//
+// Forward restates nn.LayerNorm.forward (Sources/Core/Module.swift:2754-2791)
+// and the GPT block's layerNorm (Benchmarks/GPT2Shakespeare/Sources/main.swift:
+// 364-375): mean = sum/D, var = sum((x-mean)^2)/D (population), std =
+// sqrt(var+eps), y = ((x-mean)/std)*gamma + beta, with an IEEE divide by std
+// as the reference does (it never multiplies by rsqrt).
+//
+// Backward is the closed form of the reference's autodiff chain through that
+// forward (vjpDivide/vjpSqrt/vjpMeanDims/vjpMultiply with sumAlongBroadcastDims,
+// Sources/Core/Autodiff.swift:57-94,221-257,351-370; Optimizer.swift:627-633).
+//
+// Both kernels are HBM-bound row kernels: one warp per row, 8 elements per
+// lane per step via 128-bit loads (BF16) or 2x128-bit loads (F32), the row held
+// in registers between the reduction and the store, warp-shuffle reductions in
+// a fixed butterfly order (deterministic). dgamma/dbeta are reduced per CTA in
+// shared memory in warp order, written as per-CTA partial rows to the caller's
+// workspace, then summed over CTAs in CTA order by a second kernel.
+#include "common.cuh"
+
+namespace magma {
+namespace {
+
+constexpr int kWarps = 8;            // warps per CTA (one row per warp at a time)
+constexpr int kMaxChunks = 4;        // cached 8-element chunks per lane: D <= 1024
+constexpr int kMaxBwdBlocks = 592;   // cap on per-CTA partial rows (4 x 148 SMs)
+
+template <typename TX, typename TY>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_fwd_cached(const TX* __restrict__ x, const float* __restrict__ gamma,
+              const float* __restrict__ beta, TY* __restrict__ y, float* __restrict__ mean_out,
+              float* __restrict__ rstd_out, int64_t rows, int dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int chunks = dim >> 3;
+  const float inv_d = 1.0f / (float)dim;
+  (void)inv_d;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kWarps) {
+    const TX* xr = x + row * dim;
+    float v[kMaxChunks][8];
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      int chunk = lane + c * 32;
+      if (chunk < chunks) {
+        load8(xr + chunk * 8, v[c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s += v[c][i];
+      }
+    }
+    s = warp_sum(s);
+    const float mean = __fdiv_rn(s, (float)dim);
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      int chunk = lane + c * 32;
+      if (chunk < chunks) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float d = __fsub_rn(v[c][i], mean);
+          v[c][i] = d;
+          ss += d * d;
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    const float var = __fdiv_rn(ss, (float)dim);
+    const float stdv = __fsqrt_rn(__fadd_rn(var, eps));
+    TY* yr = y + row * dim;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      int chunk = lane + c * 32;
+      if (chunk < chunks) {
+        float g[8], b[8], o[8];
+        load8(gamma + chunk * 8, g);
+        load8(beta + chunk * 8, b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          o[i] = __fadd_rn(__fmul_rn(__fdiv_rn(v[c][i], stdv), g[i]), b[i]);
+        store8(yr + chunk * 8, o);
+      }
+    }
+    if (lane == 0) {
+      if (mean_out) mean_out[row] = mean;
+      if (rstd_out) rstd_out[row] = __fdiv_rn(1.0f, stdv);
+    }
+  }
+}
+
+// Any D (scalar loads, row re-read from L1/L2 for each pass).
+template <typename TX, typename TY>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_fwd_generic(const TX* __restrict__ x, const float* __restrict__ gamma,
+               const float* __restrict__ beta, TY* __restrict__ y, float* __restrict__ mean_out,
+               float* __restrict__ rstd_out, int64_t rows, int dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kWarps) {
+    const TX* xr = x + row * dim;
+    float s = 0.f;
+    for (int i = lane; i < dim; i += 32) s += to_f32(xr[i]);
+    s = warp_sum(s);
+    const float mean = __fdiv_rn(s, (float)dim);
+    float ss = 0.f;
+    for (int i = lane; i < dim; i += 32) {
+      float d = __fsub_rn(to_f32(xr[i]), mean);
+      ss += d * d;
+    }
+    ss = warp_sum(ss);
+    const float stdv = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+    TY* yr = y + row * dim;
+    for (int i = lane; i < dim; i += 32) {
+      float d = __fsub_rn(to_f32(xr[i]), mean);
+      yr[i] = from_f32<TY>(__fadd_rn(__fmul_rn(__fdiv_rn(d, stdv), gamma[i]), beta[i]));
+    }
+    if (lane == 0) {
+      if (mean_out) mean_out[row] = mean;
+      if (rstd_out) rstd_out[row] = __fdiv_rn(1.0f, stdv);
+    }
+  }
+}
+
+// Backward, D % 8 == 0 and D <= 1024. Per-CTA dgamma/dbeta partials go to
+// part[blockIdx.x][0..D) (dgamma) and part[blockIdx.x][D..2D) (dbeta).
+template <typename TDY, typename TX, typename TDX>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_bwd_cached(const TDY* __restrict__ dy, const TX* __restrict__ x,
+              const float* __restrict__ gamma, const float* __restrict__ mean_in,
+              const float* __restrict__ rstd_in, TDX* __restrict__ dx,
+              float* __restrict__ part, int64_t rows, int dim, int accumulate_dx) {
+  extern __shared__ float smem[];  // [2*dim]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int chunks = dim >> 3;
+  float pg[kMaxChunks][8], pb[kMaxChunks][8];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pg[c][i] = pb[c][i] = 0.f;
+
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kWarps) {
+    const float mean = mean_in[row];
+    const float rstd = rstd_in[row];
+    float xh[kMaxChunks][8], g[kMaxChunks][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      int chunk = lane + c * 32;
+      if (chunk < chunks) {
+        float xv[8], dv[8], gm[8];
+        load8(x + row * dim + chunk * 8, xv);
+        load8(dy + row * dim + chunk * 8, dv);
+        load8(gamma + chunk * 8, gm);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float xhat = (xv[i] - mean) * rstd;
+          float gg = dv[i] * gm[i];
+          xh[c][i] = xhat;
+          g[c][i] = gg;
+          s1 += gg;
+          s2 += gg * xhat;
+          pg[c][i] += dv[i] * xhat;
+          pb[c][i] += dv[i];
+        }
+      }
+    }
+    s1 = warp_sum(s1) / (float)dim;
+    s2 = warp_sum(s2) / (float)dim;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      int chunk = lane + c * 32;
+      if (chunk < chunks) {
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = rstd * (g[c][i] - s1 - xh[c][i] * s2);
+        TDX* dst = dx + row * dim + chunk * 8;
+        if (accumulate_dx) {
+          float prev[8];
+          load8(dst, prev);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] += prev[i];
+        }
+        store8(dst, o);
+      }
+    }
+  }
+  // Deterministic CTA reduction of the per-lane partials: warps add into
+  // shared memory one after another, in warp order.
+  for (int w = 0; w < kWarps; ++w) {
+    if (warp == w) {
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+        int chunk = lane + c * 32;
+        if (chunk < chunks) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            int col = chunk * 8 + i;
+            if (w == 0) {
+              smem[col] = pg[c][i];
+              smem[dim + col] = pb[c][i];
+            } else {
+              smem[col] += pg[c][i];
+              smem[dim + col] += pb[c][i];
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  float* out = part + (int64_t)blockIdx.x * 2 * dim;
+  for (int i = threadIdx.x; i < 2 * dim; i += blockDim.x) out[i] = smem[i];
+}
+
+template <typename TDY, typename TX, typename TDX>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_bwd_generic(const TDY* __restrict__ dy, const TX* __restrict__ x,
+               const float* __restrict__ gamma, const float* __restrict__ mean_in,
+               const float* __restrict__ rstd_in, TDX* __restrict__ dx,
+               float* __restrict__ part, int64_t rows, int dim, int accumulate_dx) {
+  // Per-CTA partials accumulated column-wise: each CTA owns a contiguous row
+  // range; threads own columns (coalesced), rows visited in order.
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t rows_per_cta = (rows + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int64_t r1 = min(rows, r0 + rows_per_cta);
+  // dx: one warp per row within the range.
+  for (int64_t row = r0 + warp; row < r1; row += kWarps) {
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float s1 = 0.f, s2 = 0.f;
+    for (int i = lane; i < dim; i += 32) {
+      float xhat = (to_f32(x[row * dim + i]) - mean) * rstd;
+      float gg = to_f32(dy[row * dim + i]) * gamma[i];
+      s1 += gg;
+      s2 += gg * xhat;
+    }
+    s1 = warp_sum(s1) / (float)dim;
+    s2 = warp_sum(s2) / (float)dim;
+    for (int i = lane; i < dim; i += 32) {
+      float xhat = (to_f32(x[row * dim + i]) - mean) * rstd;
+      float gg = to_f32(dy[row * dim + i]) * gamma[i];
+      float o = rstd * (gg - s1 - xhat * s2);
+      if (accumulate_dx) o += to_f32(dx[row * dim + i]);
+      dx[row * dim + i] = from_f32<TDX>(o);
+    }
+  }
+  float* out = part + (int64_t)blockIdx.x * 2 * dim;
+  for (int col = threadIdx.x; col < dim; col += blockDim.x) {
+    float sg = 0.f, sb = 0.f;
+    for (int64_t row = r0; row < r1; ++row) {
+      float d = to_f32(dy[row * dim + col]);
+      sg += d * ((to_f32(x[row * dim + col]) - mean_in[row]) * rstd_in[row]);
+      sb += d;
+    }
+    out[col] = sg;
+    out[dim + col] = sb;
+  }
+}
+
+// Sums per-CTA partial rows in CTA order: out[c] (+)= sum_b part[b][c].
+__global__ void reduce_partials(const float* __restrict__ part, int nblocks, int width,
+                                float* __restrict__ dgamma, float* __restrict__ dbeta, int dim,
+                                int accumulate) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= width) return;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += part[(int64_t)b * width + c];
+  float* dst = c < dim ? dgamma + c : dbeta + (c - dim);
+  if (dst == nullptr) return;
+  *dst = accumulate ? *dst + s : s;
+}
+
+int bwd_blocks(int64_t rows) {
+  int64_t b = ceil_div(rows, kWarps);
+  int64_t cap = 2LL * num_sms();
+  if (cap > kMaxBwdBlocks) cap = kMaxBwdBlocks;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+template <typename TX, typename TY>
+magma_status_t launch_fwd(const void* x, const float* gamma, const float* beta, void* y,
+                          float* mean, float* rstd, int64_t rows, int dim, float eps,
+                          cudaStream_t stream) {
+  int64_t blocks = ceil_div(rows, kWarps);
+  int64_t cap = 16LL * num_sms();
+  if (blocks > cap) blocks = cap;
+  bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(y) &&
+             aligned16(gamma) && aligned16(beta);
+  if (vec)
+    ln_fwd_cached<TX, TY><<<(int)blocks, kWarps * 32, 0, stream>>>(
+        (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
+  else
+    ln_fwd_generic<TX, TY><<<(int)blocks, kWarps * 32, 0, stream>>>(
+        (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
+  return check_launch("layernorm_fwd");
+}
+
+template <typename TDY, typename TX, typename TDX>
+magma_status_t launch_bwd(const void* dy, const void* x, const float* gamma, const float* mean,
+                          const float* rstd, void* dx, float* dgamma, float* dbeta,
+                          int64_t rows, int dim, int acc_dx, int acc_params, float* part,
+                          cudaStream_t stream) {
+  int blocks = bwd_blocks(rows);
+  bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(dy) &&
+             aligned16(dx) && aligned16(gamma);
+  if (vec) {
+    size_t smem = 2 * (size_t)dim * sizeof(float);
+    ln_bwd_cached<TDY, TX, TDX><<<blocks, kWarps * 32, smem, stream>>>(
+        (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
+  } else {
+    ln_bwd_generic<TDY, TX, TDX><<<blocks, kWarps * 32, 0, stream>>>(
+        (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
+  }
+  if (magma_status_t s = check_launch("layernorm_bwd")) return s;
+  if (dgamma != nullptr || dbeta != nullptr) {
+    int width = 2 * dim;
+    reduce_partials<<<(width + 255) / 256, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
+                                                             dim, acc_params);
+    if (magma_status_t s = check_launch("layernorm_bwd_reduce")) return s;
+  }
+  return MAGMA_OK;
+}
+
+}  // namespace
+}  // namespace magma
+
+using namespace magma;
+
+extern "C" {
+
+magma_status_t magma_layernorm_fwd(const void* x, const float* gamma, const float* beta, void* y,
+                                   float* mean, float* rstd, int64_t rows, int64_t dim, float eps,
+                                   magma_dtype_t x_dtype, magma_dtype_t y_dtype, void* stream) {
+  MAGMA_REQUIRE(rows >= 0 && dim > 0 && dim <= (1 << 20),
+                "magma_layernorm_fwd: bad shape rows=%lld dim=%lld", (long long)rows,
+                (long long)dim);
+  MAGMA_REQUIRE(is_float_dtype(x_dtype) && is_float_dtype(y_dtype),
+                "magma_layernorm_fwd: unsupported dtypes x=%s y=%s", dtype_name(x_dtype),
+                dtype_name(y_dtype));
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(x && gamma && beta && y, "magma_layernorm_fwd: NULL pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int d = (int)dim;
+  if (x_dtype == MAGMA_DTYPE_F32 && y_dtype == MAGMA_DTYPE_F32)
+    return launch_fwd<float, float>(x, gamma, beta, y, mean, rstd, rows, d, eps, s);
+  if (x_dtype == MAGMA_DTYPE_F32 && y_dtype == MAGMA_DTYPE_BF16)
+    return launch_fwd<float, __nv_bfloat16>(x, gamma, beta, y, mean, rstd, rows, d, eps, s);
+  if (x_dtype == MAGMA_DTYPE_BF16 && y_dtype == MAGMA_DTYPE_F32)
+    return launch_fwd<__nv_bfloat16, float>(x, gamma, beta, y, mean, rstd, rows, d, eps, s);
+  return launch_fwd<__nv_bfloat16, __nv_bfloat16>(x, gamma, beta, y, mean, rstd, rows, d, eps, s);
+}
+
+size_t magma_layernorm_bwd_workspace_size(int64_t rows, int64_t dim) {
+  if (rows <= 0 || dim <= 0) return 0;
+  int64_t b = ceil_div(rows, kWarps);
+  if (b > kMaxBwdBlocks) b = kMaxBwdBlocks;
+  return (size_t)b * 2 * (size_t)dim * sizeof(float);
+}
+
+magma_status_t magma_layernorm_bwd(const void* dy, const void* x, const float* gamma,
+                                   const float* mean, const float* rstd, void* dx, float* dgamma,
+                                   float* dbeta, int64_t rows, int64_t dim,
+                                   magma_dtype_t dy_dtype, magma_dtype_t x_dtype,
+                                   magma_dtype_t dx_dtype, int32_t accumulate_dx,
+                                   int32_t accumulate_params, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  MAGMA_REQUIRE(rows >= 0 && dim > 0 && dim <= 8192,
+                "magma_layernorm_bwd: bad shape rows=%lld dim=%lld (dim <= 8192)",
+                (long long)rows, (long long)dim);
+  MAGMA_REQUIRE(is_float_dtype(dy_dtype) && is_float_dtype(x_dtype) && is_float_dtype(dx_dtype),
+                "magma_layernorm_bwd: unsupported dtypes");
+  MAGMA_REQUIRE(!accumulate_dx || dx_dtype == MAGMA_DTYPE_F32,
+                "magma_layernorm_bwd: accumulate_dx needs an F32 dx");
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(dy && x && gamma && mean && rstd && dx, "magma_layernorm_bwd: NULL pointer");
+  size_t need = magma_layernorm_bwd_workspace_size(rows, dim);
+  MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+                "magma_layernorm_bwd: workspace of %zu bytes needed, %zu given", need,
+                workspace_bytes);
+  cudaStream_t s = (cudaStream_t)stream;
+  float* part = (float*)workspace;
+  const int d = (int)dim;
+  const bool f_dy = dy_dtype == MAGMA_DTYPE_F32, f_x = x_dtype == MAGMA_DTYPE_F32,
+             f_dx = dx_dtype == MAGMA_DTYPE_F32;
+#define LN_BWD(TDY, TX, TDX)                                                                    \
+  return launch_bwd<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, dgamma, dbeta, rows, d,      \
+                                  accumulate_dx, accumulate_params, part, s)
+  if (f_dy && f_x && f_dx) LN_BWD(float, float, float);
+  if (!f_dy && f_x && f_dx) LN_BWD(__nv_bfloat16, float, float);
+  if (!f_dy && !f_x && !f_dx) LN_BWD(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
+  if (!f_dy && !f_x && f_dx) LN_BWD(__nv_bfloat16, __nv_bfloat16, float);
+  if (f_dy && !f_x && f_dx) LN_BWD(float, __nv_bfloat16, float);
+  if (f_dy && f_x && !f_dx) LN_BWD(float, float, __nv_bfloat16);
+  if (!f_dy && f_x && !f_dx) LN_BWD(__nv_bfloat16, float, __nv_bfloat16);
+  LN_BWD(float, __nv_bfloat16, __nv_bfloat16);
+#undef LN_BWD
+}
+
+}  // extern "C"

@@ -1,0 +1,367 @@
+"""GPU parity of every kernel against the oracle (the CPU restatement).
+
+Tolerances (from the target specification): F32 LayerNorm/Adam rel 1e-5,
+F32 attention/GEMM rel 1e-4, BF16 rel 2e-2, where "rel" is elementwise
+|got - want| <= rtol * (|want| + rms(want)); rms(want) keeps entries near zero
+from demanding more than the tensor's own scale allows. Integer/index outputs
+are compared exactly.
+"""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def close(got, want, rtol):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert got.shape == want.shape, (got.shape, want.shape)
+    rms = math.sqrt(float(np.mean(want * want))) if want.size else 0.0
+    err = np.abs(got - want)
+    bound = rtol * (np.abs(want) + rms) + 1e-30
+    worst = float(np.max(err / bound)) if want.size else 0.0
+    assert worst <= 1.0, f"max err/bound = {worst:.3g} (max abs err {float(err.max()):.3g}, rms {rms:.3g})"
+
+
+def t(a, dtype=torch.float32, dev="cuda"):
+    return torch.tensor(np.asarray(a), dtype=dtype, device=dev)
+
+
+def bf16_round(a):
+    return torch.tensor(a, dtype=torch.float32).to(torch.bfloat16).float().numpy()
+
+
+# --------------------------------------------------------------------- LayerNorm
+@pytest.mark.parametrize("rows,dim", [(8192, 768), (1000, 384), (37, 100), (1, 1024), (5, 2048)])
+def test_layernorm_f32(cuda, oracle, rows, dim):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(rows + dim)
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    g = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+    dy = rng.standard_normal((rows, dim)).astype(np.float32)
+    y, mean, rstd = ops.layer_norm_fwd(t(x), t(g), t(b))
+    ry, rmean, rrstd = oracle.layernorm_fwd(x, g, b)
+    close(y.cpu(), ry, 1e-5)
+    close(mean.cpu(), rmean, 1e-5)
+    close(rstd.cpu(), rrstd, 1e-5)
+    dx, dg, db = ops.layer_norm_bwd(t(dy), t(x), t(g), mean, rstd)
+    rdx, rdg, rdb = oracle.layernorm_bwd(dy, x, g)
+    close(dx.cpu(), rdx, 1e-5)
+    close(dg.cpu(), rdg, 1e-5)
+    close(db.cpu(), rdb, 1e-5)
+
+
+def test_layernorm_bf16_io_and_accumulate(cuda, oracle):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(7)
+    rows, dim = 2048, 768
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    g = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+    dy = bf16_round(rng.standard_normal((rows, dim)).astype(np.float32))
+    # F32 residual in, BF16 normalised activations out (the GPT-2 mixed layout)
+    y, mean, rstd = ops.layer_norm_fwd(t(x), t(g), t(b), out_dtype=torch.bfloat16)
+    ry, _, _ = oracle.layernorm_fwd(x, g, b)
+    close(y.float().cpu(), ry, 2e-2)
+    base = rng.standard_normal((rows, dim)).astype(np.float32)
+    dx = t(base)
+    ops.layer_norm_bwd(t(dy, torch.bfloat16), t(x), t(g), mean, rstd, dx=dx, accumulate_dx=True)
+    rdx, _, _ = oracle.layernorm_bwd(dy, x, g)
+    close(dx.cpu(), base + rdx, 1e-4)
+    # all-BF16
+    xb = bf16_round(x)
+    yb, mb, sb = ops.layer_norm_fwd(t(xb, torch.bfloat16), t(g), t(b))
+    close(yb.float().cpu(), oracle.layernorm_fwd(xb, g, b)[0], 2e-2)
+    dxb, dgb, dbb = ops.layer_norm_bwd(t(dy, torch.bfloat16), t(xb, torch.bfloat16), t(g), mb, sb)
+    r = oracle.layernorm_bwd(dy, xb, g)
+    close(dxb.float().cpu(), r[0], 2e-2)
+    close(dgb.cpu(), r[1], 1e-3)
+
+
+def test_layernorm_empty_rows(cuda):
+    from magma_b200 import ops
+
+    x = torch.empty((0, 768), device="cuda")
+    g = torch.ones(768, device="cuda")
+    y, _, _ = ops.layer_norm_fwd(x, g, torch.zeros_like(g))
+    assert y.shape == (0, 768)
+
+
+# -------------------------------------------------------------------------- Adam
+@pytest.mark.parametrize("n", [1, 7, 101_770, 1 << 20])
+def test_adam_matches_oracle_bitwise(cuda, oracle, n):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(n)
+    p = rng.standard_normal(n).astype(np.float32)
+    m = np.zeros(n, np.float32)
+    v = np.zeros(n, np.float32)
+    tp, tm, tv = t(p), t(m), t(v)
+    for step in range(1, 4):
+        g = rng.standard_normal(n).astype(np.float32)
+        ops.adam_step(tp, t(g), tm, tv, step=step, lr=1e-3, weight_decay=0.1, grad_scale=0.5)
+        oracle.adam(p, g, m, v, lr=1e-3, weight_decay=0.1, step=step, grad_scale=0.5)
+    # no FMA contraction on either side: identical F32 op sequence
+    assert np.array_equal(tp.cpu().numpy(), p)
+    assert np.array_equal(tm.cpu().numpy(), m)
+    assert np.array_equal(tv.cpu().numpy(), v)
+
+
+def test_adam_shadow_and_multi(cuda, oracle):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(11)
+    sizes = [5, 64, 1000, 3]
+    ps = [rng.standard_normal(s).astype(np.float32) for s in sizes]
+    gs = [rng.standard_normal(s).astype(np.float32) for s in sizes]
+    tps = [t(p) for p in ps]
+    tms = [torch.zeros(s, device="cuda") for s in sizes]
+    tvs = [torch.zeros(s, device="cuda") for s in sizes]
+    ops.adam_step_multi(tps, [t(g) for g in gs], tms, tvs, step=1, lr=0.01)
+    for p, g, tp in zip(ps, gs, tps):
+        m = np.zeros_like(p); v = np.zeros_like(p)
+        oracle.adam(p, g, m, v, lr=0.01, step=1)
+        assert np.array_equal(tp.cpu().numpy(), p)
+    flat = t(rng.standard_normal(4099).astype(np.float32))
+    shadow = torch.empty(4099, dtype=torch.bfloat16, device="cuda")
+    ops.adam_step(flat, torch.ones_like(flat), torch.zeros_like(flat), torch.zeros_like(flat),
+                  step=1, lr=0.1, shadow_bf16=shadow)
+    assert torch.equal(shadow, flat.to(torch.bfloat16))
+
+
+def test_adam_closed_form(cuda):
+    from magma_b200 import ops
+
+    p = torch.ones(1, device="cuda")
+    ops.adam_step(p, torch.ones(1, device="cuda"), torch.zeros(1, device="cuda"),
+                  torch.zeros(1, device="cuda"), step=1, lr=0.1)
+    assert abs(p.item() - 0.9) < 1e-4  # AdamStepValueTests.swift:15-24
+
+
+# -------------------------------------------------------------------------- GEMM
+GEMM_SHAPES = [(128, 256, 64), (256, 512, 192), (300, 200, 136), (1024, 768, 768), (64, 72, 8),
+               (8192, 768, 768), (777, 2304, 768)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+@pytest.mark.parametrize("ta,tb", [(0, 1), (0, 0), (1, 0), (1, 1)])
+def test_gemm_bf16_tcgen05(cuda, m, n, k, ta, tb):
+    from magma_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n * 3 + k + ta * 2 + tb)
+    a = torch.randn((k, m) if ta else (m, k), device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn((n, k) if tb else (k, n), device="cuda", generator=g).to(torch.bfloat16)
+    ref = (a.float().T if ta else a.float()) @ (b.float().T if tb else b.float())
+    out = ops.gemm(a, b, trans_a=bool(ta), trans_b=bool(tb), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ops.device_error_check() == 0
+    close(out.cpu(), ref.cpu(), 1e-4)
+    out16 = ops.gemm(a, b, trans_a=bool(ta), trans_b=bool(tb))
+    close(out16.float().cpu(), ref.cpu(), 2e-2)
+
+
+def test_gemm_bf16_epilogues(cuda, oracle):
+    from magma_b200 import ops, lib
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    m, n, k = 512, 384, 256
+    a = torch.randn((m, k), device="cuda", generator=g).to(torch.bfloat16)
+    w = torch.randn((n, k), device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randn(n, device="cuda", generator=g)
+    acc = a.float() @ w.float().T
+    pre = acc + bias
+    y = ops.gemm(a, w, trans_b=True, out_dtype=torch.float32, epilogue=lib.EPI_BIAS, bias=bias)
+    close(y.cpu(), pre.cpu(), 1e-4)
+    aux = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    yg = ops.gemm(a, w, trans_b=True, epilogue=lib.EPI_BIAS_GELU, bias=bias, aux_out=aux)
+    close(aux.float().cpu(), pre.cpu(), 2e-2)
+    close(yg.float().cpu(), oracle.gelu_fwd(pre.cpu().numpy()), 2e-2)
+    resid = torch.randn((m, n), device="cuda", generator=g)
+    yr = ops.gemm(a, w, trans_b=True, out_dtype=torch.float32, epilogue=lib.EPI_BIAS_RESIDUAL,
+                  bias=bias, aux_in=resid)
+    close(yr.cpu(), (resid + pre).cpu(), 1e-4)
+    dg = ops.gemm(a, w, trans_b=True, epilogue=lib.EPI_DGELU, aux_in=aux)
+    want = oracle.gelu_bwd(aux.float().cpu().numpy(), acc.cpu().numpy())
+    close(dg.float().cpu(), want, 2e-2)
+    c = torch.randn((m, n), device="cuda", generator=g)
+    c0 = c.clone()
+    ops.gemm(a, w, trans_b=True, out=c, epilogue=lib.EPI_ACCUMULATE)
+    close(c.cpu(), (c0 + acc).cpu(), 1e-4)
+    yr2 = ops.gemm(a, w, trans_b=True, out_dtype=torch.float32, epilogue=lib.EPI_BIAS_RELU,
+                   bias=bias, aux_out=torch.empty((m, n), device="cuda"))
+    close(yr2.cpu(), torch.relu(pre).cpu(), 1e-4)
+
+
+@pytest.mark.parametrize("m,n,k,ta,tb", [(256, 128, 784, 0, 0), (784, 128, 256, 1, 0),
+                                          (256, 784, 128, 0, 1), (100, 33, 17, 1, 1),
+                                          (16384, 384, 384, 0, 1)])
+def test_gemm_f32_matches_oracle(cuda, oracle, m, n, k, ta, tb):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((k, m) if ta else (m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k) if tb else (k, n)).astype(np.float32)
+    out = ops.gemm(t(a), t(b), trans_a=bool(ta), trans_b=bool(tb))
+    ref = oracle.matmul(a, b, bool(ta), bool(tb))
+    close(out.cpu(), ref, 1e-4)
+
+
+def test_gemm_rejects_bad_arguments(cuda):
+    from magma_b200 import ops, lib
+
+    a = torch.zeros((4, 8), device="cuda")
+    with pytest.raises(lib.MagmaError) as e:
+        ops.gemm(a, a, epilogue=lib.EPI_BIAS_RESIDUAL)
+    assert e.value.status == lib.INVALID_ARGUMENT and "aux_in" in e.value.message
+
+
+# --------------------------------------------------------------------- attention
+def qkv(rng, shape, dtype):
+    arrs = [rng.standard_normal(shape).astype(np.float32) for _ in range(4)]
+    if dtype == torch.bfloat16:
+        arrs = [bf16_round(a) for a in arrs]
+    return arrs
+
+
+@pytest.mark.parametrize("shape,causal", [((1, 12, 1024, 64), True), ((2, 3, 100, 64), True),
+                                          ((1, 2, 256, 32), False), ((1, 1, 4, 4), False),
+                                          ((2, 6, 256, 64), True), ((1, 2, 70, 128), True)])
+def test_attention_f32(cuda, oracle, shape, causal):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(sum(shape))
+    q, k, v, do = qkv(rng, shape, torch.float32)
+    scale = 1 / math.sqrt(shape[-1])
+    o, lse = ops.attention_fwd(t(q), t(k), t(v), scale, causal)
+    ro, rlse = oracle.attention_fwd(q, k, v, scale, causal)
+    close(o.cpu(), ro, 1e-4)
+    close(lse.cpu(), rlse, 1e-5)
+    dq, dk, dv = ops.attention_bwd(t(q), t(k), t(v), o, t(do), lse, scale, causal)
+    rdq, rdk, rdv = oracle.attention_bwd(q, k, v, do, scale, causal)
+    close(dq.cpu(), rdq, 1e-4)
+    close(dk.cpu(), rdk, 1e-4)
+    close(dv.cpu(), rdv, 1e-4)
+
+
+@pytest.mark.parametrize("shape", [(1, 12, 1024, 64), (2, 2, 320, 64), (1, 1, 64, 64)])
+def test_attention_bf16(cuda, oracle, shape):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(sum(shape) + 1)
+    q, k, v, do = qkv(rng, shape, torch.bfloat16)
+    scale = 1 / math.sqrt(shape[-1])
+    bt = lambda a: t(a, torch.bfloat16)  # noqa: E731
+    o, lse = ops.attention_fwd(bt(q), bt(k), bt(v), scale, True)
+    torch.cuda.synchronize()
+    assert ops.device_error_check() == 0
+    ro, rlse = oracle.attention_fwd(q, k, v, scale, True)
+    close(o.float().cpu(), ro, 2e-2)
+    close(lse.cpu(), rlse, 1e-3)
+    dq, dk, dv = ops.attention_bwd(bt(q), bt(k), bt(v), o, bt(do), lse, scale, True)
+    torch.cuda.synchronize()
+    assert ops.device_error_check() == 0
+    rdq, rdk, rdv = oracle.attention_bwd(q, k, v, do, scale, True)
+    close(dq.float().cpu(), rdq, 2e-2)
+    close(dk.float().cpu(), rdk, 2e-2)
+    close(dv.float().cpu(), rdv, 2e-2)
+
+
+def test_attention_strided_qkv_layout(cuda, oracle):
+    """Q/K/V read straight out of a fused [B, S, 3, H, D] QKV projection."""
+    from magma_b200 import ops
+
+    B, S, H, D = 2, 256, 4, 64
+    rng = np.random.default_rng(9)
+    packed = rng.standard_normal((B, S, 3, H, D)).astype(np.float32)
+    tp = t(packed)
+    q = tp[:, :, 0].permute(0, 2, 1, 3)
+    k = tp[:, :, 1].permute(0, 2, 1, 3)
+    v = tp[:, :, 2].permute(0, 2, 1, 3)
+    o = torch.empty((B, S, H, D), device="cuda").permute(0, 2, 1, 3)
+    ops.attention_fwd(q, k, v, 0.125, True, out=o)
+    ro, _ = oracle.attention_fwd(q.cpu().contiguous().numpy(), k.cpu().contiguous().numpy(),
+                                 v.cpu().contiguous().numpy(), 0.125, True)
+    close(o.cpu(), ro, 1e-4)
+
+
+# -------------------------------------------------------------------------- glue
+@pytest.mark.parametrize("rows,classes,ld", [(256, 10, 10), (64, 65, 72), (33, 50257, 50304)])
+def test_cross_entropy(cuda, oracle, rows, classes, ld):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(classes)
+    x = (3 * rng.standard_normal((rows, classes))).astype(np.float32)
+    tg = rng.integers(0, classes, rows).astype(np.int32)
+    buf = torch.zeros((rows, ld), device="cuda")
+    buf[:, :classes] = t(x)
+    losses = ops.cross_entropy_fwd_bwd(buf, t(tg, torch.int32), classes=classes)
+    loss = ops.reduce_sum(losses, 1.0 / rows)
+    rloss, rd = oracle.cross_entropy(x, tg)
+    assert abs(loss.item() - rloss) <= 1e-5 * max(1.0, abs(rloss))
+    close(buf[:, :classes].cpu(), rd, 1e-4)
+    assert torch.count_nonzero(buf[:, classes:]).item() == 0
+
+
+def test_cross_entropy_closed_form(cuda):
+    from magma_b200 import ops
+
+    logits = t([[1, 2, 3], [1, 1, 1]])
+    losses = ops.cross_entropy_fwd_bwd(logits, t([2, 0], torch.int32))
+    lse0 = 3 + math.log(1 + math.exp(-1) + math.exp(-2))
+    lse1 = 1 + math.log(3)
+    assert abs(losses.mean().item() - ((lse0 - 3) + (lse1 - 1)) / 2) < 1e-6
+
+
+def test_embedding_fwd_bwd(cuda):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(3)
+    B, S, D, V = 4, 16, 32, 50
+    tok = rng.integers(0, V, (B, S)).astype(np.int32)
+    wte = rng.standard_normal((V, D)).astype(np.float32)
+    wpe = rng.standard_normal((S, D)).astype(np.float32)
+    out = ops.embedding_fwd(t(tok, torch.int32), t(wte), t(wpe))
+    close(out.cpu(), (wte[tok] + wpe[None]).reshape(B * S, D), 1e-6)
+    dout = rng.standard_normal((B * S, D)).astype(np.float32)
+    dwte = torch.zeros((V, D), device="cuda")
+    dwpe = torch.zeros((S, D), device="cuda")
+    ops.embedding_bwd(t(tok, torch.int32), t(dout), dwte, dwpe)
+    want = np.zeros((V, D), np.float64)
+    np.add.at(want, tok.reshape(-1), dout)
+    close(dwte.cpu(), want, 1e-5)
+    close(dwpe.cpu(), dout.reshape(B, S, D).sum(0), 1e-5)
+
+
+def test_bad_token_sets_device_error(cuda):
+    from magma_b200 import ops, lib
+
+    tok = t([[0, 99]], torch.int32)
+    ops.embedding_fwd(tok, torch.zeros((10, 8), device="cuda"), None)
+    with pytest.raises(lib.MagmaError) as e:
+        ops.device_error_check()
+    assert e.value.status == lib.OUT_OF_RANGE
+    assert ops.device_error_check() == 0  # the word is cleared after it is read
+
+
+def test_gelu_relu_bias_convert(cuda, oracle):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(4)
+    x = (2 * rng.standard_normal(10001)).astype(np.float32)
+    dy = rng.standard_normal(10001).astype(np.float32)
+    close(ops.gelu_fwd(t(x)).cpu(), oracle.gelu_fwd(x), 1e-5)
+    close(ops.gelu_bwd(t(x), t(dy)).cpu(), oracle.gelu_bwd(x, dy), 1e-5)
+    close(ops.relu_fwd(t(x)).cpu(), np.maximum(x, 0), 0)
+    close(ops.relu_bwd(t(x), t(dy)).cpu(), np.where(x > 0, dy, 0), 0)
+    m = rng.standard_normal((3001, 77)).astype(np.float32)
+    close(ops.bias_grad(t(m)).cpu(), m.astype(np.float64).sum(0), 1e-5)
+    dst = torch.empty(10001, dtype=torch.bfloat16, device="cuda")
+    ops.convert(t(x), dst)
+    assert torch.equal(dst, t(x).to(torch.bfloat16))

@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""GPT-2-small BF16 training-step throughput on 1..8 B200s (one process per GPU).
+
+A step is one forward + backward of GPT-2 small (124M, 12 layers, 12 heads,
+d_model 768, ctx 1024, vocab 50257, tied embeddings) on a batch of 8
+sequences per GPU, the NCCL gradient all-reduce (N > 1) and the Adam update of
+the F32 master weights — all kernels from libmagma_cuda.so. Inputs are
+synthetic token ids uniform over the vocabulary (seeded per rank); weights are
+random N(0, 0.02).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl magma|reference]
+
+Prints one JSON line (rank 0). `value` is whole-job tokens/s with the batch
+already resident on the GPU, timed with CUDA events over K steps between
+barriers (max over ranks). `e2e` is the same metric through the public
+train_step() call with the token batch copied from pinned host memory and the
+loss read back every step. `--impl reference` times the CPU restatement of the
+reference's op sequence (oracle/) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "GPT-2-small train tokens/s at 1/2/4/8 B200; fused attn/LN % of roofline"
+UNIT = "tokens/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def workload_config(world: int, batch: int) -> dict:
+    return {"workload": "GPT-2 small (124M: 12 layers, 12 heads, d_model 768, ctx 1024, vocab "
+                        "50257, tied lm-head) BF16 train step, F32 master weights + Adam",
+            "model": "gpt2-small-124M", "global_batch": batch * world, "seq_len": 1024,
+            "batch_per_gpu": batch, "parallelism": f"dp{world}",
+            "l2": "no flush: each step streams >4 GB of weights and activations (L2 is 126 MB)"}
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"], stdout=open(self.path, "w"),
+                stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                "reasons": reasons, "samples": len(rows)}
+
+
+def physical_gpu(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",")]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+# ----------------------------------------------------------------- instrumentation
+def instrumented_step(trainer, lib, torch):
+    """One eager forward+backward+Adam with CUDA events around every library
+    call; returns per-kind times (ms), algorithmic work and launch counts."""
+    rec = []
+    orig = lib.call
+
+    def timed_call(name, *args):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        orig(name, *args)
+        e.record()
+        rec.append((name, args, s, e))
+
+    lib.call = timed_call
+    try:
+        trainer.step_fwd_bwd()
+        trainer.optimizer_step()
+    finally:
+        lib.call = orig
+    torch.cuda.synchronize()
+    cfg = trainer.cfg
+    out = {}
+    for name, args, s, e in rec:
+        ms = s.elapsed_time(e)
+        kind, work = classify(name, args, cfg, trainer)
+        d = out.setdefault(kind, {"ms": 0.0, "work": 0.0, "calls": 0, "launches": 0})
+        d["ms"] += ms
+        d["work"] += work
+        d["calls"] += 1
+        d["launches"] += lib.KERNELS_PER_CALL.get(name, 1)
+    return out
+
+
+def classify(name, args, cfg, tr):
+    """(kind, algorithmic work) for one library call: FLOPs for contractions,
+    bytes for the memory-bound kernels."""
+    if name == "magma_gemm":
+        m, n, k = args[3], args[4], args[5]
+        return "gemm", 2.0 * m * n * k
+    if name.startswith("magma_attention"):
+        i = 5 if name == "magma_attention_fwd" else 9
+        B, H, S, hd = args[i], args[i + 1], args[i + 2], args[i + 3]
+        causal_pairs = S * (S + 1) / 2
+        if name == "magma_attention_fwd":
+            return "attention_fwd", 4.0 * B * H * hd * causal_pairs
+        return "attention_bwd", 8.0 * B * H * hd * causal_pairs
+    if name == "magma_layernorm_fwd":
+        rows, dim = args[6], args[7]
+        xb = 4 if args[9] == 10 else 2
+        yb = 4 if args[10] == 10 else 2
+        return "layernorm", rows * dim * (xb + yb) + rows * 8
+    if name == "magma_layernorm_bwd":
+        rows, dim = args[8], args[9]
+        dyb = 4 if args[10] == 10 else 2
+        xb = 4 if args[11] == 10 else 2
+        dxb = 4 if args[12] == 10 else 2
+        acc = dxb if args[13] else 0
+        return "layernorm", rows * dim * (dyb + xb + dxb + acc) + rows * 8
+    if name == "magma_adam_step":
+        n = args[5]
+        return "adam", n * (28 + (2 if args[4] else 0))
+    return "other", 0.0
+
+
+# ------------------------------------------------------------------- CPU baseline
+def cpu_baseline(budget_s: float = 20.0) -> dict:
+    """Oracle GPT-2-small fwd+bwd+Adam on a bounded sample, all host threads."""
+    import numpy as np
+
+    from oracle import oracle
+
+    oracle.build()
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    seq = 64
+    cfg = oracle.gpt_config(vocab=50257, seq=seq, layers=12, heads=12, dim=768, tied=True)
+    n = oracle.gpt_param_count(cfg)
+    rng = np.random.default_rng(0)
+    params = (0.02 * rng.standard_normal(n)).astype(np.float32)
+    m = np.zeros(n, np.float32)
+    v = np.zeros(n, np.float32)
+    tok = rng.integers(0, 50257, (1, seq)).astype(np.int32)
+    tgt = rng.integers(0, 50257, (1, seq)).astype(np.int32)
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tgt)
+        oracle.adam(params, g, m, v, lr=3e-4, step=steps + 1)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or steps >= 3:
+            break
+    return {"value": steps * seq / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} step(s) of GPT-2 small (124M, 12 layers) F32 fwd+bwd+Adam on 1 x "
+                      f"{seq} tokens (positions < {seq}), oracle/ C restatement, OpenMP "
+                      f"{threads} threads, {el:.1f} s"}
+
+
+def run_reference(args) -> None:
+    """--impl reference: the oracle port of the reference's CPU path, timed."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import oracle
+
+    oracle.build()
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    rng = np.random.default_rng(0)
+
+    def make(seq):
+        cfg = oracle.gpt_config(vocab=50257, seq=seq, layers=12, heads=12, dim=768, tied=True)
+        n = oracle.gpt_param_count(cfg)
+        params = (0.02 * rng.standard_normal(n)).astype(np.float32)
+        return cfg, params, np.zeros(n, np.float32), np.zeros(n, np.float32)
+
+    seq = 64
+    cfg, params, m, v = make(seq)
+    tok = rng.integers(0, 50257, (1, seq)).astype(np.int32)
+    t0 = time.perf_counter()
+    _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tok)
+    oracle.adam(params, g, m, v, lr=3e-4, step=1)
+    first = time.perf_counter() - t0
+    total = args.steps + args.warmup
+    # shrink the per-step sample so the whole run stays within ~3 minutes
+    while seq > 8 and first * total * 1.0 > 180.0:
+        seq //= 2
+        first /= 2.0
+    cfg, params, m, v = make(seq)
+    tok = rng.integers(0, 50257, (1, seq)).astype(np.int32)
+    tgt = rng.integers(0, 50257, (1, seq)).astype(np.int32)
+    for i in range(args.warmup):
+        _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tgt)
+        oracle.adam(params, g, m, v, lr=3e-4, step=i + 1)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tgt)
+        oracle.adam(params, g, m, v, lr=3e-4, step=args.warmup + i + 1)
+    el = time.perf_counter() - t0
+    value = args.steps * seq / el
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(world, args.batch),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"per step: GPT-2 small F32 fwd+bwd+Adam on 1 x {seq} "
+                                       "tokens (the oracle/ C restatement of the reference's "
+                                       "op sequence; the Swift/XLA reference cannot be built "
+                                       "here)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--impl", choices=["magma", "reference"], default="magma")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from magma_b200 import dp, lib
+    from magma_b200.gpt import GPTTrainer, gpt2_small
+
+    rank, world, local = dp.init_from_env()
+    torch.cuda.set_device(local)
+    cfg = gpt2_small()
+    B, S = args.batch, cfg.seq
+    tr = GPTTrainer(cfg, B, "bf16", lr=3e-4, seed=0)
+    sync = dp.GradSync()
+    gen = torch.Generator().manual_seed(1234 + rank)
+    tok_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()
+    tgt_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()
+    tr.set_batch(tok_h, tgt_h)
+    torch.cuda.synchronize()
+    if not args.no_graph:
+        tr.capture()
+
+    def step():
+        tr.run_fwd_bwd()
+        tr.optimizer_step(grad_scale=sync(tr.grads))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # ---------------- timed region: batch resident in HBM ----------------
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu(local)) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    clocks = clk.summary()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens_per_step = B * S * world
+    value = tokens_per_step / (ms / 1e3)
+    loss_now = float(tr.loss.item())
+
+    # ---------------- e2e through the public call (host batch, host loss) ----------------
+    e2e_steps = max(3, min(args.steps, 20))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        tr.train_step(tok_h, tgt_h, allreduce=sync)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # ---------------- per-kernel roofline (eager step with events) ----------------
+    kinds = instrumented_step(tr, lib, torch)
+    peaks, peak_src = load_peaks()
+    total_ms = sum(d["ms"] for d in kinds.values())
+    launches = sum(d["launches"] for d in kinds.values())
+
+    def entry(kind, bound):
+        d = kinds.get(kind)
+        if not d or d["ms"] <= 0:
+            return None
+        if bound == "tensor":
+            ach = d["work"] / (d["ms"] / 1e3) / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            unit = "TFLOP/s"
+        else:
+            ach = d["work"] / (d["ms"] / 1e3) / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        return {"bound": "hbm" if bound == "hbm" else "tensor", "achieved": round(ach, 1),
+                "peak": peak, "unit": unit, "frac": round(ach / peak, 4),
+                "share": round(d["ms"] / total_ms, 4), "ms_per_step": round(d["ms"], 4),
+                "launches_per_step": d["launches"]}
+
+    gemm = entry("gemm", "tensor")
+    roof = dict(gemm) if gemm else {}
+    roof.update({"kernel": "gemm_tcgen05 (all GEMMs of one step)",
+                 "peak_source": f"{peak_src} bf16_tflops_sustained (kernels timed inside a step)",
+                 "traffic": None})
+    others = {k: entry(k, b) for k, b in (("attention_fwd", "tensor"), ("attention_bwd", "tensor"),
+                                           ("layernorm", "hbm"), ("adam", "hbm"))}
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(world, B),
+        "e2e": {"value": round(tokens_per_step / (e2e_ms / 1e3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": int(tok_h.numel() * 4 + tgt_h.numel() * 4),
+                "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4),
+                "call": "GPTTrainer.train_step(host tokens, host targets) -> host loss"},
+        "roofline": roof, "kernels": others,
+        "cpu_baseline": cpu,
+        "gpu_launches": int(launches * args.steps),
+        "clocks": clocks, "loss": round(loss_now, 4),
+        "mfu": round(6.54e12 / (ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

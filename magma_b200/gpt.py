@@ -1,0 +1,390 @@
+"""GPT decoder training step built only from libmagma_cuda.so kernels.
+
+The model is the reference benchmark's pre-LN decoder
+(Benchmarks/GPT2Shakespeare/Sources/main.swift:437-498): token + learned
+position embedding, per block LN -> QKV linear -> causal SDPA -> output linear
+-> residual, LN -> 4x linear -> GELU(tanh) -> linear -> residual, final LN,
+lm-head, softmax cross-entropy (mean). The reference's three Q/K/V weight
+matrices are stored as one [3D, D] matrix (their row concatenation: the same
+products), and the lm-head is tied to the token embedding (GPT-2 small's 124M
+parameters; ``tied=False`` gives the reference's separate lm-head).
+
+Forward and backward are written out explicitly (the VJPs of
+Sources/Core/Autodiff.swift, fused): the GEMM epilogues carry bias, GELU,
+residual add and the GELU VJP; LayerNorm backward accumulates into the F32
+residual gradient; Q/K/V are read in place from the fused projection and dQ/
+dK/dV written back into the same layout. Two precisions:
+
+* ``"bf16"``: BF16 GEMM/attention/LN IO on the tcgen05 tensor cores, F32
+  residual stream, F32 master weights, gradients and Adam moments; a BF16
+  shadow of the weights is written by the Adam kernel each step.
+* ``"f32"``: everything F32 (F32-accurate FFMA GEMM and SIMT attention), for
+  parity with the F32 oracle.
+
+Parameters live in one F32 arena whose layout equals the oracle's
+(oracle_gpt_param_offset): wte, wpe, per layer [ln1_w, ln1_b, qkv_w, qkv_b,
+proj_w, proj_b, ln2_w, ln2_b, fc_w, fc_b, fcproj_w, fcproj_b], lnf_w, lnf_b,
+[lm_head], every tensor starting on a 64-float boundary.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import lib
+
+PER_LAYER = ["ln1_w", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ln2_w", "ln2_b", "fc_w",
+             "fc_b", "fcproj_w", "fcproj_b"]
+
+
+@dataclass
+class GPTConfig:
+    vocab: int = 50257
+    seq: int = 1024
+    layers: int = 12
+    heads: int = 12
+    dim: int = 768
+    tied: bool = True
+    vocab_padded: int | None = None
+
+    def __post_init__(self):
+        if self.vocab_padded is None:
+            self.vocab_padded = (self.vocab + 127) // 128 * 128
+        assert self.dim % self.heads == 0
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.heads
+
+    def shapes(self) -> list[tuple[str, tuple[int, ...]]]:
+        D, Vp = self.dim, self.vocab_padded
+        out = [("wte", (Vp, D)), ("wpe", (self.seq, D))]
+        per = {"ln1_w": (D,), "ln1_b": (D,), "qkv_w": (3 * D, D), "qkv_b": (3 * D,),
+               "proj_w": (D, D), "proj_b": (D,), "ln2_w": (D,), "ln2_b": (D,),
+               "fc_w": (4 * D, D), "fc_b": (4 * D,), "fcproj_w": (D, 4 * D), "fcproj_b": (D,)}
+        for l in range(self.layers):
+            out += [(f"h{l}.{n}", per[n]) for n in PER_LAYER]
+        out += [("lnf_w", (D,)), ("lnf_b", (D,))]
+        if not self.tied:
+            out.append(("lm_head", (Vp, D)))
+        return out
+
+    def offsets(self) -> dict[str, tuple[int, tuple[int, ...]]]:
+        off = 0
+        table = {}
+        for name, shp in self.shapes():
+            table[name] = (off, shp)
+            off += (math.prod(shp) + 63) // 64 * 64
+        table["__total__"] = (off, ())
+        return table
+
+    def num_params(self) -> int:
+        """Parameters excluding the vocabulary padding rows."""
+        n = sum(math.prod(s) for _, s in self.shapes())
+        pad = (self.vocab_padded - self.vocab) * self.dim
+        return n - pad * (1 if self.tied else 2)
+
+
+def gpt2_small() -> GPTConfig:
+    return GPTConfig(vocab=50257, seq=1024, layers=12, heads=12, dim=768, tied=True)
+
+
+def char_gpt() -> GPTConfig:
+    return GPTConfig(vocab=65, seq=256, layers=6, heads=6, dim=384, tied=True)
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class GPTTrainer:
+    """One data-parallel replica: parameters, Adam state, activations, step.
+
+    ``step_fwd_bwd`` runs forward + backward on the resident token batch;
+    ``optimizer_step`` applies Adam to the (optionally already averaged)
+    gradients; ``train_step`` is the public end-to-end call (host tokens in,
+    host loss out). ``capture()`` records forward+backward as one CUDA graph.
+    """
+
+    def __init__(self, cfg: GPTConfig, batch: int, precision: str = "bf16", lr: float = 3e-4,
+                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8,
+                 weight_decay: float = 0.0, seed: int = 0, device: int | None = None,
+                 init_std: float = 0.02):
+        assert precision in ("bf16", "f32")
+        self.cfg, self.B, self.precision = cfg, batch, precision
+        self.lr, self.beta1, self.beta2, self.eps, self.wd = lr, beta1, beta2, eps, weight_decay
+        self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        lib.call("magma_init", self.dev.index)
+        self.table = cfg.offsets()
+        P = self.table["__total__"][0]
+        self.P = P
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        self.params = torch.zeros(P, **f32)
+        self.grads = torch.zeros(P, **f32)
+        self.m = torch.zeros(P, **f32)
+        self.v = torch.zeros(P, **f32)
+        self.t = 0
+        self._init_params(seed, init_std)
+        self.act_dtype = torch.bfloat16 if precision == "bf16" else torch.float32
+        self.DT = lib.BF16 if precision == "bf16" else lib.F32
+        if precision == "bf16":
+            self.shadow = torch.empty(P, dtype=torch.bfloat16, device=self.dev)
+            self._sync_shadow()
+        else:
+            self.shadow = None
+        self._alloc_activations()
+        self.graph = None
+
+    # ------------------------------------------------------------------ params
+    def view(self, arena: torch.Tensor, name: str) -> torch.Tensor:
+        off, shp = self.table[name]
+        return arena[off:off + math.prod(shp)].view(*shp)
+
+    def _init_params(self, seed: int, std: float) -> None:
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        host = torch.zeros(self.P, dtype=torch.float32)
+        cfg = self.cfg
+        for name, shp in cfg.shapes():
+            off = self.table[name][0]
+            n = math.prod(shp)
+            base = name.split(".")[-1]
+            if base.endswith("_w") and base.startswith("ln"):
+                host[off:off + n] = 1.0
+            elif base.endswith("_b"):
+                host[off:off + n] = 0.0
+            else:
+                host[off:off + n] = torch.randn(n, generator=g) * std
+        for name in ("wte", "lm_head"):
+            if name in self.table:
+                off, (vp, d) = self.table[name]
+                host[off + cfg.vocab * d: off + vp * d] = 0.0  # padding rows stay zero
+        self.params.copy_(host)
+
+    def load_params(self, flat: torch.Tensor) -> None:
+        self.params.copy_(flat.to(self.params.device, torch.float32))
+        if self.shadow is not None:
+            self._sync_shadow()
+
+    def _sync_shadow(self) -> None:
+        lib.call("magma_convert", _p(self.params), _p(self.shadow), self.P, lib.F32, lib.BF16,
+                 self._s())
+
+    def _s(self) -> int:
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def weight(self, name: str) -> torch.Tensor:
+        """The GEMM operand for a weight: BF16 shadow or F32 master."""
+        return self.view(self.shadow if self.shadow is not None else self.params, name)
+
+    # ------------------------------------------------------------- activations
+    def _alloc_activations(self) -> None:
+        cfg, B = self.cfg, self.B
+        T, D, L, Vp = B * cfg.seq, cfg.dim, cfg.layers, cfg.vocab_padded
+        H = cfg.heads
+        a = dict(dtype=self.act_dtype, device=self.dev)
+        f = dict(dtype=torch.float32, device=self.dev)
+        self.T = T
+        self.tokens = torch.zeros((B, cfg.seq), dtype=torch.int32, device=self.dev)
+        self.targets = torch.zeros((B, cfg.seq), dtype=torch.int32, device=self.dev)
+        self.x = torch.empty((L + 1, T, D), **f)      # residual entering each block (+ final)
+        self.h = torch.empty((L, T, D), **f)          # after the attention residual
+        self.ln1 = torch.empty((L, T, D), **a)
+        self.ln2 = torch.empty((L, T, D), **a)
+        self.stats = torch.empty((L, 4, T), **f)      # mean1, rstd1, mean2, rstd2
+        self.qkv = torch.empty((L, T, 3 * D), **a)
+        self.att = torch.empty((L, T, D), **a)
+        self.lse = torch.empty((L, B, H, cfg.seq), **f)
+        self.fc_pre = torch.empty((L, T, 4 * D), **a)
+        self.fc_act = torch.empty((L, T, 4 * D), **a)
+        self.lnf = torch.empty((T, D), **a)
+        self.lnf_stats = torch.empty((2, T), **f)
+        self.logits = torch.empty((T, Vp), **a)
+        self.losses = torch.empty(T, **f)
+        self.loss = torch.empty(1, **f)
+        self.dresid = torch.empty((T, D), **f)
+        self.dresid_a = torch.empty((T, D), **a) if self.act_dtype != torch.float32 else None
+        self.d_ln = torch.empty((T, D), **a)
+        self.d_fc = torch.empty((T, 4 * D), **a)
+        self.d_att = torch.empty((T, D), **a)
+        self.dqkv = torch.empty((T, 3 * D), **a)
+        ws = max(lib.query("magma_layernorm_bwd_workspace_size", T, D),
+                 lib.query("magma_attention_bwd_workspace_size", B, H, cfg.seq, cfg.head_dim, self.DT),
+                 lib.query("magma_bias_grad_workspace_size", T, 4 * D),
+                 lib.query("magma_bias_grad_workspace_size", T, 3 * D))
+        self.ws = torch.empty(max(ws, 1 << 20), dtype=torch.uint8, device=self.dev)
+        # attention geometry over the fused [B, S, 3, H, hd] projection
+        S, hd = cfg.seq, cfg.head_dim
+        self.qkv_strides = (C.c_int64 * 3)(S * 3 * D, hd, 3 * D)
+        self.o_strides = (C.c_int64 * 3)(S * D, hd, D)
+        self.scale = 1.0 / math.sqrt(hd)
+
+    # -------------------------------------------------------------- primitives
+    def _gemm(self, a, b, c, m, n, k, lda, ldb, ldc, ta, tb, epi, bias=None, aux_in=None,
+              aux_out=None, c_dtype=None):
+        lib.call("magma_gemm", _p(a), _p(b), _p(c), m, n, k, lda, ldb, ldc, ta, tb, self.DT,
+                 c_dtype if c_dtype is not None else self.DT, epi, _p(bias), _p(aux_in),
+                 _p(aux_out), None, 0, self._s())
+
+    def _ln_fwd(self, x, w, b, y, mean, rstd):
+        lib.call("magma_layernorm_fwd", _p(x), _p(w), _p(b), _p(y), _p(mean), _p(rstd), self.T,
+                 self.cfg.dim, 1e-5, lib.F32, self.DT, self._s())
+
+    def _ln_bwd(self, dy, x, w, mean, rstd, dw, db):
+        lib.call("magma_layernorm_bwd", _p(dy), _p(x), _p(w), _p(mean), _p(rstd),
+                 _p(self.dresid), _p(dw), _p(db), self.T, self.cfg.dim, self.DT, lib.F32, lib.F32,
+                 1, 0, _p(self.ws), self.ws.numel(), self._s())
+
+    def _bias_grad(self, dy, db, cols):
+        lib.call("magma_bias_grad", _p(dy), _p(db), self.T, cols, cols,
+                 lib.F32 if dy.dtype == torch.float32 else lib.BF16, 0, _p(self.ws),
+                 self.ws.numel(), self._s())
+
+    # ------------------------------------------------------------ fwd + bwd
+    def step_fwd_bwd(self) -> None:
+        """Forward + backward on the resident batch; writes self.grads and self.loss."""
+        cfg, T, D, L = self.cfg, self.T, self.cfg.dim, self.cfg.layers
+        s = self._s()
+        P, G, W = self.params, self.grads, self.weight
+        V, Vp = cfg.vocab, cfg.vocab_padded
+        E = lib
+        # embeddings (F32 master tables, main.swift:454-458)
+        lib.call("magma_embedding_fwd", _p(self.tokens), _p(self.view(P, "wte")),
+                 _p(self.view(P, "wpe")), _p(self.x[0]), self.B, cfg.seq, D, Vp, s)
+        for l in range(L):
+            n = lambda k: f"h{l}.{k}"  # noqa: E731
+            st = self.stats[l]
+            self._ln_fwd(self.x[l], self.view(P, n("ln1_w")), self.view(P, n("ln1_b")),
+                         self.ln1[l], st[0], st[1])
+            self._gemm(self.ln1[l], W(n("qkv_w")), self.qkv[l], T, 3 * D, D, D, D, 3 * D, 0, 1,
+                       E.EPI_BIAS, bias=self.view(P, n("qkv_b")))
+            q = self.qkv[l]
+            lib.call("magma_attention_fwd", _p(q), q.data_ptr() + D * q.element_size(),
+                     q.data_ptr() + 2 * D * q.element_size(), _p(self.att[l]), _p(self.lse[l]),
+                     self.B, cfg.heads, cfg.seq, cfg.head_dim, self.qkv_strides, self.o_strides,
+                     self.scale, 1, self.DT, s)
+            self._gemm(self.att[l], W(n("proj_w")), self.h[l], T, D, D, D, D, D, 0, 1,
+                       E.EPI_BIAS_RESIDUAL, bias=self.view(P, n("proj_b")), aux_in=self.x[l],
+                       c_dtype=lib.F32)
+            self._ln_fwd(self.h[l], self.view(P, n("ln2_w")), self.view(P, n("ln2_b")),
+                         self.ln2[l], st[2], st[3])
+            self._gemm(self.ln2[l], W(n("fc_w")), self.fc_act[l], T, 4 * D, D, D, D, 4 * D, 0, 1,
+                       E.EPI_BIAS_GELU, bias=self.view(P, n("fc_b")), aux_out=self.fc_pre[l])
+            self._gemm(self.fc_act[l], W(n("fcproj_w")), self.x[l + 1], T, D, 4 * D, 4 * D, 4 * D,
+                       D, 0, 1, E.EPI_BIAS_RESIDUAL, bias=self.view(P, n("fcproj_b")),
+                       aux_in=self.h[l], c_dtype=lib.F32)
+        self._ln_fwd(self.x[L], self.view(P, "lnf_w"), self.view(P, "lnf_b"), self.lnf,
+                     self.lnf_stats[0], self.lnf_stats[1])
+        head = "wte" if cfg.tied else "lm_head"
+        self._gemm(self.lnf, W(head), self.logits, T, Vp, D, D, D, Vp, 0, 1, E.EPI_NONE)
+        # loss and dlogits in place (main.swift:412-433), mean over rows
+        lib.call("magma_cross_entropy_fwd_bwd", _p(self.logits), _p(self.targets), _p(self.losses),
+                 T, V, Vp, 1.0 / T, self.DT, s)
+        lib.call("magma_reduce_sum", _p(self.losses), _p(self.loss), T, 1.0 / T, s)
+
+        # ---------------------------------------------------------- backward
+        # lm-head: d(lnf) = dlogits . Wh ; dWh = dlogits^T . lnf
+        self._gemm(self.logits, W(head), self.d_ln, T, D, Vp, Vp, D, D, 0, 0, E.EPI_NONE)
+        self._gemm(self.logits, self.lnf, self.view(G, head), Vp, D, T, Vp, D, D, 1, 0, E.EPI_NONE,
+                   c_dtype=lib.F32)
+        # final LN: dresid = LN_bwd (written, not accumulated)
+        lib.call("magma_layernorm_bwd", _p(self.d_ln), _p(self.x[L]), _p(self.view(P, "lnf_w")),
+                 _p(self.lnf_stats[0]), _p(self.lnf_stats[1]), _p(self.dresid),
+                 _p(self.view(G, "lnf_w")), _p(self.view(G, "lnf_b")), T, D, self.DT, lib.F32,
+                 lib.F32, 0, 0, _p(self.ws), self.ws.numel(), s)
+        for l in reversed(range(L)):
+            n = lambda k: f"h{l}.{k}"  # noqa: E731
+            st = self.stats[l]
+            dres = self._dresid_operand()
+            # MLP: x_{l+1} = h + fcproj(gelu(fc(ln2(h))))
+            self._gemm(dres, W(n("fcproj_w")), self.d_fc, T, 4 * D, D, D, 4 * D, 4 * D, 0, 0,
+                       E.EPI_DGELU, aux_in=self.fc_pre[l])
+            self._gemm(dres, self.fc_act[l], self.view(G, n("fcproj_w")), D, 4 * D, T, D, 4 * D,
+                       4 * D, 1, 0, E.EPI_NONE, c_dtype=lib.F32)
+            self._bias_grad(self.dresid, self.view(G, n("fcproj_b")), D)
+            self._gemm(self.d_fc, W(n("fc_w")), self.d_ln, T, D, 4 * D, 4 * D, D, D, 0, 0,
+                       E.EPI_NONE)
+            self._gemm(self.d_fc, self.ln2[l], self.view(G, n("fc_w")), 4 * D, D, T, 4 * D, D, D,
+                       1, 0, E.EPI_NONE, c_dtype=lib.F32)
+            self._bias_grad(self.d_fc, self.view(G, n("fc_b")), 4 * D)
+            self._ln_bwd(self.d_ln, self.h[l], self.view(P, n("ln2_w")), st[2], st[3],
+                         self.view(G, n("ln2_w")), self.view(G, n("ln2_b")))
+            dres = self._dresid_operand()
+            # attention: h = x + proj(attn(qkv(ln1(x))))
+            self._gemm(dres, W(n("proj_w")), self.d_att, T, D, D, D, D, D, 0, 0, E.EPI_NONE)
+            self._gemm(dres, self.att[l], self.view(G, n("proj_w")), D, D, T, D, D, D, 1, 0,
+                       E.EPI_NONE, c_dtype=lib.F32)
+            self._bias_grad(self.dresid, self.view(G, n("proj_b")), D)
+            q = self.qkv[l]
+            es = q.element_size()
+            dq = self.dqkv
+            lib.call("magma_attention_bwd", _p(q), q.data_ptr() + D * es, q.data_ptr() + 2 * D * es,
+                     _p(self.att[l]), _p(self.d_att), _p(self.lse[l]), _p(dq),
+                     dq.data_ptr() + D * es, dq.data_ptr() + 2 * D * es, self.B, cfg.heads,
+                     cfg.seq, cfg.head_dim, self.qkv_strides, self.o_strides, self.scale, 1,
+                     self.DT, _p(self.ws), self.ws.numel(), s)
+            self._gemm(self.dqkv, W(n("qkv_w")), self.d_ln, T, D, 3 * D, 3 * D, D, D, 0, 0,
+                       E.EPI_NONE)
+            self._gemm(self.dqkv, self.ln1[l], self.view(G, n("qkv_w")), 3 * D, D, T, 3 * D, D, D,
+                       1, 0, E.EPI_NONE, c_dtype=lib.F32)
+            self._bias_grad(self.dqkv, self.view(G, n("qkv_b")), 3 * D)
+            self._ln_bwd(self.d_ln, self.x[l], self.view(P, n("ln1_w")), st[0], st[1],
+                         self.view(G, n("ln1_w")), self.view(G, n("ln1_b")))
+        # embeddings: dwte += scatter(dresid); dwpe = sum over batch
+        self.view(G, "wpe").zero_()
+        if not cfg.tied:
+            self.view(G, "wte").zero_()
+        lib.call("magma_embedding_bwd", _p(self.tokens), _p(self.dresid), _p(self.view(G, "wte")),
+                 _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp, s)
+
+    def _dresid_operand(self) -> torch.Tensor:
+        """The residual gradient as a GEMM operand (BF16 copy in bf16 mode)."""
+        if self.dresid_a is None:
+            return self.dresid
+        lib.call("magma_convert", _p(self.dresid), _p(self.dresid_a), self.dresid.numel(),
+                 lib.F32, lib.BF16, self._s())
+        return self.dresid_a
+
+    # ---------------------------------------------------------------- Adam
+    def optimizer_step(self, grad_scale: float = 1.0) -> None:
+        """optim.Adam.step over the whole arena (Optimizer.swift:354-412)."""
+        self.t += 1
+        lib.call("magma_adam_step", _p(self.params), _p(self.grads), _p(self.m), _p(self.v),
+                 _p(self.shadow), self.P, self.lr, self.beta1, self.beta2, self.eps, self.wd,
+                 self.t, grad_scale, self._s())
+
+    # ------------------------------------------------------------- graphs
+    def capture(self) -> None:
+        """Records step_fwd_bwd as one CUDA graph (after one eager warm-up)."""
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.step_fwd_bwd()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step_fwd_bwd()
+        self.graph = g
+
+    def run_fwd_bwd(self) -> None:
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.step_fwd_bwd()
+
+    # --------------------------------------------------------- public step
+    def set_batch(self, tokens: torch.Tensor, targets: torch.Tensor) -> None:
+        self.tokens.copy_(tokens, non_blocking=True)
+        self.targets.copy_(targets, non_blocking=True)
+
+    def train_step(self, tokens: torch.Tensor, targets: torch.Tensor, allreduce=None) -> float:
+        """Host tokens/targets [B, S] in, host loss out: H2D, fwd+bwd, DP sync, Adam, D2H."""
+        self.set_batch(tokens, targets)
+        self.run_fwd_bwd()
+        scale = 1.0
+        if allreduce is not None:
+            scale = allreduce(self.grads)
+        self.optimizer_step(grad_scale=scale)
+        return float(self.loss.item())

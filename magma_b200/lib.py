@@ -114,6 +114,16 @@ SIGNATURES = {
     "magma_scale": (None, [_vp, _i64, _f, _vp]),
 }
 
+# Kernel launches one successful call of each op makes (for launch accounting).
+KERNELS_PER_CALL = {
+    "magma_layernorm_fwd": 1, "magma_layernorm_bwd": 2, "magma_gemm": 1,
+    "magma_attention_fwd": 1, "magma_attention_bwd": 3, "magma_adam_step": 1,
+    "magma_adam_step_multi": 1, "magma_embedding_fwd": 1, "magma_embedding_bwd": 2,
+    "magma_cross_entropy_fwd_bwd": 1, "magma_reduce_sum": 1, "magma_gelu_fwd": 1,
+    "magma_gelu_bwd": 1, "magma_relu_fwd": 1, "magma_relu_bwd": 1, "magma_bias_grad": 2,
+    "magma_convert": 1, "magma_scale": 1,
+}
+
 _lib = None
 _lock = threading.Lock()
 

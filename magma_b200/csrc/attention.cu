@@ -13,6 +13,16 @@ magma_status_t attention_bwd_simt(const void* q, const void* k, const void* v, c
                                   float* delta, int64_t batch, int64_t heads, int64_t seq,
                                   int64_t hd, const int64_t* qs, const int64_t* os, float scale,
                                   int causal, magma_dtype_t dtype, cudaStream_t s);
+bool attention_tc_supported(const void* q, const void* k, const void* v, const void* o,
+                            int64_t hd, const int64_t* qs, const int64_t* os,
+                            magma_dtype_t dtype, int64_t batch, int64_t heads, int64_t seq);
+magma_status_t attention_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse,
+                                int64_t B, int64_t H, int64_t S, const int64_t* qs,
+                                const int64_t* os, float scale, int causal, cudaStream_t s);
+magma_status_t attention_bwd_tc(const void* q, const void* k, const void* v, const void* o,
+                                const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                                float* delta, int64_t B, int64_t H, int64_t S, const int64_t* qs,
+                                const int64_t* os, float scale, int causal, cudaStream_t s);
 }  // namespace magma
 
 using namespace magma;
@@ -47,6 +57,10 @@ magma_status_t magma_attention_fwd(const void* q, const void* k, const void* v, 
     return st;
   if (batch == 0 || heads == 0 || seq == 0) return MAGMA_OK;
   MAGMA_REQUIRE(q && k && v && o, "magma_attention_fwd: NULL pointer");
+  if (attention_tc_supported(q, k, v, o, head_dim, qkv_strides, o_strides, dtype, batch, heads,
+                             seq))
+    return attention_fwd_tc(q, k, v, o, lse, batch, heads, seq, qkv_strides, o_strides, scale,
+                            causal, (cudaStream_t)stream);
   return attention_fwd_simt(q, k, v, o, lse, batch, heads, seq, head_dim, qkv_strides, o_strides,
                             scale, causal, dtype, (cudaStream_t)stream);
 }
@@ -75,6 +89,11 @@ magma_status_t magma_attention_bwd(const void* q, const void* k, const void* v, 
   MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= need,
                 "magma_attention_bwd: workspace of %zu bytes needed, %zu given", need,
                 workspace_bytes);
+  if (attention_tc_supported(q, k, v, o, head_dim, qkv_strides, o_strides, dtype, batch, heads,
+                             seq) &&
+      aligned16(d_o) && aligned16(dq) && aligned16(dk) && aligned16(dv))
+    return attention_bwd_tc(q, k, v, o, d_o, lse, dq, dk, dv, (float*)workspace, batch, heads, seq,
+                            qkv_strides, o_strides, scale, causal, (cudaStream_t)stream);
   return attention_bwd_simt(q, k, v, o, d_o, lse, dq, dk, dv, (float*)workspace, batch, heads, seq,
                             head_dim, qkv_strides, o_strides, scale, causal, dtype,
                             (cudaStream_t)stream);

@@ -471,6 +471,22 @@ magma_status_t bwd_simt(const void* q, const void* k, const void* v, const void*
 
 }  // namespace
 
+// delta[b,h,i] = sum_d dO*O for the backward kernels (F32 or BF16 inputs).
+magma_status_t attention_bwd_delta(const void* o, const void* d_o, float* delta, int64_t batch,
+                                   int64_t heads, int64_t seq, int64_t hd, const int64_t* os,
+                                   magma_dtype_t dtype, cudaStream_t s) {
+  AttnGeom g{batch, heads, seq, hd, {0, 0, 0}, {os[0], os[1], os[2]}, 0.f, 0};
+  const int64_t rows = batch * heads * seq;
+  int64_t blocks = ceil_div(rows, 8);
+  if (blocks > 16LL * num_sms()) blocks = 16LL * num_sms();
+  if (dtype == MAGMA_DTYPE_F32)
+    attn_bwd_delta<float><<<(int)blocks, 256, 0, s>>>((const float*)o, (const float*)d_o, delta, g);
+  else
+    attn_bwd_delta<__nv_bfloat16><<<(int)blocks, 256, 0, s>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)d_o, delta, g);
+  return check_launch("attention_bwd_delta");
+}
+
 // Entry points used by attention.cu's dispatcher.
 magma_status_t attention_fwd_simt(const void* q, const void* k, const void* v, void* o,
                                   float* lse, int64_t batch, int64_t heads, int64_t seq,

@@ -1,0 +1,808 @@
+// Causal attention on the tcgen05 tensor cores (BF16 in, F32 accumulate),
+// head_dim 64. Same math as the SIMT path (GPT block attention,
+// Benchmarks/GPT2Shakespeare/Sources/main.swift:467-481; VJP chain
+// Sources/Core/Autodiff.swift:309-317,379-386), tiled 128 x 128.
+//
+// Every kernel has the same six-warp shape:
+//   warps 0-3  row math: thread r owns TMEM lane r (one query or key row);
+//   warp 4     TMA producer (4-D tensor maps straight over the caller's strided
+//              [B, H, S, D] views: Q/K/V can be read in place from the fused
+//              QKV projection, no head transposes);
+//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer.
+// Score tiles and accumulators live in TMEM; P / dS are written by the row
+// threads as BF16 into 128-byte-swizzled shared memory (the K-major operand
+// layout TMA produces) and fed back to the tensor cores.
+//
+// Forward (one CTA per 128-query tile, heaviest causal tiles first):
+//   S_j = Q K_j^T (TMEM, double-buffered) -> online softmax in registers
+//   (exp2, running max/sum) -> P_j (smem, double-buffered) -> PV_j = P_j V_j
+//   (TMEM, double-buffered) folded into a register accumulator two tiles
+//   later with the matching rescale. The MMA warp issues S_{j+1} while the row
+//   threads work on S_j. Outputs O (BF16) and the row log-sum-exp.
+// Backward, deterministic (no atomics), two kernels after the delta pre-pass:
+//   dK/dV: one CTA per 128-key tile, loop over query tiles: S^T = K Q^T,
+//     dP^T = V dO^T, P^T = exp(S^T*scale - lse), dS^T = P^T (dP^T - delta),
+//     dV += P^T dO, dK += dS^T Q (TMEM accumulators).
+//   dQ: one CTA per 128-query tile, loop over key tiles: S, dP, dS as above,
+//     dQ += dS K.
+// All mbarrier waits are bounded (they set the device error word and the
+// kernel winds down instead of hanging).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace magma {
+magma_status_t attention_bwd_delta(const void* o, const void* d_o, float* delta, int64_t batch,
+                                   int64_t heads, int64_t seq, int64_t hd, const int64_t* os,
+                                   magma_dtype_t dtype, cudaStream_t s);
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kTile = 128;     // queries / keys per tile
+constexpr int kHd = 64;        // head dim
+constexpr int kThreads = 192;  // 4 row warps + producer + MMA
+constexpr int kTileBytes = kTile * kHd * 2;  // 16 KB: one [128 x 64] BF16 tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct AttnTcArgs {
+  int S, H, B;
+  float scale;
+  int causal;
+  void* o;         // fwd output / bwd: unused
+  float* lse;
+  const float* delta;
+  void* dq;        // dQ / dK / dV outputs (qkv strides)
+  void* dk;
+  void* dv;
+  int64_t os0, os1, os2;  // O strides (elements)
+  int64_t qs0, qs1, qs2;  // Q/K/V (and dQ/dK/dV) strides
+  int* err;
+};
+
+__device__ __forceinline__ uint64_t desc_k(uint32_t addr) { return smem_desc_sw128(addr, 16, 1024); }
+__device__ __forceinline__ uint64_t desc_mn(uint32_t addr) {
+  return smem_desc_sw128(addr, 8192, 1024);
+}
+
+// Address in a [128 rows x 128 cols] BF16 K-major SW128 operand (two 64-column
+// blocks of 16 KB) of the 16-byte chunk holding columns [8*chunk, 8*chunk+8)
+// of row r.
+__device__ __forceinline__ uint32_t swz_chunk_addr(uint32_t base, int r, int chunk) {
+  const int blk = chunk >> 3, c = chunk & 7;
+  return base + blk * 16384 + r * 128 + ((c ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Writes 32 F32 values as BF16 columns [32*c32, 32*c32+32) of row r.
+__device__ __forceinline__ void store_row32(uint32_t base, int r, int c32, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int chunk = c32 * 4 + q;
+    st_shared_v4(swz_chunk_addr(base, r, chunk), pack_bf16(v[q * 8 + 0], v[q * 8 + 1]),
+                 pack_bf16(v[q * 8 + 2], v[q * 8 + 3]), pack_bf16(v[q * 8 + 4], v[q * 8 + 5]),
+                 pack_bf16(v[q * 8 + 6], v[q * 8 + 7]));
+  }
+}
+
+// Stores 64 F32 values * mul as one BF16 row of 128 bytes.
+__device__ __forceinline__ void store_global_row64(__nv_bfloat16* dst, const float* v, float mul) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint4 u;
+    u.x = pack_bf16(v[q * 8 + 0] * mul, v[q * 8 + 1] * mul);
+    u.y = pack_bf16(v[q * 8 + 2] * mul, v[q * 8 + 3] * mul);
+    u.z = pack_bf16(v[q * 8 + 4] * mul, v[q * 8 + 5] * mul);
+    u.w = pack_bf16(v[q * 8 + 6] * mul, v[q * 8 + 7] * mul);
+    reinterpret_cast<uint4*>(dst)[q] = u;
+  }
+}
+
+__device__ __forceinline__ uint32_t align1024(uint8_t* raw, uint8_t** aligned_ptr) {
+  const uint32_t a = smem_u32(raw);
+  const uint32_t base = (a + 1023u) & ~1023u;
+  *aligned_ptr = raw + (base - a);
+  return base;
+}
+
+// =============================================================== forward
+constexpr int kFwdKvStages = 3;
+constexpr int kFwdQ = 0;
+constexpr int kFwdKv = kFwdQ + kTileBytes;                          // K,V per stage
+constexpr int kFwdP = kFwdKv + kFwdKvStages * 2 * kTileBytes;      // 2 x 32 KB
+constexpr int kFwdBar = kFwdP + 2 * 2 * kTileBytes;
+// q_full, kv_full[3], kv_empty[3], s_full[2], s_empty[2], p_full[2], pv_done[2], done
+constexpr int kFwdNumBars = 16;
+constexpr int kFwdSmem = kFwdBar + kFwdNumBars * 8 + 16 + 1024;
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+            const __grid_constant__ CUtensorMap tmV, AttnTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sp;
+  const uint32_t base = align1024(smem_raw, &sp);
+  const uint32_t sQ = base + kFwdQ;
+  auto sK = [&](int st) { return base + kFwdKv + st * 2 * kTileBytes; };
+  auto sV = [&](int st) { return base + kFwdKv + st * 2 * kTileBytes + kTileBytes; };
+  auto sP = [&](int b) { return base + kFwdP + b * 2 * kTileBytes; };
+  const uint32_t bars = base + kFwdBar;
+  const uint32_t q_full = bars;
+  auto kv_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (4 + s); };
+  auto s_full = [&](int b) { return bars + 8u * (7 + b); };
+  auto s_empty = [&](int b) { return bars + 8u * (9 + b); };
+  auto p_full = [&](int b) { return bars + 8u * (11 + b); };
+  auto pv_done = [&](int b) { return bars + 8u * (13 + b); };
+  const uint32_t done_bar = bars + 8u * 15;
+  const uint32_t tslot = bars + 8u * kFwdNumBars;
+  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kFwdBar + 8 * kFwdNumBars);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (a.S + kTile - 1) / kTile;
+  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * kTile;
+  const int n_kv = a.causal ? qt + 1 : n_qt;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kFwdKvStages; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(s_empty(i), 4);
+      mbar_init(p_full(i), 4);
+      mbar_init(pv_done(i), 1);
+    }
+    mbar_init(done_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
+  const uint32_t tS = tmem;          // S buffers at columns 0, 128
+  const uint32_t tO = tmem + 256;    // PV partial buffers at columns 256, 320
+
+  if (warp == 4) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_expect_tx(q_full, kTileBytes);
+      tma_load_4d(sQ, &tmQ, 0, q0, h, b, q_full);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % kFwdKvStages;
+        const uint32_t ph = (uint32_t)((j / kFwdKvStages) & 1);
+        if (!mbar_wait(kv_empty(st), ph ^ 1u, a.err)) { ok = false; break; }
+        mbar_expect_tx(kv_full(st), 2 * kTileBytes);
+        tma_load_4d(sK(st), &tmK, 0, j * kTile, h, b, kv_full(st));
+        tma_load_4d(sV(st), &tmV, 0, j * kTile, h, b, kv_full(st));
+      }
+      // every stage issued above has been consumed before the producer leaves
+      for (int j = n_kv; j < n_kv + kFwdKvStages && ok; ++j) {
+        const int st = j % kFwdKvStages;
+        const uint32_t ph = (uint32_t)((j / kFwdKvStages) & 1);
+        if (!mbar_wait(kv_empty(st), ph ^ 1u, a.err)) ok = false;
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
+      constexpr uint32_t idPV = idesc_bf16_f32(kTile, kHd, 0, 1);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_pv = [&](int i) -> bool {
+        const int pb = i & 1, st = i % kFwdKvStages;
+        if (!mbar_wait(p_full(pb), (uint32_t)((i >> 1) & 1), a.err)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint64_t ad = desc_k(sP(pb) + (kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t bd = desc_mn(sV(st) + kk * 2048);
+          mma_bf16_ss(tO + pb * kHd, ad, bd, idPV, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(pv_done(pb));
+        mma_commit(kv_empty(st));
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % kFwdKvStages, sb = j & 1;
+        if (!mbar_wait(kv_full(st), (uint32_t)((j / kFwdKvStages) & 1), a.err)) { ok = false; break; }
+        if (!mbar_wait(s_empty(sb), (uint32_t)(((j >> 1) & 1) ^ 1), a.err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk)
+          mma_bf16_ss(tS + sb * kTile, desc_k(sQ + kk * 32), desc_k(sK(st) + kk * 32), idS,
+                      kk > 0 ? 1u : 0u);
+        mma_commit(s_full(sb));
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && n_kv >= 1) issue_pv(n_kv - 1);
+      mma_commit(done_bar);
+      mbar_wait(done_bar, 0, a.err);
+    }
+  } else {
+    // ------------------------------ row threads ------------------------------
+    const int r = warp * 32 + lane;
+    const int qg = q0 + r;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float sl2 = a.scale * kLog2e;
+    float m_run = -INFINITY, l_run = 0.f;
+    float o[kHd];
+#pragma unroll
+    for (int i = 0; i < kHd; ++i) o[i] = 0.f;
+    float ring0 = 0.f, ring1 = 0.f;  // rescale factor pending for PV buffer 0 / 1
+    bool ok = true;
+    auto absorb = [&](int i) -> bool {
+      const int pb = i & 1;
+      if (!mbar_wait(pv_done(pb), (uint32_t)((i >> 1) & 1), a.err)) return false;
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tO + pb * kHd + lane_off, v0);
+      tmem_ld32(tO + pb * kHd + 32 + lane_off, v1);
+      tmem_wait_ld();
+      const float al = pb ? ring1 : ring0;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        o[c] = o[c] * al + __uint_as_float(v0[c]);
+        o[32 + c] = o[32 + c] * al + __uint_as_float(v1[c]);
+      }
+      return true;
+    };
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(s_full(sb), (uint32_t)((j >> 1) & 1), a.err)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t srow = tS + sb * kTile + lane_off;
+      const int k0 = j * kTile;
+      const bool diag = a.causal && (k0 + kTile > q0);
+      const bool tail = k0 + kTile > a.S;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(srow + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kg = k0 + c * 32 + e;
+          const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
+          if (!masked) mx = fmaxf(mx, __uint_as_float(v[e]));
+        }
+      }
+      const float m_new = fmaxf(m_run, mx * sl2);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = ex2_approx(m_run - m_use);
+      if (j >= 2 && !absorb(j - 2)) { ok = false; break; }
+      if (sb) ring1 = alpha; else ring0 = alpha;
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(srow + c * 32, v);
+        tmem_wait_ld();
+        float p[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kg = k0 + c * 32 + e;
+          const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
+          p[e] = masked ? 0.f : ex2_approx(__uint_as_float(v[e]) * sl2 - m_use);
+          rs += p[e];
+        }
+        store_row32(sP(sb), r, c, p);
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_use;
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_empty(sb));
+        mbar_arrive(p_full(sb));
+      }
+    }
+    if (ok) {
+      for (int i = (n_kv >= 2 ? n_kv - 2 : 0); i < n_kv && ok; ++i) ok = absorb(i);
+    }
+    if (ok && qg < a.S) {
+      const float inv = 1.0f / l_run;
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.o) + (int64_t)b * a.os0 +
+                           (int64_t)h * a.os1 + (int64_t)qg * a.os2;
+      store_global_row64(dst, o, inv);
+      if (a.lse != nullptr) a.lse[((int64_t)b * a.H + h) * a.S + qg] = m_run * kLn2 + logf(l_run);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ========================================================== backward dK/dV
+constexpr int kKvK = 0;
+constexpr int kKvV = kTileBytes;
+constexpr int kKvQdo = 2 * kTileBytes;                       // 2 stages x (Q, dO)
+constexpr int kKvPT = kKvQdo + 2 * 2 * kTileBytes;           // 32 KB
+constexpr int kKvDST = kKvPT + 2 * kTileBytes;               // 32 KB
+constexpr int kKvStats = kKvDST + 2 * kTileBytes;            // lse[2][128], delta[2][128]
+constexpr int kKvBar = kKvStats + 4 * kTile * 4;
+// kv_full, qdo_full[2], qdo_empty[2], st_full, pds_full, final
+constexpr int kKvNumBars = 8;
+constexpr int kKvSmem = kKvBar + kKvNumBars * 8 + 16 + 1024;
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                 AttnTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sp;
+  const uint32_t base = align1024(smem_raw, &sp);
+  const uint32_t sK = base + kKvK, sV = base + kKvV;
+  auto sQ = [&](int st) { return base + kKvQdo + st * 2 * kTileBytes; };
+  auto sdO = [&](int st) { return base + kKvQdo + st * 2 * kTileBytes + kTileBytes; };
+  const uint32_t sPT = base + kKvPT, sDST = base + kKvDST;
+  float* lse_s = reinterpret_cast<float*>(sp + kKvStats);           // [2][128]
+  float* delta_s = reinterpret_cast<float*>(sp + kKvStats + 2 * kTile * 4);
+  const uint32_t bars = base + kKvBar;
+  const uint32_t kv_full = bars;
+  auto qdo_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto qdo_empty = [&](int s) { return bars + 8u * (3 + s); };
+  const uint32_t st_full = bars + 8u * 5;
+  const uint32_t pds_full = bars + 8u * 6;
+  const uint32_t final_bar = bars + 8u * 7;
+  const uint32_t tslot = bars + 8u * kKvNumBars;
+  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kKvBar + 8 * kKvNumBars);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_t = (a.S + kTile - 1) / kTile;
+  const int kt = (int)blockIdx.x;  // tile 0 has the most query tiles under causal
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int k0 = kt * kTile;
+  const int first_q = a.causal ? kt : 0;
+  const int n_it = n_t - first_q;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmdO);
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(qdo_full(s), 1);
+      mbar_init(qdo_empty(s), 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(pds_full, 4);
+    mbar_init(final_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
+  const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_expect_tx(kv_full, 2 * kTileBytes);
+      tma_load_4d(sK, &tmK, 0, k0, h, b, kv_full);
+      tma_load_4d(sV, &tmV, 0, k0, h, b, kv_full);
+      for (int i = 0; i < n_it && ok; ++i) {
+        const int st = i & 1;
+        const int q0 = (first_q + i) * kTile;
+        if (!mbar_wait(qdo_empty(st), (uint32_t)(((i >> 1) & 1) ^ 1), a.err)) { ok = false; break; }
+        mbar_expect_tx(qdo_full(st), 2 * kTileBytes);
+        tma_load_4d(sQ(st), &tmQ, 0, q0, h, b, qdo_full(st));
+        tma_load_4d(sdO(st), &tmdO, 0, q0, h, b, qdo_full(st));
+      }
+      for (int i = n_it; i < n_it + 2 && ok; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(qdo_empty(st), (uint32_t)(((i >> 1) & 1) ^ 1), a.err)) ok = false;
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
+      constexpr uint32_t idG = idesc_bf16_f32(kTile, kHd, 0, 1);
+      bool ok = mbar_wait(kv_full, 0, a.err);
+      auto issue_grad = [&](int i) -> bool {
+        const int st = i & 1;
+        if (!mbar_wait(pds_full, (uint32_t)(i & 1), a.err)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_bf16_ss(tDV, desc_k(sPT + aoff), desc_mn(sdO(st) + kk * 2048), idG,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tDK, desc_k(sDST + aoff), desc_mn(sQ(st) + kk * 2048), idG,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(qdo_empty(st));
+        return true;
+      };
+      for (int i = 0; i < n_it && ok; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(qdo_full(st), (uint32_t)((i >> 1) & 1), a.err)) { ok = false; break; }
+        tc_fence_after();
+        if (i > 0 && !issue_grad(i - 1)) { ok = false; break; }
+#pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          mma_bf16_ss(tST, desc_k(sK + kk * 32), desc_k(sQ(st) + kk * 32), idS, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tDPT, desc_k(sV + kk * 32), desc_k(sdO(st) + kk * 32), idS,
+                      kk > 0 ? 1u : 0u);
+        }
+        mma_commit(st_full);
+      }
+      if (ok && n_it >= 1) issue_grad(n_it - 1);
+      mma_commit(final_bar);
+      mbar_wait(final_bar, 0, a.err);
+    }
+  } else {
+    // row threads: r = key row
+    const int r = warp * 32 + lane;
+    const int kg = k0 + r;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float sl2 = a.scale * kLog2e;
+    const int64_t bh = (int64_t)b * a.H + h;
+    bool ok = true;
+    for (int i = 0; i < n_it; ++i) {
+      const int st = i & 1;
+      const int q0 = (first_q + i) * kTile;
+      {
+        const int qi = q0 + r;
+        lse_s[st * kTile + r] = qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
+        delta_s[st * kTile + r] = qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
+      }
+      named_barrier(1, 128);
+      if (!mbar_wait(st_full, (uint32_t)(i & 1), a.err)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = a.causal && (q0 < k0 + kTile);
+      const bool tail = q0 + kTile > a.S || kg >= a.S;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t vs[32], vd[32];
+        tmem_ld32(tST + lane_off + c * 32, vs);
+        tmem_ld32(tDPT + lane_off + c * 32, vd);
+        tmem_wait_ld();
+        float p[32], ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int ql = c * 32 + e;
+          const int qg = q0 + ql;
+          const bool masked = (diag && qg < kg) || (tail && (qg >= a.S || kg >= a.S));
+          const float pe =
+              masked ? 0.f : ex2_approx(__uint_as_float(vs[e]) * sl2 - lse_s[st * kTile + ql]);
+          p[e] = pe;
+          ds[e] = pe * (__uint_as_float(vd[e]) - delta_s[st * kTile + ql]);
+        }
+        store_row32(sPT, r, c, p);
+        store_row32(sDST, r, c, ds);
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_full);
+    }
+    if (ok && mbar_wait(final_bar, 0, a.err)) {
+      tc_fence_after();
+      float acc[kHd];
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tDV + lane_off, v0);
+      tmem_ld32(tDV + lane_off + 32, v1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        acc[c] = __uint_as_float(v0[c]);
+        acc[32 + c] = __uint_as_float(v1[c]);
+      }
+      const int64_t off = (int64_t)b * a.qs0 + (int64_t)h * a.qs1 + (int64_t)kg * a.qs2;
+      if (kg < a.S) store_global_row64(static_cast<__nv_bfloat16*>(a.dv) + off, acc, 1.f);
+      tmem_ld32(tDK + lane_off, v0);
+      tmem_ld32(tDK + lane_off + 32, v1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        acc[c] = __uint_as_float(v0[c]);
+        acc[32 + c] = __uint_as_float(v1[c]);
+      }
+      if (kg < a.S) store_global_row64(static_cast<__nv_bfloat16*>(a.dk) + off, acc, a.scale);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================= backward dQ
+constexpr int kDqQ = 0;
+constexpr int kDqDo = kTileBytes;
+constexpr int kDqKv = 2 * kTileBytes;                    // 2 stages x (K, V)
+constexpr int kDqDs = kDqKv + 2 * 2 * kTileBytes;        // 32 KB
+constexpr int kDqBar = kDqDs + 2 * kTileBytes;
+// q_full, kv_full[2], kv_empty[2], s_full, ds_full, final
+constexpr int kDqNumBars = 8;
+constexpr int kDqSmem = kDqBar + kDqNumBars * 8 + 16 + 1024;
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+               AttnTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sp;
+  const uint32_t base = align1024(smem_raw, &sp);
+  const uint32_t sQ = base + kDqQ, sdO = base + kDqDo;
+  auto sK = [&](int st) { return base + kDqKv + st * 2 * kTileBytes; };
+  auto sV = [&](int st) { return base + kDqKv + st * 2 * kTileBytes + kTileBytes; };
+  const uint32_t sDS = base + kDqDs;
+  const uint32_t bars = base + kDqBar;
+  const uint32_t q_full = bars;
+  auto kv_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (3 + s); };
+  const uint32_t s_full = bars + 8u * 5;
+  const uint32_t ds_full = bars + 8u * 6;
+  const uint32_t final_bar = bars + 8u * 7;
+  const uint32_t tslot = bars + 8u * kDqNumBars;
+  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kDqBar + 8 * kDqNumBars);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_t = (a.S + kTile - 1) / kTile;
+  const int qt = n_t - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * kTile;
+  const int n_kv = a.causal ? qt + 1 : n_t;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmdO);
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(ds_full, 4);
+    mbar_init(final_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
+  const uint32_t tS = tmem, tDP = tmem + 128, tDQ = tmem + 256;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_expect_tx(q_full, 2 * kTileBytes);
+      tma_load_4d(sQ, &tmQ, 0, q0, h, b, q_full);
+      tma_load_4d(sdO, &tmdO, 0, q0, h, b, q_full);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty(st), (uint32_t)(((j >> 1) & 1) ^ 1), a.err)) { ok = false; break; }
+        mbar_expect_tx(kv_full(st), 2 * kTileBytes);
+        tma_load_4d(sK(st), &tmK, 0, j * kTile, h, b, kv_full(st));
+        tma_load_4d(sV(st), &tmV, 0, j * kTile, h, b, kv_full(st));
+      }
+      for (int j = n_kv; j < n_kv + 2 && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty(st), (uint32_t)(((j >> 1) & 1) ^ 1), a.err)) ok = false;
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
+      constexpr uint32_t idG = idesc_bf16_f32(kTile, kHd, 0, 1);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_dq = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(ds_full, (uint32_t)(j & 1), a.err)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_bf16_ss(tDQ, desc_k(sDS + (kk >> 2) * 16384 + (kk & 3) * 32),
+                      desc_mn(sK(st) + kk * 2048), idG, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(kv_empty(st));
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_full(st), (uint32_t)((j >> 1) & 1), a.err)) { ok = false; break; }
+        tc_fence_after();
+        if (j > 0 && !issue_dq(j - 1)) { ok = false; break; }
+#pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          mma_bf16_ss(tS, desc_k(sQ + kk * 32), desc_k(sK(st) + kk * 32), idS, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tDP, desc_k(sdO + kk * 32), desc_k(sV(st) + kk * 32), idS,
+                      kk > 0 ? 1u : 0u);
+        }
+        mma_commit(s_full);
+      }
+      if (ok && n_kv >= 1) issue_dq(n_kv - 1);
+      mma_commit(final_bar);
+      mbar_wait(final_bar, 0, a.err);
+    }
+  } else {
+    const int r = warp * 32 + lane;
+    const int qg = q0 + r;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float sl2 = a.scale * kLog2e;
+    const int64_t bh = (int64_t)b * a.H + h;
+    const float lse2 = qg < a.S ? a.lse[bh * a.S + qg] * kLog2e : INFINITY;
+    const float dl = qg < a.S ? a.delta[bh * a.S + qg] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int k0 = j * kTile;
+      if (!mbar_wait(s_full, (uint32_t)(j & 1), a.err)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = a.causal && (k0 + kTile > q0);
+      const bool tail = k0 + kTile > a.S;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t vs[32], vd[32];
+        tmem_ld32(tS + lane_off + c * 32, vs);
+        tmem_ld32(tDP + lane_off + c * 32, vd);
+        tmem_wait_ld();
+        float ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kg = k0 + c * 32 + e;
+          const bool masked = (diag && kg > qg) || (tail && kg >= a.S) || qg >= a.S;
+          const float pe = masked ? 0.f : ex2_approx(__uint_as_float(vs[e]) * sl2 - lse2);
+          ds[e] = pe * (__uint_as_float(vd[e]) - dl);
+        }
+        store_row32(sDS, r, c, ds);
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    if (ok && mbar_wait(final_bar, 0, a.err)) {
+      tc_fence_after();
+      float acc[kHd];
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tDQ + lane_off, v0);
+      tmem_ld32(tDQ + lane_off + 32, v1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        acc[c] = __uint_as_float(v0[c]);
+        acc[32 + c] = __uint_as_float(v1[c]);
+      }
+      if (qg < a.S)
+        store_global_row64(static_cast<__nv_bfloat16*>(a.dq) + (int64_t)b * a.qs0 +
+                               (int64_t)h * a.qs1 + (int64_t)qg * a.qs2,
+                           acc, a.scale);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// 4-D tensor map over a [B, H, S, 64] BF16 view with element strides
+// (sb, sh, ss), box [128 rows x 64] with 128-byte swizzle.
+magma_status_t head_map(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t S,
+                        int64_t sb, int64_t sh, int64_t ss) {
+  const uint64_t dims[4] = {(uint64_t)kHd, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)ss * 2, (uint64_t)sh * 2, (uint64_t)sb * 2};
+  const uint32_t box[4] = {(uint32_t)kHd, (uint32_t)kTile, 1, 1};
+  return encode_tensor_map_nd(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, 4, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Opts kernel `ID` into `bytes` of dynamic shared memory once per device
+// (the cache is keyed by ID: the kernels share one function type).
+template <int ID, typename K>
+magma_status_t set_smem_attr(K kern, int bytes) {
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return MAGMA_OK;
+  if (magma_status_t s = cuda_status(
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+          "cudaFuncSetAttribute(attention_tc)"))
+    return s;
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return MAGMA_OK;
+}
+
+bool strides_ok(const int64_t* s) {
+  for (int i = 0; i < 3; ++i)
+    if ((s[i] * 2) % 16 != 0) return false;
+  return true;
+}
+
+}  // namespace
+
+// True if the tcgen05 kernels can take this problem (BF16, head_dim 64, TMA-
+// compatible strides and 16-byte aligned bases).
+bool attention_tc_supported(const void* q, const void* k, const void* v, const void* o,
+                            int64_t hd, const int64_t* qs, const int64_t* os,
+                            magma_dtype_t dtype, int64_t batch, int64_t heads, int64_t seq) {
+  return dtype == MAGMA_DTYPE_BF16 && hd == kHd && aligned16(q) && aligned16(k) && aligned16(v) &&
+         aligned16(o) && strides_ok(qs) && strides_ok(os) && batch < 65536 && heads < 65536 &&
+         seq < (1LL << 30);
+}
+
+magma_status_t attention_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse,
+                                int64_t B, int64_t H, int64_t S, const int64_t* qs,
+                                const int64_t* os, float scale, int causal, cudaStream_t s) {
+  CUtensorMap mq, mk, mv;
+  if (magma_status_t st = head_map(&mq, q, B, H, S, qs[0], qs[1], qs[2])) return st;
+  if (magma_status_t st = head_map(&mk, k, B, H, S, qs[0], qs[1], qs[2])) return st;
+  if (magma_status_t st = head_map(&mv, v, B, H, S, qs[0], qs[1], qs[2])) return st;
+  AttnTcArgs a{};
+  a.S = (int)S; a.H = (int)H; a.B = (int)B; a.scale = scale; a.causal = causal;
+  a.o = o; a.lse = lse;
+  a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
+  a.qs0 = qs[0]; a.qs1 = qs[1]; a.qs2 = qs[2];
+  a.err = device_error_word();
+  if (magma_status_t st = set_smem_attr<0>(attn_fwd_tc, kFwdSmem)) return st;
+  dim3 grid((unsigned)ceil_div(S, kTile), (unsigned)H, (unsigned)B);
+  attn_fwd_tc<<<grid, kThreads, kFwdSmem, s>>>(mq, mk, mv, a);
+  return check_launch("attention_fwd_tcgen05");
+}
+
+magma_status_t attention_bwd_tc(const void* q, const void* k, const void* v, const void* o,
+                                const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                                float* delta, int64_t B, int64_t H, int64_t S, const int64_t* qs,
+                                const int64_t* os, float scale, int causal, cudaStream_t s) {
+  if (magma_status_t st = attention_bwd_delta(o, d_o, delta, B, H, S, kHd, os, MAGMA_DTYPE_BF16, s))
+    return st;
+  CUtensorMap mq, mk, mv, mdo;
+  if (magma_status_t st = head_map(&mq, q, B, H, S, qs[0], qs[1], qs[2])) return st;
+  if (magma_status_t st = head_map(&mk, k, B, H, S, qs[0], qs[1], qs[2])) return st;
+  if (magma_status_t st = head_map(&mv, v, B, H, S, qs[0], qs[1], qs[2])) return st;
+  if (magma_status_t st = head_map(&mdo, d_o, B, H, S, os[0], os[1], os[2])) return st;
+  AttnTcArgs a{};
+  a.S = (int)S; a.H = (int)H; a.B = (int)B; a.scale = scale; a.causal = causal;
+  a.lse = const_cast<float*>(lse); a.delta = delta;
+  a.dq = dq; a.dk = dk; a.dv = dv;
+  a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
+  a.qs0 = qs[0]; a.qs1 = qs[1]; a.qs2 = qs[2];
+  a.err = device_error_word();
+  if (magma_status_t st = set_smem_attr<1>(attn_bwd_dkdv_tc, kKvSmem)) return st;
+  if (magma_status_t st = set_smem_attr<2>(attn_bwd_dq_tc, kDqSmem)) return st;
+  dim3 grid((unsigned)ceil_div(S, kTile), (unsigned)H, (unsigned)B);
+  attn_bwd_dkdv_tc<<<grid, kThreads, kKvSmem, s>>>(mq, mk, mv, mdo, a);
+  if (magma_status_t st = check_launch("attention_bwd_dkdv_tcgen05")) return st;
+  attn_bwd_dq_tc<<<grid, kThreads, kDqSmem, s>>>(mq, mk, mv, mdo, a);
+  return check_launch("attention_bwd_dq_tcgen05");
+}
+
+}  // namespace magma

@@ -145,6 +145,36 @@ __device__ __forceinline__ float gelu_grad_f(float x) {
   return __fadd_rn(left, right);
 }
 
+// Hardware tanh approximation (max relative error ~2^-11): used where the
+// result is rounded to BF16 anyway.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// GELU / GELU' with the hardware tanh, same op order as gelu_f / gelu_grad_f.
+__device__ __forceinline__ float gelu_fast(float x) {
+  float inner = x + 0.044715f * (x * (x * x));
+  float t = tanh_approx(0.7978845608f * inner);
+  return 0.5f * (x * (1.0f + t));
+}
+__device__ __forceinline__ float gelu_grad_fast(float x) {
+  const float c = 0.7978845608f, a = 0.044715f;
+  float x2 = x * x;
+  float t = tanh_approx(c * (x + a * (x2 * x)));
+  float up = c * (1.0f + (3.0f * a) * x2);
+  return 0.5f * (1.0f + t) + ((0.5f * x) * (1.0f - t * t)) * up;
+}
+
+// GELU variants by output precision: the accurate form for F32 outputs, the
+// hardware-tanh form when the result is stored as BF16.
+template <typename T> __device__ __forceinline__ float gelu_t(float x) { return gelu_f(x); }
+template <> __device__ __forceinline__ float gelu_t<__nv_bfloat16>(float x) { return gelu_fast(x); }
+template <typename T> __device__ __forceinline__ float gelu_grad_t(float x) { return gelu_grad_f(x); }
+template <> __device__ __forceinline__ float gelu_grad_t<__nv_bfloat16>(float x) {
+  return gelu_grad_fast(x);
+}
+
 }  // namespace magma
 
 // Argument-check helper used at the top of every entry point.

@@ -52,14 +52,14 @@ __device__ __forceinline__ float epi_value(const EpiArgs& e, const TC* C, int64_
     case MAGMA_EPI_BIAS_GELU: {
       float pre = e.bias ? __fadd_rn(acc, e.bias[col]) : acc;
       static_cast<TC*>(e.aux_out)[off] = from_f32<TC>(pre);
-      return gelu_f(pre);
+      return gelu_t<TC>(pre);
     }
     case MAGMA_EPI_BIAS_RESIDUAL: {
       float t = e.bias ? __fadd_rn(acc, e.bias[col]) : acc;
       return __fadd_rn(static_cast<const float*>(e.aux_in)[off], t);
     }
     case MAGMA_EPI_DGELU:
-      return __fmul_rn(acc, gelu_grad_f(to_f32(static_cast<const TC*>(e.aux_in)[off])));
+      return __fmul_rn(acc, gelu_grad_t<TC>(to_f32(static_cast<const TC*>(e.aux_in)[off])));
     case MAGMA_EPI_ACCUMULATE:
       return __fadd_rn(to_f32(C[off]), acc);
     case MAGMA_EPI_BIAS_RELU: {
@@ -184,6 +184,13 @@ struct TcArgs {
   EpiArgs e;
   int* err;
   int vec_ok;  // C/aux pointers 16-B aligned and ldc % 8 == 0: 8-wide vector stores
+  // Split-K: work unit u covers output tile (u % tiles) over k-blocks
+  // [s*kb_per_split, (s+1)*kb_per_split) with s = u / tiles. With splits > 1
+  // the raw F32 accumulator goes to ws + s*M*N (leading dimension N) and a
+  // second kernel applies the epilogue to the sum over s.
+  int splits;
+  int kb_per_split;
+  float* ws;
 };
 
 // Stores 8 consecutive columns (col .. col+7) of one row with the epilogue.
@@ -215,7 +222,7 @@ __device__ __forceinline__ void epi_store8(const TcArgs& a, int64_t row, int64_t
         store8(static_cast<TC*>(a.e.aux_out) + off, pre);
         if (epi == MAGMA_EPI_BIAS_GELU) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] = gelu_f(pre[i]);
+          for (int i = 0; i < 8; ++i) o[i] = gelu_t<TC>(pre[i]);
         } else {
 #pragma unroll
           for (int i = 0; i < 8; ++i) o[i] = fmaxf(pre[i], 0.f);
@@ -226,7 +233,7 @@ __device__ __forceinline__ void epi_store8(const TcArgs& a, int64_t row, int64_t
       load8(static_cast<const TC*>(a.e.aux_in) + off, x);
       if (epi == MAGMA_EPI_DGELU) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[i], gelu_grad_f(x[i]));
+        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[i], gelu_grad_t<TC>(x[i]));
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = x[i] > 0.f ? v[i] : 0.f;
@@ -272,6 +279,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int tiles_m = (int)((M + kBM - 1) / kBM);
   const int tiles_n = (int)((N + BN - 1) / BN);
   const int num_tiles = tiles_m * tiles_n;
+  const int num_units = num_tiles * args.splits;
   const int kblocks = (int)((K + kBK - 1) / kBK);
 
   if (threadIdx.x == 0) {
@@ -299,10 +307,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+      const int tile = unit % num_tiles, split = unit / num_tiles;
       const int m0 = (tile % tiles_m) * kBM;
       const int n0 = (tile / tiles_m) * BN;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      const int kb0 = split * args.kb_per_split;
+      const int kb1 = min(kblocks, kb0 + args.kb_per_split);
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!sm100::mbar_wait(empty_bar(stage), phase ^ 1u, args.err)) { ok = false; break; }
         const uint32_t sa = base + stage * Cfg::kStageBytes;
         const uint32_t sb = sa + Cfg::kABytes;
@@ -338,11 +349,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+      const int split = unit / num_tiles;
+      const int kb0 = split * args.kb_per_split;
+      const int kb1 = min(kblocks, kb0 + args.kb_per_split);
       if (!sm100::mbar_wait(tempty_bar(acc), acc_phase ^ 1u, args.err)) { ok = false; break; }
       sm100::tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!sm100::mbar_wait(full_bar(stage), phase, args.err)) { ok = false; break; }
         sm100::tc_fence_after();
         const uint32_t sa = base + stage * Cfg::kStageBytes;
@@ -357,7 +371,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint64_t bdesc =
               B_MN ? sm100::smem_desc_sw128(sb + kk * 2048, 8192, 1024)
                    : sm100::smem_desc_sw128(sb + kk * 32, 16, 1024);
-          sm100::mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          sm100::mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
         }
         sm100::mma_commit(empty_bar(stage));
         if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -374,9 +388,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // ------------------------------ epilogue ------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const bool vec_ok = args.vec_ok != 0;
+    const bool ws_vec = (N % 8) == 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+      const int tile = unit % num_tiles, split = unit / num_tiles;
       const int m0 = (tile % tiles_m) * kBM;
       const int n0 = (tile / tiles_m) * BN;
       if (!sm100::mbar_wait(tfull_bar(acc), acc_phase, args.err)) break;
@@ -395,7 +411,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[g * 8 + i]);
             const int64_t col = (int64_t)n0 + c0 + g * 8;
-            if (col < N) epi_store8<TC>(args, row, col, v, vec_ok);
+            if (col >= N) continue;
+            if (args.splits > 1) {
+              float* dst = args.ws + (int64_t)split * M * N + row * N + col;
+              if (ws_vec && col + 8 <= N) {
+                store8(dst, v);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  if (col + i < N) dst[i] = v[i];
+              }
+            } else {
+              epi_store8<TC>(args, row, col, v, vec_ok);
+            }
           }
         }
       }
@@ -415,9 +443,64 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
+struct TcPlan {
+  int bn;
+  int splits;
+  int kb_per_split;
+};
+
+// Picks the tile width BN and the K-split count from a cost model: the time of
+// a persistent launch is (waves over the SMs) x (k-blocks per unit) x (cost
+// of one k-block: BN=128 is ~15% less efficient per FLOP than BN=256), plus,
+// when splitting, the HBM time to write and re-read the F32 partials.
+TcPlan choose_plan(int64_t M, int64_t N, int64_t K) {
+  const int sms = num_sms();
+  const int kblocks = (int)ceil_div(K, kBK);
+  const double kb_us[2] = {0.27 * 0.5 * 1.15, 0.27};  // BN=128, BN=256 (one k-block)
+  TcPlan best{256, 1, kblocks};
+  double best_t = 1e30;
+  for (int bi = 1; bi >= 0; --bi) {
+    const int bn = bi ? 256 : 128;
+    const int64_t tiles = ceil_div(M, kBM) * ceil_div(N, bn);
+    for (int s = 1; s <= 16; ++s) {
+      const int kbps = (int)ceil_div(kblocks, s);
+      if (s > 1 && kbps < 4) break;
+      const int splits = (int)ceil_div(kblocks, kbps);
+      if (splits != s) continue;
+      const int64_t units = tiles * splits;
+      const double waves = (double)ceil_div(units, sms);
+      double t = waves * kbps * kb_us[bi] + 2.0;
+      if (splits > 1) t += (double)(splits + 1) * M * N * 4.0 / 5.0e6;  // bytes / (5 TB/s) in us
+      if (t < best_t * 0.97) {
+        best_t = t;
+        best = {bn, splits, kbps};
+      }
+    }
+  }
+  return best;
+}
+
+// c = epilogue(sum over splits of ws[s]) in split order (deterministic).
+template <typename TC>
+__global__ void __launch_bounds__(256)
+splitk_reduce(const float* __restrict__ ws, int splits, int64_t M, int64_t N, TC* __restrict__ C,
+              EpiArgs e) {
+  const int64_t total = M * N;
+  const int64_t plane = total;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = ws[i];
+    for (int s = 1; s < splits; ++s) acc += ws[(int64_t)s * plane + i];
+    const int64_t row = i / N, col = i - row * N;
+    const int64_t off = row * e.ldc + col;
+    C[off] = from_f32<TC>(epi_value<TC>(e, C, off, col, acc));
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, typename TC>
 magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                          int64_t lda, int64_t ldb, const TcArgs& args, cudaStream_t stream) {
+  static_assert(BN == 128 || BN == 256, "BN");
   using Cfg = TcCfg<BN>;
   CUtensorMap ta, tb;
   magma_status_t st;
@@ -446,11 +529,19 @@ magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int
       return s2;
     attr_set[dev] = true;
   }
-  const int64_t tiles = ceil_div(M, kBM) * ceil_div(N, BN);
+  const int64_t units = ceil_div(M, kBM) * ceil_div(N, BN) * args.splits;
   int grid = num_sms();
-  if (tiles < grid) grid = (int)tiles;
+  if (units < grid) grid = (int)units;
   kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, args);
-  return check_launch("gemm_tcgen05");
+  if (magma_status_t st = check_launch("gemm_tcgen05")) return st;
+  if (args.splits > 1) {
+    int64_t blocks = ceil_div(M * N, 256);
+    if (blocks > 8LL * num_sms()) blocks = 8LL * num_sms();
+    splitk_reduce<TC><<<(int)blocks, 256, 0, stream>>>(args.ws, args.splits, M, N,
+                                                       static_cast<TC*>(args.C), args.e);
+    return check_launch("gemm_splitk_reduce");
+  }
+  return MAGMA_OK;
 }
 
 template <int BN, typename TC>
@@ -463,17 +554,6 @@ magma_status_t dispatch_major(const void* a, const void* b, int64_t M, int64_t N
   if (!a_mn && b_mn) return launch_tc<BN, false, true, TC>(a, b, M, N, K, lda, ldb, args, s);
   if (a_mn && !b_mn) return launch_tc<BN, true, false, TC>(a, b, M, N, K, lda, ldb, args, s);
   return launch_tc<BN, true, true, TC>(a, b, M, N, K, lda, ldb, args, s);
-}
-
-// Picks BN by wave quantisation over the SMs: BN=256 halves the shared-memory
-// operand traffic per FLOP, BN=128 fills the SMs better when tiles are few.
-int choose_bn(int64_t M, int64_t N) {
-  const int sms = num_sms();
-  const int64_t t256 = ceil_div(M, kBM) * ceil_div(N, 256);
-  const int64_t t128 = ceil_div(M, kBM) * ceil_div(N, 128);
-  const double cost256 = (double)ceil_div(t256, sms) * 1.0;
-  const double cost128 = (double)ceil_div(t128, sms) * 0.5 * 1.15;
-  return cost128 < cost256 ? 128 : 256;
 }
 
 template <typename TA, typename TC>
@@ -499,8 +579,9 @@ using namespace magma;
 extern "C" {
 
 size_t magma_gemm_workspace_size(int64_t m, int64_t n, int64_t k, magma_dtype_t ab_dtype) {
-  (void)m; (void)n; (void)k; (void)ab_dtype;
-  return 0;
+  if (ab_dtype != MAGMA_DTYPE_BF16 || m <= 0 || n <= 0 || k <= 0) return 0;
+  const TcPlan p = choose_plan(m, n, k);
+  return p.splits > 1 ? (size_t)p.splits * (size_t)m * (size_t)n * sizeof(float) : 0;
 }
 
 magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
@@ -508,8 +589,6 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
                           magma_dtype_t ab_dtype, magma_dtype_t c_dtype, int32_t epilogue,
                           const float* bias, const void* aux_in, void* aux_out, void* workspace,
                           size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   MAGMA_REQUIRE(m >= 0 && n >= 0 && k >= 0, "magma_gemm: negative size");
   MAGMA_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31),
                 "magma_gemm: dimension exceeds 2^31");
@@ -542,8 +621,14 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
   if (tc_ok) {
     const int vec_ok = (ldc % 8) == 0 && aligned16(c) && (aux_in == nullptr || aligned16(aux_in)) &&
                        (aux_out == nullptr || aligned16(aux_out));
-    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok};
-    const int bn = choose_bn(m, n);
+    TcPlan plan = choose_plan(m, n, k);
+    // Split-K only with a large enough caller workspace; otherwise one pass.
+    const size_t need = plan.splits > 1 ? (size_t)plan.splits * m * n * sizeof(float) : 0;
+    if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
+      plan = {plan.bn, 1, (int)ceil_div(k, kBK)};
+    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, plan.splits, plan.kb_per_split,
+                static_cast<float*>(workspace)};
+    const int bn = plan.bn;
     if (bn == 256)
       return c32 ? dispatch_major<256, float>(a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
                  : dispatch_major<256, __nv_bfloat16>(a, b, m, n, k, lda, ldb, trans_a, trans_b,

@@ -236,13 +236,27 @@ __global__ void bias_grad_partial(const T* __restrict__ dy, float* __restrict__ 
   part[(int64_t)blockIdx.y * cols + c] = s;
 }
 
-__global__ void bias_grad_final(const float* __restrict__ part, float* __restrict__ dbias,
-                                int nblocks, int cols, int accumulate) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+// Sums the partial rows in a fixed order (32 columns x 8 partial phases per
+// CTA, then the 8 phase sums in order).
+__global__ void __launch_bounds__(256)
+bias_grad_final(const float* __restrict__ part, float* __restrict__ dbias, int nblocks, int cols,
+                int accumulate) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += part[(int64_t)b * cols + c];
-  dbias[c] = accumulate ? dbias[c] + s : s;
+  if (c < cols) {
+#pragma unroll 4
+    for (int b = ty; b < nblocks; b += 8) s += part[(int64_t)b * cols + c];
+  }
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    float t = red[0][tx];
+#pragma unroll
+    for (int y = 1; y < 8; ++y) t += red[y][tx];
+    dbias[c] = accumulate ? dbias[c] + t : t;
+  }
 }
 
 int bias_row_blocks(int64_t rows) {
@@ -405,8 +419,8 @@ magma_status_t magma_bias_grad(const void* dy, float* dbias, int64_t rows, int64
     bias_grad_partial<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part, rows,
                                                           (int)cols, ld, rpb);
   if (magma_status_t st = check_launch("bias_grad_partial")) return st;
-  bias_grad_final<<<(unsigned)ceil_div(cols, 256), 256, 0, s>>>(part, dbias, nb, (int)cols,
-                                                                accumulate);
+  bias_grad_final<<<(unsigned)ceil_div(cols, 32), 256, 0, s>>>(part, dbias, nb, (int)cols,
+                                                               accumulate);
   return check_launch("bias_grad_final");
 }
 

@@ -261,17 +261,30 @@ ln_bwd_generic(const TDY* __restrict__ dy, const TX* __restrict__ x,
   }
 }
 
-// Sums per-CTA partial rows in CTA order: out[c] (+)= sum_b part[b][c].
-__global__ void reduce_partials(const float* __restrict__ part, int nblocks, int width,
-                                float* __restrict__ dgamma, float* __restrict__ dbeta, int dim,
-                                int accumulate) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= width) return;
+// Sums per-CTA partial rows: out[c] (+)= sum_b part[b][c]. A 32 x 8 CTA
+// covers 32 columns; row y of threads sums partials b = y, y+8, ... in order,
+// then the 8 sums are added in y order (fixed order: deterministic).
+__global__ void __launch_bounds__(256)
+reduce_partials(const float* __restrict__ part, int nblocks, int width,
+                float* __restrict__ dgamma, float* __restrict__ dbeta, int dim, int accumulate) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += part[(int64_t)b * width + c];
-  float* dst = c < dim ? dgamma + c : dbeta + (c - dim);
-  if (dst == nullptr) return;
-  *dst = accumulate ? *dst + s : s;
+  if (c < width) {
+#pragma unroll 4
+    for (int b = ty; b < nblocks; b += 8) s += part[(int64_t)b * width + c];
+  }
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < width) {
+    float t = red[0][tx];
+#pragma unroll
+    for (int y = 1; y < 8; ++y) t += red[y][tx];
+    float* dst = c < dim ? dgamma + c : dbeta + (c - dim);
+    if (dst == nullptr) return;
+    *dst = accumulate ? *dst + t : t;
+  }
 }
 
 int bwd_blocks(int64_t rows) {
@@ -320,8 +333,8 @@ magma_status_t launch_bwd(const void* dy, const void* x, const float* gamma, con
   if (magma_status_t s = check_launch("layernorm_bwd")) return s;
   if (dgamma != nullptr || dbeta != nullptr) {
     int width = 2 * dim;
-    reduce_partials<<<(width + 255) / 256, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
-                                                             dim, acc_params);
+    reduce_partials<<<(width + 31) / 32, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
+                                                           dim, acc_params);
     if (magma_status_t s = check_launch("layernorm_bwd_reduce")) return s;
   }
   return MAGMA_OK;

@@ -84,6 +84,33 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 4-D TMA tile load (x innermost).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, int w, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (tensor-core operand reads through smem descriptors).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -215,6 +242,9 @@ magma_status_t encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype,
                                     uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                                     uint32_t box_inner, uint32_t box_outer,
                                     CUtensorMapSwizzle swizzle);
+magma_status_t encode_tensor_map_nd(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                                    int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                                    const uint32_t* box, CUtensorMapSwizzle swizzle);
 magma_status_t encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                                     const uint64_t dims[3], const uint64_t strides_bytes[2],
                                     const uint32_t box[3], CUtensorMapSwizzle swizzle);

@@ -68,4 +68,29 @@ magma_status_t encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype,
   return MAGMA_OK;
 }
 
+magma_status_t encode_tensor_map_nd(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                                    int rank, const uint64_t* dims_in,
+                                    const uint64_t* strides_bytes, const uint32_t* box_in,
+                                    CUtensorMapSwizzle swizzle) {
+  auto enc = get_encode();
+  if (enc == nullptr)
+    return fail(MAGMA_UNAVAILABLE, "cuTensorMapEncodeTiled unavailable (%s)",
+                cudaGetErrorString(g_encode_err));
+  if (rank < 1 || rank > 5) return fail(MAGMA_INVALID_ARGUMENT, "tensor map rank %d", rank);
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    dims[i] = dims_in[i];
+    box[i] = box_in[i];
+    estr[i] = 1;
+    if (i + 1 < rank) strides[i] = strides_bytes[i];
+  }
+  CUresult r = enc(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MAGMA_INVALID_ARGUMENT, "cuTensorMapEncodeTiled (%d-D) failed (%d)", rank, (int)r);
+  return MAGMA_OK;
+}
+
 }  // namespace magma

@@ -210,7 +210,13 @@ class GPTTrainer:
         self.d_fc = torch.empty((T, 4 * D), **a)
         self.d_att = torch.empty((T, D), **a)
         self.dqkv = torch.empty((T, 3 * D), **a)
-        ws = max(lib.query("magma_layernorm_bwd_workspace_size", T, D),
+        Vp4 = cfg.vocab_padded
+        gemm_shapes = [(T, 3 * D, D), (T, D, D), (T, 4 * D, D), (T, D, 4 * D), (T, Vp4, D),
+                       (T, D, Vp4), (Vp4, D, T), (T, 4 * D, D), (T, D, 3 * D), (3 * D, D, T),
+                       (D, D, T), (4 * D, D, T), (D, 4 * D, T)]
+        ws = max(max(lib.query("magma_gemm_workspace_size", m, n, k, self.DT)
+                     for m, n, k in gemm_shapes),
+                 lib.query("magma_layernorm_bwd_workspace_size", T, D),
                  lib.query("magma_attention_bwd_workspace_size", B, H, cfg.seq, cfg.head_dim, self.DT),
                  lib.query("magma_bias_grad_workspace_size", T, 4 * D),
                  lib.query("magma_bias_grad_workspace_size", T, 3 * D))
@@ -226,7 +232,7 @@ class GPTTrainer:
               aux_out=None, c_dtype=None):
         lib.call("magma_gemm", _p(a), _p(b), _p(c), m, n, k, lda, ldb, ldc, ta, tb, self.DT,
                  c_dtype if c_dtype is not None else self.DT, epi, _p(bias), _p(aux_in),
-                 _p(aux_out), None, 0, self._s())
+                 _p(aux_out), _p(self.ws), self.ws.numel(), self._s())
 
     def _ln_fwd(self, x, w, b, y, mean, rstd):
         lib.call("magma_layernorm_fwd", _p(x), _p(w), _p(b), _p(y), _p(mean), _p(rstd), self.T,

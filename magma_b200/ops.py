@@ -116,9 +116,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, trans_a: bool = False, trans_b: bo
     for t in (aux_in, aux_out):
         if t is not None:
             assert t.shape == (m, n) and t.stride(0) == out.stride(0)
+    ws_n = lib.query("magma_gemm_workspace_size", m, n, k, _dtype(a))
+    ws = workspace(ws_n, a.device) if ws_n else None
     lib.call("magma_gemm", _ptr(a), _ptr(b), _ptr(out), m, n, k, a.stride(0), b.stride(0),
              out.stride(0), int(trans_a), int(trans_b), _dtype(a), _dtype(out), int(epilogue),
-             _ptr(bias), _ptr(aux_in), _ptr(aux_out), None, 0, _stream())
+             _ptr(bias), _ptr(aux_in), _ptr(aux_out), _ptr(ws), 0 if ws is None else ws.numel(),
+             _stream())
     return out
 
 

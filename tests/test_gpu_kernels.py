@@ -31,9 +31,11 @@ def close_norm(got, want, rtol):
     """Norm-wise relative error ||got - want|| / ||want|| <= rtol.
 
     Used for BF16 attention backward: O is stored in BF16, so rowsum(dO*O)
-    carries BF16 rounding and dS = P*(dP - rowsum) cancels for some entries;
-    isolated elements then exceed an elementwise bound although the tensor
-    as a whole is within tolerance.
+    carries BF16 rounding and dS = P*(dP - rowsum) cancels for some entries,
+    and the tensor-core path rounds P and dS to BF16 before the P^T.dO and
+    dS.K contractions (as any BF16 flash-attention backward does); isolated
+    elements then exceed an elementwise bound although the tensor as a whole
+    is within tolerance.
     """
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
@@ -181,6 +183,42 @@ def test_gemm_bf16_tcgen05(cuda, m, n, k, ta, tb):
     close(out16.float().cpu(), ref.cpu(), 2e-2)
 
 
+@pytest.mark.parametrize("m,n,k,ta,tb", [(768, 768, 8192, 1, 0), (8192, 768, 50304, 0, 0),
+                                          (2304, 768, 8192, 1, 0), (200, 136, 4096, 1, 0),
+                                          (256, 256, 2048, 0, 1)])
+def test_gemm_bf16_split_k(cuda, m, n, k, ta, tb):
+    """Few output tiles, long K: the K-split path (F32 partials + ordered sum).
+
+    rtol 1e-3 against an F32 reference: over K up to 50304 products the two
+    F32 accumulation orders differ by a few 1e-4 of the output scale; a wrong
+    split would be off by whole partial sums (order 1 relative)."""
+    from magma_b200 import ops, lib
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn((k, m) if ta else (m, k), device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn((n, k) if tb else (k, n), device="cuda", generator=g).to(torch.bfloat16)
+    ref = (a.float().T if ta else a.float()) @ (b.float().T if tb else b.float())
+    need = lib.query("magma_gemm_workspace_size", m, n, k, lib.BF16)
+    out = ops.gemm(a, b, trans_a=bool(ta), trans_b=bool(tb), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ops.device_error_check() == 0
+    close(out.cpu(), ref.cpu(), 1e-3)
+    # deterministic: a second run gives identical bits
+    out2 = ops.gemm(a, b, trans_a=bool(ta), trans_b=bool(tb), out_dtype=torch.float32)
+    assert torch.equal(out, out2)
+    if need:
+        # without a workspace the same call runs unsplit and stays correct
+        c = torch.empty((m, n), device="cuda")
+        lib.call("magma_gemm", a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, a.stride(0),
+                 b.stride(0), n, ta, tb, lib.BF16, lib.F32, lib.EPI_NONE, None, None, None, None,
+                 0, torch.cuda.current_stream().cuda_stream)
+        close(c.cpu(), ref.cpu(), 1e-3)
+    # split + epilogue (bias, BF16 out)
+    bias = torch.randn(n, device="cuda", generator=g)
+    yb = ops.gemm(a, b, trans_a=bool(ta), trans_b=bool(tb), epilogue=lib.EPI_BIAS, bias=bias)
+    close(yb.float().cpu(), (ref + bias).cpu(), 2e-2)
+
+
 def test_gemm_bf16_epilogues(cuda, oracle):
     from magma_b200 import ops, lib
 
@@ -264,45 +302,51 @@ def test_attention_f32(cuda, oracle, shape, causal):
     close(dv.cpu(), rdv, 1e-4)
 
 
-@pytest.mark.parametrize("shape", [(1, 12, 1024, 64), (2, 2, 320, 64), (1, 1, 64, 64)])
-def test_attention_bf16(cuda, oracle, shape):
+@pytest.mark.parametrize("shape,causal", [((1, 12, 1024, 64), True), ((2, 2, 320, 64), True),
+                                          ((1, 1, 64, 64), True), ((1, 2, 256, 64), False),
+                                          ((1, 3, 200, 64), False)])
+def test_attention_bf16(cuda, oracle, shape, causal):
+    """BF16, head_dim 64: the tcgen05 kernels."""
     from magma_b200 import ops
 
     rng = np.random.default_rng(sum(shape) + 1)
     q, k, v, do = qkv(rng, shape, torch.bfloat16)
     scale = 1 / math.sqrt(shape[-1])
     bt = lambda a: t(a, torch.bfloat16)  # noqa: E731
-    o, lse = ops.attention_fwd(bt(q), bt(k), bt(v), scale, True)
+    o, lse = ops.attention_fwd(bt(q), bt(k), bt(v), scale, causal)
     torch.cuda.synchronize()
     assert ops.device_error_check() == 0
-    ro, rlse = oracle.attention_fwd(q, k, v, scale, True)
+    ro, rlse = oracle.attention_fwd(q, k, v, scale, causal)
     close(o.float().cpu(), ro, 2e-2)
     close(lse.cpu(), rlse, 1e-3)
-    dq, dk, dv = ops.attention_bwd(bt(q), bt(k), bt(v), o, bt(do), lse, scale, True)
+    dq, dk, dv = ops.attention_bwd(bt(q), bt(k), bt(v), o, bt(do), lse, scale, causal)
     torch.cuda.synchronize()
     assert ops.device_error_check() == 0
-    rdq, rdk, rdv = oracle.attention_bwd(q, k, v, do, scale, True)
+    rdq, rdk, rdv = oracle.attention_bwd(q, k, v, do, scale, causal)
     close_norm(dq.float().cpu(), rdq, 2e-2)
     close_norm(dk.float().cpu(), rdk, 2e-2)
-    close(dv.float().cpu(), rdv, 2e-2)
+    close_norm(dv.float().cpu(), rdv, 2e-2)
 
 
-def test_attention_strided_qkv_layout(cuda, oracle):
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_attention_strided_qkv_layout(cuda, oracle, dtype):
     """Q/K/V read straight out of a fused [B, S, 3, H, D] QKV projection."""
     from magma_b200 import ops
 
     B, S, H, D = 2, 256, 4, 64
     rng = np.random.default_rng(9)
     packed = rng.standard_normal((B, S, 3, H, D)).astype(np.float32)
-    tp = t(packed)
+    if dtype == torch.bfloat16:
+        packed = bf16_round(packed)
+    tp = t(packed, dtype)
     q = tp[:, :, 0].permute(0, 2, 1, 3)
     k = tp[:, :, 1].permute(0, 2, 1, 3)
     v = tp[:, :, 2].permute(0, 2, 1, 3)
-    o = torch.empty((B, S, H, D), device="cuda").permute(0, 2, 1, 3)
+    o = torch.empty((B, S, H, D), device="cuda", dtype=dtype).permute(0, 2, 1, 3)
     ops.attention_fwd(q, k, v, 0.125, True, out=o)
-    ro, _ = oracle.attention_fwd(q.cpu().contiguous().numpy(), k.cpu().contiguous().numpy(),
-                                 v.cpu().contiguous().numpy(), 0.125, True)
-    close(o.cpu(), ro, 1e-4)
+    f = lambda x: x.float().cpu().contiguous().numpy()  # noqa: E731
+    ro, _ = oracle.attention_fwd(f(q), f(k), f(v), 0.125, True)
+    close(o.float().cpu(), ro, 1e-4 if dtype == torch.float32 else 2e-2)
 
 
 # -------------------------------------------------------------------------- glue

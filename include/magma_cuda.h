@@ -137,6 +137,34 @@ MAGMA_API magma_status_t magma_layernorm_bwd(const void* dy, const void* x, cons
                                    int32_t accumulate_dx, int32_t accumulate_params,
                                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of magma_layernorm_bwd (no counterpart in the
+ * reference: Magma's own runtime always hands XLA a buffer pool).
+ *
+ * For callers that cannot allocate device memory for the per-CTA dgamma/dbeta
+ * partial sums: a plugin whose host framework owns all device memory and has no
+ * allocation hook for it, code running inside an existing stream capture or a
+ * real-time step loop where a cudaMalloc would synchronise the device, or a
+ * caller working inside a fixed memory budget. Same arguments and results as
+ * magma_layernorm_bwd, without the workspace: the partial sums go to a
+ * scratch array compiled into the library (2.3 MiB on every GPU that loads the
+ * library, held until the process exits). Limits: dim <= 1024 (larger dims
+ * return MAGMA_INVALID_ARGUMENT; use magma_layernorm_bwd with a workspace).
+ * The first call on a device looks up the scratch array's device address
+ * (cudaGetSymbolAddress) — make that first call before any stream capture.
+ * Every call on a device shares the one scratch array: calls that overlap on
+ * the GPU (on different streams without ordering) race and give wrong sums;
+ * order them on one stream. Each call writes every scratch entry it later
+ * reads, so nothing carried over from the previous call is used. Calls no
+ * cudaMalloc, cudaFree or allocating library routine. */
+MAGMA_API magma_status_t magma_layernorm_bwd_noalloc(const void* dy, const void* x,
+                                   const float* gamma, const float* mean, const float* rstd,
+                                   void* dx, float* dgamma, float* dbeta,
+                                   int64_t rows, int64_t dim,
+                                   magma_dtype_t dy_dtype, magma_dtype_t x_dtype,
+                                   magma_dtype_t dx_dtype,
+                                   int32_t accumulate_dx, int32_t accumulate_params,
+                                   void* stream);
+
 /* ---- Linear contraction (GEMM) ------------------------------------------------
  * Replaces Tensor.matmul -> stablehlo.dot (Sources/Core/Tensor.swift:1102-1121,
  * Sources/StableHLO/Builder/MLIRBuilder.swift:372-378) as used by value Linear

@@ -16,6 +16,8 @@
 // a fixed butterfly order (deterministic). dgamma/dbeta are reduced per CTA in
 // shared memory in warp order, written as per-CTA partial rows to the caller's
 // workspace, then summed over CTAs in CTA order by a second kernel.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace magma {
@@ -340,6 +342,67 @@ magma_status_t launch_bwd(const void* dy, const void* x, const float* gamma, con
   return MAGMA_OK;
 }
 
+// ---- allocation-free backward --------------------------------------------
+// Scratch for magma_layernorm_bwd_noalloc: one partial row of [dgamma | dbeta]
+// per CTA. Bounds: at most kNoAllocMaxBlocks CTAs and dim <= kNoAllocMaxDim,
+// i.e. 296 x 2 x 1024 floats = 2.3 MiB, held on every GPU that loads the
+// library until the process exits.
+constexpr int kNoAllocMaxDim = 1024;
+constexpr int kNoAllocMaxBlocks = 296;
+static __device__ __align__(256) float g_ln_bwd_scratch[kNoAllocMaxBlocks * 2 * kNoAllocMaxDim];
+
+constexpr int kNoAllocMaxDevices = 64;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device, resolved once per
+// device with that device current. Host code must not use the array's name as
+// a pointer: on the host it only stands in for the symbol.
+magma_status_t noalloc_scratch(float** out) {
+  int dev = 0;
+  if (magma_status_t st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice")) return st;
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(MAGMA_UNIMPLEMENTED, "magma_layernorm_bwd_noalloc: device ordinal %d >= %d", dev,
+                kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&p, g_ln_bwd_scratch);
+    if (err != cudaSuccess)
+      return cuda_status(err, "cudaGetSymbolAddress(layernorm backward scratch)");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MAGMA_OK;
+}
+
+template <typename TDY, typename TX, typename TDX>
+magma_status_t launch_bwd_noalloc(const void* dy, const void* x, const float* gamma,
+                                  const float* mean, const float* rstd, void* dx, float* dgamma,
+                                  float* dbeta, int64_t rows, int dim, int acc_dx, int acc_params,
+                                  float* part, cudaStream_t stream) {
+  int blocks = bwd_blocks(rows);
+  if (blocks > kNoAllocMaxBlocks) blocks = kNoAllocMaxBlocks;
+  const bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(dy) &&
+                   aligned16(dx) && aligned16(gamma);
+  if (vec) {
+    const size_t smem = 2 * (size_t)dim * sizeof(float);
+    ln_bwd_cached<TDY, TX, TDX><<<blocks, kWarps * 32, smem, stream>>>(
+        (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
+  } else {
+    ln_bwd_generic<TDY, TX, TDX><<<blocks, kWarps * 32, 0, stream>>>(
+        (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
+  }
+  if (magma_status_t s = check_launch("layernorm_bwd_noalloc")) return s;
+  if (dgamma != nullptr || dbeta != nullptr) {
+    const int width = 2 * dim;
+    reduce_partials<<<(width + 31) / 32, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
+                                                           dim, acc_params);
+    if (magma_status_t s = check_launch("layernorm_bwd_noalloc_reduce")) return s;
+  }
+  return MAGMA_OK;
+}
+
 }  // namespace
 }  // namespace magma
 
@@ -413,6 +476,45 @@ magma_status_t magma_layernorm_bwd(const void* dy, const void* x, const float* g
   if (!f_dy && f_x && !f_dx) LN_BWD(__nv_bfloat16, float, __nv_bfloat16);
   LN_BWD(float, __nv_bfloat16, __nv_bfloat16);
 #undef LN_BWD
+}
+
+magma_status_t magma_layernorm_bwd_noalloc(const void* dy, const void* x, const float* gamma,
+                                           const float* mean, const float* rstd, void* dx,
+                                           float* dgamma, float* dbeta, int64_t rows, int64_t dim,
+                                           magma_dtype_t dy_dtype, magma_dtype_t x_dtype,
+                                           magma_dtype_t dx_dtype, int32_t accumulate_dx,
+                                           int32_t accumulate_params, void* stream) {
+  MAGMA_REQUIRE(rows >= 0 && dim > 0, "magma_layernorm_bwd_noalloc: bad shape rows=%lld dim=%lld",
+                (long long)rows, (long long)dim);
+  MAGMA_REQUIRE(dim <= kNoAllocMaxDim,
+                "magma_layernorm_bwd_noalloc: dim %lld exceeds the built-in scratch limit of %d "
+                "(use magma_layernorm_bwd with a workspace)",
+                (long long)dim, kNoAllocMaxDim);
+  MAGMA_REQUIRE(is_float_dtype(dy_dtype) && is_float_dtype(x_dtype) && is_float_dtype(dx_dtype),
+                "magma_layernorm_bwd_noalloc: unsupported dtypes");
+  MAGMA_REQUIRE(!accumulate_dx || dx_dtype == MAGMA_DTYPE_F32,
+                "magma_layernorm_bwd_noalloc: accumulate_dx needs an F32 dx");
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(dy && x && gamma && mean && rstd && dx,
+                "magma_layernorm_bwd_noalloc: NULL pointer");
+  float* part = nullptr;
+  if (magma_status_t st = noalloc_scratch(&part)) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int d = (int)dim;
+  const bool f_dy = dy_dtype == MAGMA_DTYPE_F32, f_x = x_dtype == MAGMA_DTYPE_F32,
+             f_dx = dx_dtype == MAGMA_DTYPE_F32;
+#define LN_BWD_NA(TDY, TX, TDX)                                                                 \
+  return launch_bwd_noalloc<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, dgamma, dbeta, rows, d, \
+                                          accumulate_dx, accumulate_params, part, s)
+  if (f_dy && f_x && f_dx) LN_BWD_NA(float, float, float);
+  if (!f_dy && f_x && f_dx) LN_BWD_NA(__nv_bfloat16, float, float);
+  if (!f_dy && !f_x && !f_dx) LN_BWD_NA(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16);
+  if (!f_dy && !f_x && f_dx) LN_BWD_NA(__nv_bfloat16, __nv_bfloat16, float);
+  if (f_dy && !f_x && f_dx) LN_BWD_NA(float, __nv_bfloat16, float);
+  if (f_dy && f_x && !f_dx) LN_BWD_NA(float, float, __nv_bfloat16);
+  if (!f_dy && f_x && !f_dx) LN_BWD_NA(__nv_bfloat16, float, __nv_bfloat16);
+  LN_BWD_NA(float, __nv_bfloat16, __nv_bfloat16);
+#undef LN_BWD_NA
 }
 
 }  // extern "C"

@@ -87,6 +87,8 @@ SIGNATURES = {
     "magma_layernorm_bwd_workspace_size": (_sz, [_i64, _i64]),
     "magma_layernorm_bwd": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32,
                                    _i32, _i32, _i32, _vp, _sz, _vp]),
+    "magma_layernorm_bwd_noalloc": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                           _i32, _i32, _i32, _i32, _i32, _vp]),
     "magma_gemm_workspace_size": (_sz, [_i64, _i64, _i64, _i32]),
     "magma_gemm": (None, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
                           _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
@@ -116,7 +118,8 @@ SIGNATURES = {
 
 # Kernel launches one successful call of each op makes (for launch accounting).
 KERNELS_PER_CALL = {
-    "magma_layernorm_fwd": 1, "magma_layernorm_bwd": 2, "magma_gemm": 1,
+    "magma_layernorm_fwd": 1, "magma_layernorm_bwd": 2, "magma_layernorm_bwd_noalloc": 2,
+    "magma_gemm": 1,
     "magma_attention_fwd": 1, "magma_attention_bwd": 3, "magma_adam_step": 1,
     "magma_adam_step_multi": 1, "magma_embedding_fwd": 1, "magma_embedding_bwd": 2,
     "magma_cross_entropy_fwd_bwd": 1, "magma_reduce_sum": 1, "magma_gelu_fwd": 1,

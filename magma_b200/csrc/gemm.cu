@@ -171,10 +171,17 @@ struct TcCfg {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = kStages * kStageBytes;
+  // Epilogue staging: per epilogue warp a 32 x 64 F32 chunk, row pitch 66 floats
+  // (8-byte aligned rows; conflict-free 8-byte stores by row and loads by column pair).
+  static constexpr int kStageOffset = kStages * kStageBytes;
+  static constexpr int kStagePitch = 66;
+  static constexpr int kStageWarpFloats = 32 * kStagePitch;
+  static constexpr int kStagingBytes = 4 * kStageWarpFloats * 4;
+  static constexpr int kBarOffset = kStageOffset + kStagingBytes;
   // full[S], empty[S], tfull[2], tempty[2], done -> 8 B each; then TMEM slot.
   static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  static_assert(kSmemBytes <= 232448, "GEMM shared memory exceeds the sm_100 per-block limit");
   static constexpr int kTmemCols = 2 * BN;
 };
 
@@ -183,7 +190,8 @@ struct TcArgs {
   void* C;
   EpiArgs e;
   int* err;
-  int vec_ok;  // C/aux pointers 16-B aligned and ldc % 8 == 0: 8-wide vector stores
+  int vec_ok;   // C/aux pointers 8-B aligned and ldc even: column-pair vector accesses
+  int vec8_ok;  // C 16-B aligned and ldc % 8 == 0: 8-column vector stores
   // Split-K: work unit u covers output tile (u % tiles) over k-blocks
   // [s*kb_per_split, (s+1)*kb_per_split) with s = u / tiles. With splits > 1
   // the raw F32 accumulator goes to ws + s*M*N (leading dimension N) and a
@@ -193,63 +201,154 @@ struct TcArgs {
   float* ws;
 };
 
-// Stores 8 consecutive columns (col .. col+7) of one row with the epilogue.
+// Epilogue on two consecutive columns (col, col+1) of one row; b0/b1 are the
+// columns' bias values (0 without bias). pair: both columns exist and the
+// pointers allow one 2-element access.
 template <typename TC>
-__device__ __forceinline__ void epi_store8(const TcArgs& a, int64_t row, int64_t col,
-                                           const float (&v)[8], bool vec_ok) {
+__device__ __forceinline__ void epi_store2(const TcArgs& a, int64_t row, int64_t col, float v0,
+                                           float v1, float b0, float b1, bool pair) {
   TC* C = static_cast<TC*>(a.C);
   const int64_t off = row * a.e.ldc + col;
-  if (vec_ok && col + 8 <= a.N) {
-    float o[8];
-    const int epi = a.e.epi;
-    if (epi == MAGMA_EPI_NONE) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = v[i];
-    } else if (epi == MAGMA_EPI_BIAS || epi == MAGMA_EPI_BIAS_GELU || epi == MAGMA_EPI_BIAS_RELU ||
-               epi == MAGMA_EPI_BIAS_RESIDUAL) {
-      float pre[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pre[i] = a.e.bias ? __fadd_rn(v[i], a.e.bias[col + i]) : v[i];
-      if (epi == MAGMA_EPI_BIAS) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = pre[i];
-      } else if (epi == MAGMA_EPI_BIAS_RESIDUAL) {
-        float r[8];
-        load8(static_cast<const float*>(a.e.aux_in) + off, r);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(r[i], pre[i]);
-      } else {
-        store8(static_cast<TC*>(a.e.aux_out) + off, pre);
-        if (epi == MAGMA_EPI_BIAS_GELU) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] = gelu_t<TC>(pre[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] = fmaxf(pre[i], 0.f);
-        }
-      }
-    } else if (epi == MAGMA_EPI_DGELU || epi == MAGMA_EPI_DRELU) {
-      float x[8];
-      load8(static_cast<const TC*>(a.e.aux_in) + off, x);
-      if (epi == MAGMA_EPI_DGELU) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[i], gelu_grad_t<TC>(x[i]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = x[i] > 0.f ? v[i] : 0.f;
-      }
-    } else {  // ACCUMULATE
-      float c[8];
-      load8(C + off, c);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(c[i], v[i]);
+  const int epi = a.e.epi;
+  if (!pair) {
+    C[off] = from_f32<TC>(epi_value<TC>(a.e, C, off, col, v0));
+    if (col + 1 < a.N) C[off + 1] = from_f32<TC>(epi_value<TC>(a.e, C, off + 1, col + 1, v1));
+    return;
+  }
+  float o0, o1;
+  if (epi == MAGMA_EPI_NONE) {
+    o0 = v0;
+    o1 = v1;
+  } else if (epi == MAGMA_EPI_BIAS) {
+    o0 = __fadd_rn(v0, b0);
+    o1 = __fadd_rn(v1, b1);
+  } else if (epi == MAGMA_EPI_BIAS_RESIDUAL) {
+    const float2 r = *reinterpret_cast<const float2*>(static_cast<const float*>(a.e.aux_in) + off);
+    o0 = __fadd_rn(r.x, __fadd_rn(v0, b0));
+    o1 = __fadd_rn(r.y, __fadd_rn(v1, b1));
+  } else if (epi == MAGMA_EPI_BIAS_GELU || epi == MAGMA_EPI_BIAS_RELU) {
+    const float p0 = __fadd_rn(v0, b0), p1 = __fadd_rn(v1, b1);
+    store2(static_cast<TC*>(a.e.aux_out) + off, p0, p1);
+    if (epi == MAGMA_EPI_BIAS_GELU) {
+      o0 = gelu_t<TC>(p0);
+      o1 = gelu_t<TC>(p1);
+    } else {
+      o0 = fmaxf(p0, 0.f);
+      o1 = fmaxf(p1, 0.f);
     }
-    store8(C + off, o);
-  } else {
+  } else if (epi == MAGMA_EPI_DGELU || epi == MAGMA_EPI_DRELU) {
+    float x0, x1;
+    load2(static_cast<const TC*>(a.e.aux_in) + off, x0, x1);
+    if (epi == MAGMA_EPI_DGELU) {
+      o0 = __fmul_rn(v0, gelu_grad_t<TC>(x0));
+      o1 = __fmul_rn(v1, gelu_grad_t<TC>(x1));
+    } else {
+      o0 = x0 > 0.f ? v0 : 0.f;
+      o1 = x1 > 0.f ? v1 : 0.f;
+    }
+  } else {  // ACCUMULATE (F32 output)
+    float c0, c1;
+    load2(C + off, c0, c1);
+    o0 = __fadd_rn(c0, v0);
+    o1 = __fadd_rn(c1, v1);
+  }
+  store2(C + off, o0, o1);
+}
+
+// Row-per-thread store of 64 accumulator columns (NONE / BIAS epilogues and
+// split-K partials): 16-byte stores, one row per thread — the fewest
+// instructions when nothing has to be read back from global memory.
+template <typename TO>
+__device__ __forceinline__ void direct_store64(TO* dst_row, const float* bias, int64_t col0,
+                                               int64_t N, const uint32_t (&ra)[32],
+                                               const uint32_t (&rb)[32], bool vec8) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (col + i < a.N)
-        C[off + i] = from_f32<TC>(epi_value<TC>(a.e, C, off + i, col + i, v[i]));
+  for (int g = 0; g < 8; ++g) {
+    const int64_t col = col0 + 8 * g;
+    if (col >= N) break;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      v[i] = __uint_as_float(g < 4 ? ra[8 * g + i] : rb[8 * (g - 4) + i]);
+    if (bias != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (col + i < N) v[i] = __fadd_rn(v[i], bias[col + i]);
+    }
+    if (vec8 && col + 8 <= N) {
+      store8(dst_row + col, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (col + i < N) dst_row[col + i] = from_f32<TO>(v[i]);
+    }
+  }
+}
+
+// One 64-column chunk of one warp's 32 tile rows, lane = column pair
+// (col, col+1). st points at this lane's pair in row 0 of the staged F32
+// accumulators (row pitch P). The epilogue is a template parameter (no
+// per-row branches) and every auxiliary load of the 32 rows is issued before
+// the first store so their latencies overlap.
+template <typename TC, int EPI, int P>
+__device__ __forceinline__ void epi_rows(const TcArgs& a, const float* __restrict__ st,
+                                         int64_t row0, int rows_here, int64_t col, float b0,
+                                         float b1) {
+  constexpr bool kAux = EPI == MAGMA_EPI_BIAS_RESIDUAL || EPI == MAGMA_EPI_DGELU ||
+                        EPI == MAGMA_EPI_DRELU || EPI == MAGMA_EPI_ACCUMULATE;
+  const int64_t ldc = a.e.ldc;
+  const int64_t base = row0 * ldc + col;
+  TC* c = static_cast<TC*>(a.C) + base;
+  float x0[32], x1[32];
+  if constexpr (kAux) {
+#pragma unroll
+    for (int rr = 0; rr < 32; ++rr) {
+      x0[rr] = x1[rr] = 0.f;
+      if (rr < rows_here) {
+        if constexpr (EPI == MAGMA_EPI_BIAS_RESIDUAL)
+          load2(static_cast<const float*>(a.e.aux_in) + base + rr * ldc, x0[rr], x1[rr]);
+        else if constexpr (EPI == MAGMA_EPI_ACCUMULATE)
+          load2(c + rr * ldc, x0[rr], x1[rr]);
+        else
+          load2(static_cast<const TC*>(a.e.aux_in) + base + rr * ldc, x0[rr], x1[rr]);
+      }
+    }
+  }
+#pragma unroll
+  for (int rr = 0; rr < 32; ++rr) {
+    if (rr < rows_here) {
+      const float2 v = *reinterpret_cast<const float2*>(st + rr * P);
+      float o0, o1;
+      if constexpr (EPI == MAGMA_EPI_NONE) {
+        o0 = v.x;
+        o1 = v.y;
+      } else if constexpr (EPI == MAGMA_EPI_BIAS) {
+        o0 = __fadd_rn(v.x, b0);
+        o1 = __fadd_rn(v.y, b1);
+      } else if constexpr (EPI == MAGMA_EPI_BIAS_RESIDUAL) {
+        o0 = __fadd_rn(x0[rr], __fadd_rn(v.x, b0));
+        o1 = __fadd_rn(x1[rr], __fadd_rn(v.y, b1));
+      } else if constexpr (EPI == MAGMA_EPI_BIAS_GELU || EPI == MAGMA_EPI_BIAS_RELU) {
+        const float p0 = __fadd_rn(v.x, b0), p1 = __fadd_rn(v.y, b1);
+        store2(static_cast<TC*>(a.e.aux_out) + base + rr * ldc, p0, p1);
+        if constexpr (EPI == MAGMA_EPI_BIAS_GELU) {
+          o0 = gelu_t<TC>(p0);
+          o1 = gelu_t<TC>(p1);
+        } else {
+          o0 = fmaxf(p0, 0.f);
+          o1 = fmaxf(p1, 0.f);
+        }
+      } else if constexpr (EPI == MAGMA_EPI_DGELU) {
+        o0 = __fmul_rn(v.x, gelu_grad_t<TC>(x0[rr]));
+        o1 = __fmul_rn(v.y, gelu_grad_t<TC>(x1[rr]));
+      } else if constexpr (EPI == MAGMA_EPI_DRELU) {
+        o0 = x0[rr] > 0.f ? v.x : 0.f;
+        o1 = x1[rr] > 0.f ? v.y : 0.f;
+      } else {  // ACCUMULATE
+        o0 = __fadd_rn(x0[rr], v.x);
+        o1 = __fadd_rn(x1[rr], v.y);
+      }
+      store2(c + rr * ldc, o0, o1);
     }
   }
 }
@@ -386,9 +485,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     sm100::mbar_wait(done_bar, 0, args.err);
   } else if (warp >= 2) {
     // ------------------------------ epilogue ------------------------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const bool vec_ok = args.vec_ok != 0;
-    const bool ws_vec = (N % 8) == 0;
+    // A warp owns TMEM lanes [32q, 32q+32) = tile rows. Per 64-column chunk:
+    // tcgen05.ld (thread = row) -> padded smem stage -> lanes take column
+    // pairs and walk the 32 rows, so each global access of the warp is one
+    // contiguous row segment (bias / residual / pre-activation reads and the
+    // stores alike).
+    const int q = warp & 3;
+    float* stage = reinterpret_cast<float*>(base_ptr + Cfg::kStageOffset) +
+                   (warp - 2) * Cfg::kStageWarpFloats;
+    const bool vec2 = args.vec_ok != 0;
+    const bool ws_pair = (N % 2) == 0;
+    const bool ws_vec8 = (N % 8) == 0;
+    const bool c_vec8 = args.vec8_ok != 0;
+    const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
+                        args.e.epi == MAGMA_EPI_BIAS;
+    const bool has_bias = args.e.bias != nullptr &&
+                          (args.e.epi == MAGMA_EPI_BIAS || args.e.epi == MAGMA_EPI_BIAS_GELU ||
+                           args.e.epi == MAGMA_EPI_BIAS_RESIDUAL || args.e.epi == MAGMA_EPI_BIAS_RELU);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
@@ -397,39 +510,85 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int n0 = (tile / tiles_m) * BN;
       if (!sm100::mbar_wait(tfull_bar(acc), acc_phase, args.err)) break;
       sm100::tc_fence_after();
-      const int64_t row = (int64_t)m0 + q * 32 + lane;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const int64_t row0 = (int64_t)m0 + q * 32;
+      const int rows_here = (int)min((int64_t)32, M - row0);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        sm100::tmem_ld32(taddr + c0, r);
+      for (int c0 = 0; c0 < BN; c0 += 64) {
+        uint32_t ra[32], rb[32];
+        sm100::tmem_ld32(taddr + c0, ra);
+        sm100::tmem_ld32(taddr + c0 + 32, rb);
         sm100::tmem_wait_ld();
-        if (row < M && n0 + c0 < N) {
+        if (c0 + 64 >= BN) {
+          // last TMEM read of this accumulator: hand it back to the MMA warp
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(tempty_bar(acc));
+        }
+        if (direct) {
+          const int64_t row = row0 + lane;
+          if (row < M && n0 + c0 < N) {
+            if (args.splits > 1)
+              direct_store64<float>(args.ws + (int64_t)split * M * N + row * N, nullptr,
+                                    (int64_t)n0 + c0, N, ra, rb, ws_vec8);
+            else
+              direct_store64<TC>(static_cast<TC*>(args.C) + row * args.e.ldc,
+                                 has_bias ? args.e.bias : nullptr, (int64_t)n0 + c0, N, ra, rb,
+                                 c_vec8);
+          }
+          continue;
+        }
+        float* srow = stage + lane * Cfg::kStagePitch;
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[g * 8 + i]);
-            const int64_t col = (int64_t)n0 + c0 + g * 8;
-            if (col >= N) continue;
-            if (args.splits > 1) {
-              float* dst = args.ws + (int64_t)split * M * N + row * N + col;
-              if (ws_vec && col + 8 <= N) {
-                store8(dst, v);
+        for (int j = 0; j < 16; ++j) {
+          *reinterpret_cast<float2*>(srow + 2 * j) =
+              make_float2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
+          *reinterpret_cast<float2*>(srow + 32 + 2 * j) =
+              make_float2(__uint_as_float(rb[2 * j]), __uint_as_float(rb[2 * j + 1]));
+        }
+        __syncwarp();
+        const int64_t col = (int64_t)n0 + c0 + 2 * lane;
+        if (col < N && rows_here > 0) {
+          const bool pair = col + 1 < N;
+          float b0 = 0.f, b1 = 0.f;
+          if (has_bias) {
+            b0 = args.e.bias[col];
+            b1 = pair ? args.e.bias[col + 1] : 0.f;
+          }
+          const float* st = stage + 2 * lane;
+          constexpr int P = Cfg::kStagePitch;
+          if (args.splits > 1) {
+            float* dst = args.ws + (int64_t)split * M * N + row0 * N + col;
+#pragma unroll 8
+            for (int rr = 0; rr < rows_here; ++rr) {
+              const float2 v = *reinterpret_cast<const float2*>(st + rr * P);
+              if (pair && ws_pair) {
+                *reinterpret_cast<float2*>(dst + (int64_t)rr * N) = v;
               } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  if (col + i < N) dst[i] = v[i];
+                dst[(int64_t)rr * N] = v.x;
+                if (pair) dst[(int64_t)rr * N + 1] = v.y;
               }
-            } else {
-              epi_store8<TC>(args, row, col, v, vec_ok);
+            }
+          } else if (pair && vec2) {
+            switch (args.e.epi) {
+              case MAGMA_EPI_NONE: epi_rows<TC, MAGMA_EPI_NONE, P>(args, st, row0, rows_here, col, b0, b1); break;
+              case MAGMA_EPI_BIAS: epi_rows<TC, MAGMA_EPI_BIAS, P>(args, st, row0, rows_here, col, b0, b1); break;
+              case MAGMA_EPI_BIAS_GELU: epi_rows<TC, MAGMA_EPI_BIAS_GELU, P>(args, st, row0, rows_here, col, b0, b1); break;
+              case MAGMA_EPI_BIAS_RESIDUAL: epi_rows<TC, MAGMA_EPI_BIAS_RESIDUAL, P>(args, st, row0, rows_here, col, b0, b1); break;
+              case MAGMA_EPI_DGELU: epi_rows<TC, MAGMA_EPI_DGELU, P>(args, st, row0, rows_here, col, b0, b1); break;
+              case MAGMA_EPI_ACCUMULATE: epi_rows<TC, MAGMA_EPI_ACCUMULATE, P>(args, st, row0, rows_here, col, b0, b1); break;
+              case MAGMA_EPI_BIAS_RELU: epi_rows<TC, MAGMA_EPI_BIAS_RELU, P>(args, st, row0, rows_here, col, b0, b1); break;
+              default: epi_rows<TC, MAGMA_EPI_DRELU, P>(args, st, row0, rows_here, col, b0, b1); break;
+            }
+          } else {
+            for (int rr = 0; rr < rows_here; ++rr) {
+              const float2 v = *reinterpret_cast<const float2*>(st + rr * P);
+              epi_store2<TC>(args, row0 + rr, col, v.x, v.y, b0, b1, false);
             }
           }
         }
+        __syncwarp();
       }
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(tempty_bar(acc));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -619,15 +778,16 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
   const bool tc_ok = ab_dtype == MAGMA_DTYPE_BF16 && k > 0 && aligned16(a) && aligned16(b) &&
                      (lda % 8) == 0 && (ldb % 8) == 0;
   if (tc_ok) {
-    const int vec_ok = (ldc % 8) == 0 && aligned16(c) && (aux_in == nullptr || aligned16(aux_in)) &&
-                       (aux_out == nullptr || aligned16(aux_out));
+    auto al8 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+    const int vec_ok = (ldc % 2) == 0 && al8(c) && al8(aux_in) && al8(aux_out);
     TcPlan plan = choose_plan(m, n, k);
     // Split-K only with a large enough caller workspace; otherwise one pass.
     const size_t need = plan.splits > 1 ? (size_t)plan.splits * m * n * sizeof(float) : 0;
     if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
       plan = {plan.bn, 1, (int)ceil_div(k, kBK)};
-    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, plan.splits, plan.kb_per_split,
-                static_cast<float*>(workspace)};
+    const int vec8_ok = (ldc % 8) == 0 && aligned16(c);
+    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, vec8_ok, plan.splits,
+                plan.kb_per_split, static_cast<float*>(workspace)};
     const int bn = plan.bn;
     if (bn == 256)
       return c32 ? dispatch_major<256, float>(a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)

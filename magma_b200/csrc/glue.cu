@@ -135,6 +135,95 @@ ce_block_kernel(T* __restrict__ logits, const int32_t* __restrict__ targets,
   }
 }
 
+// Large class counts, 16-byte-aligned rows with ld % 8 == 0: a CTA per row,
+// one read pass with a per-thread online (max, sum of exp) over 8-element
+// vectors, a block combine, then one pass that writes the gradient: two reads
+// and one write of the row instead of three reads.
+__device__ __forceinline__ void online_add(float& m, float& s, float x) {
+  if (x > m) {
+    s = s * expf(m - x) + 1.0f;
+    m = x;
+  } else {
+    s += expf(x - m);
+  }
+}
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;
+  s = s * expf(m - mm) + s2 * expf(m2 - mm);
+  m = mm;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512)
+ce_block_vec_kernel(T* __restrict__ logits, const int32_t* __restrict__ targets,
+                    float* __restrict__ losses, int64_t rows, int classes, int64_t ld,
+                    float grad_scale, int* err) {
+  __shared__ float red_m[16], red_s[16];
+  __shared__ float bm, bs;
+  const int tid = threadIdx.x;
+  const int nw = blockDim.x >> 5;
+  const int nvec = (int)(ld >> 3);
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    T* row = logits + r * ld;
+    float m = -INFINITY, s = 0.f;
+    for (int vi = tid; vi < nvec; vi += blockDim.x) {
+      float v[8];
+      load8(row + vi * 8, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (vi * 8 + i < classes) online_add(m, s, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      online_merge(m, s, m2, s2);
+    }
+    if ((tid & 31) == 0) {
+      red_m[tid >> 5] = m;
+      red_s[tid >> 5] = s;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      float mm = tid < nw ? red_m[tid] : -INFINITY;
+      float ss = tid < nw ? red_s[tid] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+        online_merge(mm, ss, m2, s2);
+      }
+      if (tid == 0) {
+        bm = mm;
+        bs = ss;
+      }
+    }
+    __syncthreads();
+    const float mx = bm, sum = bs;
+    const int32_t t = targets[r];
+    const bool bad = t < 0 || t >= classes;
+    if (tid == 0) {
+      if (bad) set_device_error(err, kDevErrBadIndex);
+      const float xt = bad ? mx : to_f32(row[t]);
+      losses[r] = -((xt - mx) - logf(sum));
+    }
+    __syncthreads();  // row[t] read before it is overwritten
+    const float inv = 1.0f / sum;
+    for (int vi = tid; vi < nvec; vi += blockDim.x) {
+      float v[8];
+      load8(row + vi * 8, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = vi * 8 + i;
+        v[i] = c < classes ? grad_scale * (expf(v[i] - mx) * inv - (c == t ? 1.f : 0.f)) : 0.f;
+      }
+      store8(row + vi * 8, v);
+    }
+    __syncthreads();
+  }
+}
+
 // Small class counts: one warp per row.
 template <typename T>
 __global__ void ce_warp_kernel(T* __restrict__ logits, const int32_t* __restrict__ targets,
@@ -338,6 +427,16 @@ magma_status_t magma_cross_entropy_fwd_bwd(void* logits, const int32_t* targets,
     else
       ce_warp_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((__nv_bfloat16*)logits, targets, losses,
                                                       rows, (int)classes, ld, grad_scale, err);
+  } else if (ld % 8 == 0 && aligned16(logits)) {
+    int64_t g = rows;
+    const int64_t cap = 4LL * num_sms();
+    if (g > cap) g = cap;
+    if (dtype == MAGMA_DTYPE_F32)
+      ce_block_vec_kernel<float><<<(int)g, 512, 0, s>>>((float*)logits, targets, losses, rows,
+                                                        (int)classes, ld, grad_scale, err);
+    else
+      ce_block_vec_kernel<__nv_bfloat16><<<(int)g, 512, 0, s>>>(
+          (__nv_bfloat16*)logits, targets, losses, rows, (int)classes, ld, grad_scale, err);
   } else {
     int64_t g = rows;
     int64_t cap = 16LL * num_sms();

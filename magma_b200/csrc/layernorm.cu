@@ -10,12 +10,14 @@
 // forward (vjpDivide/vjpSqrt/vjpMeanDims/vjpMultiply with sumAlongBroadcastDims,
 // Sources/Core/Autodiff.swift:57-94,221-257,351-370; Optimizer.swift:627-633).
 //
-// Both kernels are HBM-bound row kernels: one warp per row, 8 elements per
-// lane per step via 128-bit loads (BF16) or 2x128-bit loads (F32), the row held
-// in registers between the reduction and the store, warp-shuffle reductions in
-// a fixed butterfly order (deterministic). dgamma/dbeta are reduced per CTA in
-// shared memory in warp order, written as per-CTA partial rows to the caller's
-// workspace, then summed over CTAs in CTA order by a second kernel.
+// Both kernels are HBM-bound row kernels: a warp owns whole rows (two at a
+// time, their loads issued before any arithmetic), 8 elements per lane per
+// step via 128-bit loads (BF16) or 2x128-bit loads (F32), rows held in
+// registers between the reduction and the store, warp-shuffle reductions in a
+// fixed butterfly order (deterministic). dgamma/dbeta are accumulated per warp
+// in shared memory, summed over the CTA's warps in warp order into per-CTA
+// partial rows in the caller's workspace, then over CTAs in CTA order by a
+// second kernel.
 #include <mutex>
 
 #include "common.cuh"
@@ -27,65 +29,72 @@ constexpr int kWarps = 8;            // warps per CTA (one row per warp at a tim
 constexpr int kMaxChunks = 4;        // cached 8-element chunks per lane: D <= 1024
 constexpr int kMaxBwdBlocks = 592;   // cap on per-CTA partial rows (4 x 148 SMs)
 
-template <typename TX, typename TY>
+// D = 8*32*CPL' (CPL' <= CPL chunks per lane), RPW rows per warp: the loads of
+// all RPW rows are issued before any reduction so each warp keeps
+// RPW x 8 x CPL elements in flight (memory-level parallelism for an
+// HBM-bound kernel with one wave of warps).
+template <int CPL, int RPW, typename TX, typename TY>
 __global__ void __launch_bounds__(kWarps * 32)
-ln_fwd_cached(const TX* __restrict__ x, const float* __restrict__ gamma,
-              const float* __restrict__ beta, TY* __restrict__ y, float* __restrict__ mean_out,
-              float* __restrict__ rstd_out, int64_t rows, int dim, float eps) {
+ln_fwd_rows(const TX* __restrict__ x, const float* __restrict__ gamma,
+            const float* __restrict__ beta, TY* __restrict__ y, float* __restrict__ mean_out,
+            float* __restrict__ rstd_out, int64_t rows, int dim, float eps) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int chunks = dim >> 3;
-  const float inv_d = 1.0f / (float)dim;
-  (void)inv_d;
-  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
-       row += (int64_t)gridDim.x * kWarps) {
-    const TX* xr = x + row * dim;
-    float v[kMaxChunks][8];
-    float s = 0.f;
+  for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + warp) * RPW; r0 < rows;
+       r0 += (int64_t)gridDim.x * kWarps * RPW) {
+    float v[RPW][CPL][8];
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      int chunk = lane + c * 32;
-      if (chunk < chunks) {
-        load8(xr + chunk * 8, v[c]);
+    for (int q = 0; q < RPW; ++q) {
+      const int64_t row = r0 + q;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) s += v[c][i];
+      for (int c = 0; c < CPL; ++c) {
+        const int chunk = lane + c * 32;
+        if (row < rows && chunk < chunks) load8(x + row * dim + chunk * 8, v[q][c]);
       }
     }
-    s = warp_sum(s);
-    const float mean = __fdiv_rn(s, (float)dim);
-    float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      int chunk = lane + c * 32;
-      if (chunk < chunks) {
+    for (int q = 0; q < RPW; ++q) {
+      const int64_t row = r0 + q;
+      if (row >= rows) break;
+      float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float d = __fsub_rn(v[c][i], mean);
-          v[c][i] = d;
-          ss += d * d;
+      for (int c = 0; c < CPL; ++c)
+        if (lane + c * 32 < chunks)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) s += v[q][c][i];
+      s = warp_sum(s);
+      const float mean = __fdiv_rn(s, (float)dim);
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c)
+        if (lane + c * 32 < chunks)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float d = __fsub_rn(v[q][c][i], mean);
+            v[q][c][i] = d;
+            ss += d * d;
+          }
+      ss = warp_sum(ss);
+      const float stdv = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+      TY* yr = y + row * dim;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int chunk = lane + c * 32;
+        if (chunk < chunks) {
+          float g[8], b[8], o[8];
+          load8(gamma + chunk * 8, g);
+          load8(beta + chunk * 8, b);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            o[i] = __fadd_rn(__fmul_rn(__fdiv_rn(v[q][c][i], stdv), g[i]), b[i]);
+          store8(yr + chunk * 8, o);
         }
       }
-    }
-    ss = warp_sum(ss);
-    const float var = __fdiv_rn(ss, (float)dim);
-    const float stdv = __fsqrt_rn(__fadd_rn(var, eps));
-    TY* yr = y + row * dim;
-#pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      int chunk = lane + c * 32;
-      if (chunk < chunks) {
-        float g[8], b[8], o[8];
-        load8(gamma + chunk * 8, g);
-        load8(beta + chunk * 8, b);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          o[i] = __fadd_rn(__fmul_rn(__fdiv_rn(v[c][i], stdv), g[i]), b[i]);
-        store8(yr + chunk * 8, o);
+      if (lane == 0) {
+        if (mean_out) mean_out[row] = mean;
+        if (rstd_out) rstd_out[row] = __fdiv_rn(1.0f, stdv);
       }
-    }
-    if (lane == 0) {
-      if (mean_out) mean_out[row] = mean;
-      if (rstd_out) rstd_out[row] = __fdiv_rn(1.0f, stdv);
     }
   }
 }
@@ -124,97 +133,95 @@ ln_fwd_generic(const TX* __restrict__ x, const float* __restrict__ gamma,
   }
 }
 
-// Backward, D % 8 == 0 and D <= 1024. Per-CTA dgamma/dbeta partials go to
-// part[blockIdx.x][0..D) (dgamma) and part[blockIdx.x][D..2D) (dbeta).
-template <typename TDY, typename TX, typename TDX>
-__global__ void __launch_bounds__(kWarps * 32)
-ln_bwd_cached(const TDY* __restrict__ dy, const TX* __restrict__ x,
-              const float* __restrict__ gamma, const float* __restrict__ mean_in,
-              const float* __restrict__ rstd_in, TDX* __restrict__ dx,
-              float* __restrict__ part, int64_t rows, int dim, int accumulate_dx) {
-  extern __shared__ float smem[];  // [2*dim]
+// Backward, D % 8 == 0, D <= 256*CPL: RPW rows per warp with their loads
+// issued up front; each warp accumulates its dgamma/dbeta partials in its own
+// shared-memory row (no atomics), the 8 warp rows are then summed in warp
+// order into the CTA's partial row part[blockIdx.x] = [dgamma | dbeta].
+template <int CPL, int RPW, typename TDY, typename TX, typename TDX>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+ln_bwd_rows(const TDY* __restrict__ dy, const TX* __restrict__ x,
+            const float* __restrict__ gamma, const float* __restrict__ mean_in,
+            const float* __restrict__ rstd_in, TDX* __restrict__ dx,
+            float* __restrict__ part, int64_t rows, int dim, int accumulate_dx) {
+  extern __shared__ float smem[];  // [kWarps][2*dim]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int chunks = dim >> 3;
-  float pg[kMaxChunks][8], pb[kMaxChunks][8];
+  float* wp = smem + (size_t)warp * 2 * dim;
+  for (int i = lane; i < 2 * dim; i += 32) wp[i] = 0.f;
+  __syncwarp();
+  for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + warp) * RPW; r0 < rows;
+       r0 += (int64_t)gridDim.x * kWarps * RPW) {
+    float xv[RPW][CPL][8], dv[RPW][CPL][8];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
+    for (int q = 0; q < RPW; ++q) {
+      const int64_t row = r0 + q;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pg[c][i] = pb[c][i] = 0.f;
-
-  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
-       row += (int64_t)gridDim.x * kWarps) {
-    const float mean = mean_in[row];
-    const float rstd = rstd_in[row];
-    float xh[kMaxChunks][8], g[kMaxChunks][8];
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      int chunk = lane + c * 32;
-      if (chunk < chunks) {
-        float xv[8], dv[8], gm[8];
-        load8(x + row * dim + chunk * 8, xv);
-        load8(dy + row * dim + chunk * 8, dv);
-        load8(gamma + chunk * 8, gm);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float xhat = (xv[i] - mean) * rstd;
-          float gg = dv[i] * gm[i];
-          xh[c][i] = xhat;
-          g[c][i] = gg;
-          s1 += gg;
-          s2 += gg * xhat;
-          pg[c][i] += dv[i] * xhat;
-          pb[c][i] += dv[i];
+      for (int c = 0; c < CPL; ++c) {
+        const int chunk = lane + c * 32;
+        if (row < rows && chunk < chunks) {
+          load8(x + row * dim + chunk * 8, xv[q][c]);
+          load8(dy + row * dim + chunk * 8, dv[q][c]);
         }
       }
     }
-    s1 = warp_sum(s1) / (float)dim;
-    s2 = warp_sum(s2) / (float)dim;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      int chunk = lane + c * 32;
-      if (chunk < chunks) {
-        float o[8];
+    for (int q = 0; q < RPW; ++q) {
+      const int64_t row = r0 + q;
+      if (row >= rows) break;
+      const float mean = mean_in[row];
+      const float rstd = rstd_in[row];
+      float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = rstd * (g[c][i] - s1 - xh[c][i] * s2);
-        TDX* dst = dx + row * dim + chunk * 8;
-        if (accumulate_dx) {
-          float prev[8];
-          load8(dst, prev);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] += prev[i];
-        }
-        store8(dst, o);
-      }
-    }
-  }
-  // Deterministic CTA reduction of the per-lane partials: warps add into
-  // shared memory one after another, in warp order.
-  for (int w = 0; w < kWarps; ++w) {
-    if (warp == w) {
-#pragma unroll
-      for (int c = 0; c < kMaxChunks; ++c) {
-        int chunk = lane + c * 32;
+      for (int c = 0; c < CPL; ++c) {
+        const int chunk = lane + c * 32;
         if (chunk < chunks) {
+          float gm[8];
+          load8(gamma + chunk * 8, gm);
+          float* pg = wp + chunk * 8;
+          float* pb = wp + dim + chunk * 8;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            int col = chunk * 8 + i;
-            if (w == 0) {
-              smem[col] = pg[c][i];
-              smem[dim + col] = pb[c][i];
-            } else {
-              smem[col] += pg[c][i];
-              smem[dim + col] += pb[c][i];
-            }
+            const float xhat = (xv[q][c][i] - mean) * rstd;
+            const float gg = dv[q][c][i] * gm[i];
+            pg[i] += dv[q][c][i] * xhat;
+            pb[i] += dv[q][c][i];
+            xv[q][c][i] = xhat;
+            dv[q][c][i] = gg;
+            s1 += gg;
+            s2 += gg * xhat;
           }
         }
       }
+      s1 = warp_sum(s1) / (float)dim;
+      s2 = warp_sum(s2) / (float)dim;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int chunk = lane + c * 32;
+        if (chunk < chunks) {
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = rstd * (dv[q][c][i] - s1 - xv[q][c][i] * s2);
+          TDX* dst = dx + row * dim + chunk * 8;
+          if (accumulate_dx) {
+            float prev[8];
+            load8(dst, prev);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] += prev[i];
+          }
+          store8(dst, o);
+        }
+      }
     }
-    __syncthreads();
   }
+  __syncthreads();
   float* out = part + (int64_t)blockIdx.x * 2 * dim;
-  for (int i = threadIdx.x; i < 2 * dim; i += blockDim.x) out[i] = smem[i];
+  for (int i = threadIdx.x; i < 2 * dim; i += blockDim.x) {
+    float t = smem[i];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) t += smem[(size_t)w * 2 * dim + i];
+    out[i] = t;
+  }
 }
 
 template <typename TDY, typename TX, typename TDX>
@@ -298,6 +305,37 @@ int bwd_blocks(int64_t rows) {
   return (int)b;
 }
 
+// Launches ln_bwd_rows; *blocks (in: upper bound on the CTA count the caller's
+// partial buffer holds; out: CTAs launched = partial rows written).
+template <typename TDY, typename TX, typename TDX>
+magma_status_t launch_bwd_rows(const void* dy, const void* x, const float* gamma,
+                               const float* mean, const float* rstd, void* dx, int64_t rows,
+                               int dim, int acc_dx, float* part, int* blocks,
+                               cudaStream_t stream) {
+  int64_t b = ceil_div(rows, kWarps * 2);
+  const int64_t cap = 2LL * num_sms();
+  if (b > cap) b = cap;
+  if (b > *blocks) b = *blocks;
+  if (b < 1) b = 1;
+  *blocks = (int)b;
+  const size_t smem = (size_t)kWarps * 2 * dim * sizeof(float);
+  const int cpl = (dim + 255) / 256;
+#define LN_BWD_ROWS(C)                                                                         \
+  do {                                                                                         \
+    auto kern = ln_bwd_rows<C, (C <= 3 ? 2 : 1), TDY, TX, TDX>;                                \
+    if (smem > 48 * 1024)                                                                      \
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
+    kern<<<(int)b, kWarps * 32, smem, stream>>>((const TDY*)dy, (const TX*)x, gamma, mean, rstd, \
+                                                 (TDX*)dx, part, rows, dim, acc_dx);           \
+  } while (0)
+  if (cpl == 1) LN_BWD_ROWS(1);
+  else if (cpl == 2) LN_BWD_ROWS(2);
+  else if (cpl == 3) LN_BWD_ROWS(3);
+  else LN_BWD_ROWS(4);
+#undef LN_BWD_ROWS
+  return check_launch("layernorm_bwd");
+}
+
 template <typename TX, typename TY>
 magma_status_t launch_fwd(const void* x, const float* gamma, const float* beta, void* y,
                           float* mean, float* rstd, int64_t rows, int dim, float eps,
@@ -307,10 +345,23 @@ magma_status_t launch_fwd(const void* x, const float* gamma, const float* beta, 
   if (blocks > cap) blocks = cap;
   bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(y) &&
              aligned16(gamma) && aligned16(beta);
-  if (vec)
-    ln_fwd_cached<TX, TY><<<(int)blocks, kWarps * 32, 0, stream>>>(
-        (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
-  else
+  if (vec) {
+    const int cpl = (dim + 255) / 256;
+    int64_t b2 = ceil_div(rows, kWarps * 2);
+    if (b2 > cap) b2 = cap;
+    if (cpl == 1)
+      ln_fwd_rows<1, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
+          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
+    else if (cpl == 2)
+      ln_fwd_rows<2, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
+          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
+    else if (cpl == 3)
+      ln_fwd_rows<3, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
+          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
+    else
+      ln_fwd_rows<4, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
+          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
+  } else
     ln_fwd_generic<TX, TY><<<(int)blocks, kWarps * 32, 0, stream>>>(
         (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
   return check_launch("layernorm_fwd");
@@ -325,9 +376,9 @@ magma_status_t launch_bwd(const void* dy, const void* x, const float* gamma, con
   bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(dy) &&
              aligned16(dx) && aligned16(gamma);
   if (vec) {
-    size_t smem = 2 * (size_t)dim * sizeof(float);
-    ln_bwd_cached<TDY, TX, TDX><<<blocks, kWarps * 32, smem, stream>>>(
-        (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
+    if (magma_status_t st = launch_bwd_rows<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, rows, dim,
+                                                          acc_dx, part, &blocks, stream))
+      return st;
   } else {
     ln_bwd_generic<TDY, TX, TDX><<<blocks, kWarps * 32, 0, stream>>>(
         (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
@@ -386,9 +437,9 @@ magma_status_t launch_bwd_noalloc(const void* dy, const void* x, const float* ga
   const bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(dy) &&
                    aligned16(dx) && aligned16(gamma);
   if (vec) {
-    const size_t smem = 2 * (size_t)dim * sizeof(float);
-    ln_bwd_cached<TDY, TX, TDX><<<blocks, kWarps * 32, smem, stream>>>(
-        (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
+    if (magma_status_t st = launch_bwd_rows<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, rows, dim,
+                                                          acc_dx, part, &blocks, stream))
+      return st;
   } else {
     ln_bwd_generic<TDY, TX, TDX><<<blocks, kWarps * 32, 0, stream>>>(
         (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);

@@ -123,24 +123,35 @@ def physical_gpu(local: int) -> int:
 
 # ----------------------------------------------------------------- instrumentation
 def instrumented_step(trainer, lib, torch):
-    """One eager forward+backward+Adam with CUDA events around every library
-    call; returns per-kind times (ms), algorithmic work and launch counts."""
+    """Forward+backward+Adam captured as one CUDA graph with a timing event
+    record node before and after every library call; the graph is replayed and
+    the device time of each call read back (no host launch gaps, so small
+    kernels are timed as the real step runs them). Returns per-kind times (ms),
+    algorithmic work and launch counts."""
     rec = []
     orig = lib.call
 
     def timed_call(name, *args):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s = torch.cuda.Event(enable_timing=True, external=True)
+        e = torch.cuda.Event(enable_timing=True, external=True)
         s.record()
         orig(name, *args)
         e.record()
         rec.append((name, args, s, e))
 
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
     lib.call = timed_call
     try:
-        trainer.step_fwd_bwd()
-        trainer.optimizer_step()
+        with torch.cuda.graph(g, stream=side):
+            trainer.step_fwd_bwd()
+            trainer.optimizer_step()
     finally:
         lib.call = orig
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(2):
+        g.replay()
     torch.cuda.synchronize()
     cfg = trainer.cfg
     out = {}

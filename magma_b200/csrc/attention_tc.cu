@@ -275,17 +275,25 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       const int k0 = j * kTile;
       const bool diag = a.causal && (k0 + kTile > q0);
       const bool tail = k0 + kTile > a.S;
+      // Only the diagonal tile (causal) and a ragged last tile need masking;
+      // every other tile takes the mask-free loops (warp-uniform branch).
+      const bool masked_tile = diag || tail;
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
         tmem_ld32(srow + c * 32, v);
         tmem_wait_ld();
+        if (!masked_tile) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kg = k0 + c * 32 + e;
-          const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
-          if (!masked) mx = fmaxf(mx, __uint_as_float(v[e]));
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int kg = k0 + c * 32 + e;
+            const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
+            if (!masked) mx = fmaxf(mx, __uint_as_float(v[e]));
+          }
         }
       }
       const float m_new = fmaxf(m_run, mx * sl2);
@@ -300,12 +308,20 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         tmem_ld32(srow + c * 32, v);
         tmem_wait_ld();
         float p[32];
+        if (!masked_tile) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kg = k0 + c * 32 + e;
-          const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
-          p[e] = masked ? 0.f : ex2_approx(__uint_as_float(v[e]) * sl2 - m_use);
-          rs += p[e];
+          for (int e = 0; e < 32; ++e) {
+            p[e] = ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -m_use));
+            rs += p[e];
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int kg = k0 + c * 32 + e;
+            const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
+            p[e] = masked ? 0.f : ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -m_use));
+            rs += p[e];
+          }
         }
         store_row32(sP(sb), r, c, p);
       }
@@ -480,23 +496,40 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       if (!mbar_wait(st_full, (uint32_t)(i & 1), a.err)) { ok = false; break; }
       tc_fence_after();
       const bool diag = a.causal && (q0 < k0 + kTile);
-      const bool tail = q0 + kTile > a.S || kg >= a.S;
+      const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
+      const bool masked_tile = diag || tail;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t vs[32], vd[32];
         tmem_ld32(tST + lane_off + c * 32, vs);
         tmem_ld32(tDPT + lane_off + c * 32, vd);
+        float ls[32], dl[32];
+        const float4* l4 = reinterpret_cast<const float4*>(lse_s + st * kTile + c * 32);
+        const float4* d4 = reinterpret_cast<const float4*>(delta_s + st * kTile + c * 32);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 lv = l4[j], dv4 = d4[j];
+          ls[4 * j] = lv.x; ls[4 * j + 1] = lv.y; ls[4 * j + 2] = lv.z; ls[4 * j + 3] = lv.w;
+          dl[4 * j] = dv4.x; dl[4 * j + 1] = dv4.y; dl[4 * j + 2] = dv4.z; dl[4 * j + 3] = dv4.w;
+        }
         tmem_wait_ld();
         float p[32], ds[32];
+        if (!masked_tile) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int ql = c * 32 + e;
-          const int qg = q0 + ql;
-          const bool masked = (diag && qg < kg) || (tail && (qg >= a.S || kg >= a.S));
-          const float pe =
-              masked ? 0.f : ex2_approx(__uint_as_float(vs[e]) * sl2 - lse_s[st * kTile + ql]);
-          p[e] = pe;
-          ds[e] = pe * (__uint_as_float(vd[e]) - delta_s[st * kTile + ql]);
+          for (int e = 0; e < 32; ++e) {
+            const float pe = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[e]));
+            p[e] = pe;
+            ds[e] = pe * (__uint_as_float(vd[e]) - dl[e]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qg = q0 + c * 32 + e;
+            const bool masked = (diag && qg < kg) || (tail && (qg >= a.S || kg >= a.S));
+            const float pe = masked ? 0.f : ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[e]));
+            p[e] = pe;
+            ds[e] = pe * (__uint_as_float(vd[e]) - dl[e]);
+          }
         }
         store_row32(sPT, r, c, p);
         store_row32(sDST, r, c, ds);
@@ -665,7 +698,8 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       if (!mbar_wait(s_full, (uint32_t)(j & 1), a.err)) { ok = false; break; }
       tc_fence_after();
       const bool diag = a.causal && (k0 + kTile > q0);
-      const bool tail = k0 + kTile > a.S;
+      const bool tail = k0 + kTile > a.S || q0 + kTile > a.S;
+      const bool masked_tile = diag || tail;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t vs[32], vd[32];
@@ -673,12 +707,20 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tmem_ld32(tDP + lane_off + c * 32, vd);
         tmem_wait_ld();
         float ds[32];
+        if (!masked_tile) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kg = k0 + c * 32 + e;
-          const bool masked = (diag && kg > qg) || (tail && kg >= a.S) || qg >= a.S;
-          const float pe = masked ? 0.f : ex2_approx(__uint_as_float(vs[e]) * sl2 - lse2);
-          ds[e] = pe * (__uint_as_float(vd[e]) - dl);
+          for (int e = 0; e < 32; ++e) {
+            const float pe = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -lse2));
+            ds[e] = pe * (__uint_as_float(vd[e]) - dl);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int kg = k0 + c * 32 + e;
+            const bool masked = (diag && kg > qg) || (tail && kg >= a.S) || qg >= a.S;
+            const float pe = masked ? 0.f : ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -lse2));
+            ds[e] = pe * (__uint_as_float(vd[e]) - dl);
+          }
         }
         store_row32(sDS, r, c, ds);
       }

@@ -27,6 +27,9 @@
 // TMA cannot describe.
 #include <cuda.h>
 
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -163,25 +166,37 @@ gemm_simt_kernel(const TA* __restrict__ A, const TA* __restrict__ B, TC* __restr
 
 // ============================ tcgen05 BF16 kernel ============================
 constexpr int kBM = 128, kBK = 64;
-constexpr int kGemmThreads = 192;
+// warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue (two warps per
+// TMEM lane quarter, each owning half of the tile's columns)
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 32 * (2 + kEpiWarps);
 
-template <int BN>
+// BN = N extent of one MMA tile. PAIR: a cluster of two CTAs issues one
+// M=256 MMA (cta_group::2); each CTA holds 128 rows of A, BN/2 rows of B and a
+// 128 x BN accumulator in its own TMEM.
+template <int BN, bool PAIR>
 struct TcCfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;
   static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  // Epilogue staging: per epilogue warp a 32 x 64 F32 chunk, row pitch 66 floats
-  // (8-byte aligned rows; conflict-free 8-byte stores by row and loads by column pair).
-  static constexpr int kStageOffset = kStages * kStageBytes;
-  static constexpr int kStagePitch = 66;
+  // Epilogue staging: per epilogue warp a 32 x 32 F32 chunk, row pitch 34
+  // floats (8-byte aligned rows; conflict-free 8-byte stores by row and
+  // 8-byte loads by column pair).
+  static constexpr int kStagePitch = 34;
   static constexpr int kStageWarpFloats = 32 * kStagePitch;
-  static constexpr int kStagingBytes = 4 * kStageWarpFloats * 4;
+  static constexpr int kStagingBytes = kEpiWarps * kStageWarpFloats * 4;
+  static constexpr int kSmemLimit = 232448;  // sm_100 dynamic shared memory per block
+  static constexpr int kReserve = kStagingBytes + 1024 + 256;  // staging, alignment, barriers
+  static constexpr int kStagesFit = (kSmemLimit - kReserve) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kStageOffset = kStages * kStageBytes;
   static constexpr int kBarOffset = kStageOffset + kStagingBytes;
   // full[S], empty[S], tfull[2], tempty[2], done -> 8 B each; then TMEM slot.
   static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
-  static_assert(kSmemBytes <= 232448, "GEMM shared memory exceeds the sm_100 per-block limit");
+  static_assert(kStages >= 3, "GEMM pipeline too shallow");
+  static_assert(kSmemBytes <= kSmemLimit, "GEMM shared memory exceeds the sm_100 per-block limit");
   static constexpr int kTmemCols = 2 * BN;
 };
 
@@ -271,9 +286,16 @@ __device__ __forceinline__ void direct_store64(TO* dst_row, const float* bias, i
     for (int i = 0; i < 8; ++i)
       v[i] = __uint_as_float(g < 4 ? ra[8 * g + i] : rb[8 * (g - 4) + i]);
     if (bias != nullptr) {
+      if (vec8 && col + 8 <= N && (reinterpret_cast<uintptr_t>(bias + col) & 15u) == 0) {
+        float bv[8];
+        load8(bias + col, bv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (col + i < N) v[i] = __fadd_rn(v[i], bias[col + i]);
+        for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(v[i], bv[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (col + i < N) v[i] = __fadd_rn(v[i], bias[col + i]);
+      }
     }
     if (vec8 && col + 8 <= N) {
       store8(dst_row + col, v);
@@ -285,39 +307,40 @@ __device__ __forceinline__ void direct_store64(TO* dst_row, const float* bias, i
   }
 }
 
-// One 64-column chunk of one warp's 32 tile rows, lane = column pair
-// (col, col+1). st points at this lane's pair in row 0 of the staged F32
-// accumulators (row pitch P). The epilogue is a template parameter (no
-// per-row branches) and every auxiliary load of the 32 rows is issued before
-// the first store so their latencies overlap.
+// One 32-column chunk of one warp's 32 tile rows: this lane handles the
+// column pair (col, col+1) of rows rsel, rsel+2, ..., st points at that pair
+// in row rsel of the staged F32 accumulators (row pitch P). The epilogue is a
+// template parameter (no per-row branches) and every auxiliary load is issued
+// before the first store so their latencies overlap.
 template <typename TC, int EPI, int P>
 __device__ __forceinline__ void epi_rows(const TcArgs& a, const float* __restrict__ st,
-                                         int64_t row0, int rows_here, int64_t col, float b0,
-                                         float b1) {
+                                         int64_t row0, int rows_here, int rsel, int64_t col,
+                                         float b0, float b1) {
   constexpr bool kAux = EPI == MAGMA_EPI_BIAS_RESIDUAL || EPI == MAGMA_EPI_DGELU ||
                         EPI == MAGMA_EPI_DRELU || EPI == MAGMA_EPI_ACCUMULATE;
   const int64_t ldc = a.e.ldc;
-  const int64_t base = row0 * ldc + col;
+  const int64_t base = (row0 + rsel) * ldc + col;
   TC* c = static_cast<TC*>(a.C) + base;
-  float x0[32], x1[32];
+  float x0[16], x1[16];
   if constexpr (kAux) {
 #pragma unroll
-    for (int rr = 0; rr < 32; ++rr) {
-      x0[rr] = x1[rr] = 0.f;
-      if (rr < rows_here) {
+    for (int i = 0; i < 16; ++i) {
+      x0[i] = x1[i] = 0.f;
+      if (2 * i + rsel < rows_here) {
+        const int64_t off = base + 2 * i * ldc;
         if constexpr (EPI == MAGMA_EPI_BIAS_RESIDUAL)
-          load2(static_cast<const float*>(a.e.aux_in) + base + rr * ldc, x0[rr], x1[rr]);
+          load2(static_cast<const float*>(a.e.aux_in) + off, x0[i], x1[i]);
         else if constexpr (EPI == MAGMA_EPI_ACCUMULATE)
-          load2(c + rr * ldc, x0[rr], x1[rr]);
+          load2(c + 2 * i * ldc, x0[i], x1[i]);
         else
-          load2(static_cast<const TC*>(a.e.aux_in) + base + rr * ldc, x0[rr], x1[rr]);
+          load2(static_cast<const TC*>(a.e.aux_in) + off, x0[i], x1[i]);
       }
     }
   }
 #pragma unroll
-  for (int rr = 0; rr < 32; ++rr) {
-    if (rr < rows_here) {
-      const float2 v = *reinterpret_cast<const float2*>(st + rr * P);
+  for (int i = 0; i < 16; ++i) {
+    if (2 * i + rsel < rows_here) {
+      const float2 v = *reinterpret_cast<const float2*>(st + 2 * i * P);
       float o0, o1;
       if constexpr (EPI == MAGMA_EPI_NONE) {
         o0 = v.x;
@@ -326,11 +349,11 @@ __device__ __forceinline__ void epi_rows(const TcArgs& a, const float* __restric
         o0 = __fadd_rn(v.x, b0);
         o1 = __fadd_rn(v.y, b1);
       } else if constexpr (EPI == MAGMA_EPI_BIAS_RESIDUAL) {
-        o0 = __fadd_rn(x0[rr], __fadd_rn(v.x, b0));
-        o1 = __fadd_rn(x1[rr], __fadd_rn(v.y, b1));
+        o0 = __fadd_rn(x0[i], __fadd_rn(v.x, b0));
+        o1 = __fadd_rn(x1[i], __fadd_rn(v.y, b1));
       } else if constexpr (EPI == MAGMA_EPI_BIAS_GELU || EPI == MAGMA_EPI_BIAS_RELU) {
         const float p0 = __fadd_rn(v.x, b0), p1 = __fadd_rn(v.y, b1);
-        store2(static_cast<TC*>(a.e.aux_out) + base + rr * ldc, p0, p1);
+        store2(static_cast<TC*>(a.e.aux_out) + base + 2 * i * ldc, p0, p1);
         if constexpr (EPI == MAGMA_EPI_BIAS_GELU) {
           o0 = gelu_t<TC>(p0);
           o1 = gelu_t<TC>(p1);
@@ -339,25 +362,26 @@ __device__ __forceinline__ void epi_rows(const TcArgs& a, const float* __restric
           o1 = fmaxf(p1, 0.f);
         }
       } else if constexpr (EPI == MAGMA_EPI_DGELU) {
-        o0 = __fmul_rn(v.x, gelu_grad_t<TC>(x0[rr]));
-        o1 = __fmul_rn(v.y, gelu_grad_t<TC>(x1[rr]));
+        o0 = __fmul_rn(v.x, gelu_grad_t<TC>(x0[i]));
+        o1 = __fmul_rn(v.y, gelu_grad_t<TC>(x1[i]));
       } else if constexpr (EPI == MAGMA_EPI_DRELU) {
-        o0 = x0[rr] > 0.f ? v.x : 0.f;
-        o1 = x1[rr] > 0.f ? v.y : 0.f;
+        o0 = x0[i] > 0.f ? v.x : 0.f;
+        o1 = x1[i] > 0.f ? v.y : 0.f;
       } else {  // ACCUMULATE
-        o0 = __fadd_rn(x0[rr], v.x);
-        o1 = __fadd_rn(x1[rr], v.y);
+        o0 = __fadd_rn(x0[i], v.x);
+        o1 = __fadd_rn(x1[i], v.y);
       }
-      store2(c + rr * ldc, o0, o1);
+      store2(c + 2 * i * ldc, o0, o1);
     }
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, typename TC>
+template <int BN, bool A_MN, bool B_MN, typename TC, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                TcArgs args) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, PAIR>;
+  constexpr int kTM = PAIR ? 2 * kBM : kBM;  // output rows per tile
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = sm100::smem_u32(smem_raw);
@@ -375,11 +399,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t M = args.M, N = args.N, K = args.K;
-  const int tiles_m = (int)((M + kBM - 1) / kBM);
+  const int tiles_m = (int)((M + kTM - 1) / kTM);
   const int tiles_n = (int)((N + BN - 1) / BN);
   const int num_tiles = tiles_m * tiles_n;
   const int num_units = num_tiles * args.splits;
   const int kblocks = (int)((K + kBK - 1) / kBK);
+  const uint32_t rank = PAIR ? sm100::cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int ustart = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     sm100::prefetch_tensormap(&tmA);
@@ -390,14 +418,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       sm100::mbar_init(tfull_bar(a), 1);
-      sm100::mbar_init(tempty_bar(a), 4);
+      sm100::mbar_init(tempty_bar(a), PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     sm100::mbar_init(done_bar, 1);
     sm100::fence_barrier_init();
   }
-  if (warp == 1) sm100::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  if (warp == 1) {
+    if constexpr (PAIR) sm100::tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    else sm100::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  }
   sm100::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) sm100::cluster_sync();  // peer barriers initialised before any remote use
   sm100::tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr);
 
@@ -406,30 +438,35 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+    auto load = [&](uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+      if constexpr (PAIR) sm100::tma_load_2d_pair(dst, map, x, y, sm100::mapa_shared(bar, 0));
+      else sm100::tma_load_2d(dst, map, x, y, bar);
+    };
+    for (int unit = ustart; unit < num_units && ok; unit += ustride) {
       const int tile = unit % num_tiles, split = unit / num_tiles;
-      const int m0 = (tile % tiles_m) * kBM;
-      const int n0 = (tile / tiles_m) * BN;
+      const int a_row0 = (tile % tiles_m) * kTM + (int)rank * kBM;
+      const int b_row0 = (tile / tiles_m) * BN + (int)rank * Cfg::kBRows;
       const int kb0 = split * args.kb_per_split;
       const int kb1 = min(kblocks, kb0 + args.kb_per_split);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!sm100::mbar_wait(empty_bar(stage), phase ^ 1u, args.err)) { ok = false; break; }
         const uint32_t sa = base + stage * Cfg::kStageBytes;
         const uint32_t sb = sa + Cfg::kABytes;
-        sm100::mbar_expect_tx(full_bar(stage), Cfg::kStageBytes);
+        // the leader's full barrier counts both CTAs' bytes
+        if (leader) sm100::mbar_expect_tx(full_bar(stage), (PAIR ? 2 : 1) * Cfg::kStageBytes);
         if (!A_MN) {
-          sm100::tma_load_2d(sa, &tmA, kb * kBK, m0, full_bar(stage));
+          load(sa, &tmA, kb * kBK, a_row0, full_bar(stage));
         } else {
 #pragma unroll
           for (int j = 0; j < kBM / 64; ++j)
-            sm100::tma_load_2d(sa + j * 8192, &tmA, m0 + j * 64, kb * kBK, full_bar(stage));
+            load(sa + j * 8192, &tmA, a_row0 + j * 64, kb * kBK, full_bar(stage));
         }
         if (!B_MN) {
-          sm100::tma_load_2d(sb, &tmB, kb * kBK, n0, full_bar(stage));
+          load(sb, &tmB, kb * kBK, b_row0, full_bar(stage));
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            sm100::tma_load_2d(sb + j * 8192, &tmB, n0 + j * 64, kb * kBK, full_bar(stage));
+          for (int j = 0; j < Cfg::kBRows / 64; ++j)
+            load(sb + j * 8192, &tmB, b_row0 + j * 64, kb * kBK, full_bar(stage));
         }
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
@@ -440,15 +477,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!sm100::mbar_wait(empty_bar(stage), phase ^ 1u, args.err)) ok = false;
       if (++stage == S) { stage = 0; phase ^= 1u; }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1 && lane == 0 && leader) {
     // ----------------------------- MMA issuer -----------------------------
-    constexpr uint32_t idesc = sm100::idesc_bf16_f32(kBM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+    constexpr uint32_t idesc = sm100::idesc_bf16_f32(kTM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+    auto commit = [&](uint32_t bar) {
+      if constexpr (PAIR) sm100::mma_commit_pair(bar, 0x3);  // arrive in both CTAs
+      else sm100::mma_commit(bar);
+    };
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+    for (int unit = ustart; unit < num_units && ok; unit += ustride) {
       const int split = unit / num_tiles;
       const int kb0 = split * args.kb_per_split;
       const int kb1 = min(kblocks, kb0 + args.kb_per_split);
@@ -470,31 +511,40 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint64_t bdesc =
               B_MN ? sm100::smem_desc_sw128(sb + kk * 2048, 8192, 1024)
                    : sm100::smem_desc_sw128(sb + kk * 32, 16, 1024);
-          sm100::mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          if constexpr (PAIR)
+            sm100::mma_bf16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          else
+            sm100::mma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
         }
-        sm100::mma_commit(empty_bar(stage));
+        commit(empty_bar(stage));
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
       if (!ok) break;
-      sm100::mma_commit(tfull_bar(acc));
+      commit(tfull_bar(acc));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
     // Wait for every MMA this thread issued before TMEM is released.
-    sm100::mma_commit(done_bar);
+    commit(done_bar);
+    sm100::mbar_wait(done_bar, 0, args.err);
+  } else if (PAIR && warp == 1 && lane == 0) {
+    // non-leader: the leader's MMAs write this CTA's TMEM; wait for all of them
     sm100::mbar_wait(done_bar, 0, args.err);
   } else if (warp >= 2) {
     // ------------------------------ epilogue ------------------------------
-    // A warp owns TMEM lanes [32q, 32q+32) = tile rows. Per 64-column chunk:
-    // tcgen05.ld (thread = row) -> padded smem stage -> lanes take column
-    // pairs and walk the 32 rows, so each global access of the warp is one
-    // contiguous row segment (bias / residual / pre-activation reads and the
-    // stores alike).
+    // Warp w owns TMEM lane quarter q = w & 3 (tile rows [32q, 32q+32)) and
+    // column half h = (w - 2) / 4. Plain / bias epilogues and split-K partials:
+    // thread = row, 16-byte stores. Epilogues that read auxiliary tensors or
+    // write two outputs: per 32-column chunk the accumulators go through a
+    // padded shared-memory stage, then each lane takes a column pair of one of
+    // two rows, so every global access is a contiguous row segment, and all
+    // auxiliary loads of the chunk are issued before the first store.
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int kCols = BN / 2;  // columns per epilogue warp
     float* stage = reinterpret_cast<float*>(base_ptr + Cfg::kStageOffset) +
                    (warp - 2) * Cfg::kStageWarpFloats;
     const bool vec2 = args.vec_ok != 0;
-    const bool ws_pair = (N % 2) == 0;
     const bool ws_vec8 = (N % 8) == 0;
     const bool c_vec8 = args.vec8_ok != 0;
     const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
@@ -504,28 +554,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                            args.e.epi == MAGMA_EPI_BIAS_RESIDUAL || args.e.epi == MAGMA_EPI_BIAS_RELU);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+    for (int unit = ustart; unit < num_units; unit += ustride) {
       const int tile = unit % num_tiles, split = unit / num_tiles;
-      const int m0 = (tile % tiles_m) * kBM;
-      const int n0 = (tile / tiles_m) * BN;
+      const int m0 = (tile % tiles_m) * kTM + (int)rank * kBM;
+      const int n0 = (tile / tiles_m) * BN + half * kCols;
       if (!sm100::mbar_wait(tfull_bar(acc), acc_phase, args.err)) break;
       sm100::tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) +
+                             (uint32_t)(half * kCols);
       const int64_t row0 = (int64_t)m0 + q * 32;
       const int rows_here = (int)min((int64_t)32, M - row0);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 64) {
-        uint32_t ra[32], rb[32];
-        sm100::tmem_ld32(taddr + c0, ra);
-        sm100::tmem_ld32(taddr + c0 + 32, rb);
-        sm100::tmem_wait_ld();
-        if (c0 + 64 >= BN) {
-          // last TMEM read of this accumulator: hand it back to the MMA warp
-          sm100::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) sm100::mbar_arrive(tempty_bar(acc));
+      auto release = [&]() {  // last TMEM read of this accumulator by this warp
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR) sm100::mbar_arrive_cluster(sm100::mapa_shared(tempty_bar(acc), 0));
+          else sm100::mbar_arrive(tempty_bar(acc));
         }
-        if (direct) {
+      };
+      if (direct) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < kCols; c0 += 64) {
+          uint32_t ra[32], rb[32];
+          sm100::tmem_ld32(taddr + c0, ra);
+          sm100::tmem_ld32(taddr + c0 + 32, rb);
+          sm100::tmem_wait_ld();
+          if (c0 + 64 >= kCols) release();
           const int64_t row = row0 + lane;
           if (row < M && n0 + c0 < N) {
             if (args.splits > 1)
@@ -536,58 +590,50 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                  has_bias ? args.e.bias : nullptr, (int64_t)n0 + c0, N, ra, rb,
                                  c_vec8);
           }
-          continue;
         }
-        float* srow = stage + lane * Cfg::kStagePitch;
+      } else {
+        constexpr int P = Cfg::kStagePitch;
+        const int cp = lane & 15;     // column pair within the chunk
+        const int rsel = lane >> 4;   // row parity handled by this lane
+#pragma unroll 1
+        for (int c0 = 0; c0 < kCols; c0 += 32) {
+          uint32_t ra[32];
+          sm100::tmem_ld32(taddr + c0, ra);
+          sm100::tmem_wait_ld();
+          if (c0 + 32 >= kCols) release();
+          float* srow = stage + lane * P;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          *reinterpret_cast<float2*>(srow + 2 * j) =
-              make_float2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
-          *reinterpret_cast<float2*>(srow + 32 + 2 * j) =
-              make_float2(__uint_as_float(rb[2 * j]), __uint_as_float(rb[2 * j + 1]));
-        }
-        __syncwarp();
-        const int64_t col = (int64_t)n0 + c0 + 2 * lane;
-        if (col < N && rows_here > 0) {
-          const bool pair = col + 1 < N;
-          float b0 = 0.f, b1 = 0.f;
-          if (has_bias) {
-            b0 = args.e.bias[col];
-            b1 = pair ? args.e.bias[col + 1] : 0.f;
-          }
-          const float* st = stage + 2 * lane;
-          constexpr int P = Cfg::kStagePitch;
-          if (args.splits > 1) {
-            float* dst = args.ws + (int64_t)split * M * N + row0 * N + col;
-#pragma unroll 8
-            for (int rr = 0; rr < rows_here; ++rr) {
-              const float2 v = *reinterpret_cast<const float2*>(st + rr * P);
-              if (pair && ws_pair) {
-                *reinterpret_cast<float2*>(dst + (int64_t)rr * N) = v;
-              } else {
-                dst[(int64_t)rr * N] = v.x;
-                if (pair) dst[(int64_t)rr * N + 1] = v.y;
+          for (int j = 0; j < 16; ++j)
+            *reinterpret_cast<float2*>(srow + 2 * j) =
+                make_float2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
+          __syncwarp();
+          const int64_t col = (int64_t)n0 + c0 + 2 * cp;
+          if (col < N && rows_here > 0) {
+            const bool pair = col + 1 < N;
+            float b0 = 0.f, b1 = 0.f;
+            if (has_bias) {
+              b0 = args.e.bias[col];
+              b1 = pair ? args.e.bias[col + 1] : 0.f;
+            }
+            const float* st = stage + rsel * P + 2 * cp;
+            if (pair && vec2) {
+              switch (args.e.epi) {
+                case MAGMA_EPI_BIAS_GELU: epi_rows<TC, MAGMA_EPI_BIAS_GELU, P>(args, st, row0, rows_here, rsel, col, b0, b1); break;
+                case MAGMA_EPI_BIAS_RESIDUAL: epi_rows<TC, MAGMA_EPI_BIAS_RESIDUAL, P>(args, st, row0, rows_here, rsel, col, b0, b1); break;
+                case MAGMA_EPI_DGELU: epi_rows<TC, MAGMA_EPI_DGELU, P>(args, st, row0, rows_here, rsel, col, b0, b1); break;
+                case MAGMA_EPI_ACCUMULATE: epi_rows<TC, MAGMA_EPI_ACCUMULATE, P>(args, st, row0, rows_here, rsel, col, b0, b1); break;
+                case MAGMA_EPI_BIAS_RELU: epi_rows<TC, MAGMA_EPI_BIAS_RELU, P>(args, st, row0, rows_here, rsel, col, b0, b1); break;
+                default: epi_rows<TC, MAGMA_EPI_DRELU, P>(args, st, row0, rows_here, rsel, col, b0, b1); break;
+              }
+            } else {
+              for (int rr = rsel; rr < rows_here; rr += 2) {
+                const float2 v = *reinterpret_cast<const float2*>(st + (rr - rsel) * P);
+                epi_store2<TC>(args, row0 + rr, col, v.x, v.y, b0, b1, false);
               }
             }
-          } else if (pair && vec2) {
-            switch (args.e.epi) {
-              case MAGMA_EPI_NONE: epi_rows<TC, MAGMA_EPI_NONE, P>(args, st, row0, rows_here, col, b0, b1); break;
-              case MAGMA_EPI_BIAS: epi_rows<TC, MAGMA_EPI_BIAS, P>(args, st, row0, rows_here, col, b0, b1); break;
-              case MAGMA_EPI_BIAS_GELU: epi_rows<TC, MAGMA_EPI_BIAS_GELU, P>(args, st, row0, rows_here, col, b0, b1); break;
-              case MAGMA_EPI_BIAS_RESIDUAL: epi_rows<TC, MAGMA_EPI_BIAS_RESIDUAL, P>(args, st, row0, rows_here, col, b0, b1); break;
-              case MAGMA_EPI_DGELU: epi_rows<TC, MAGMA_EPI_DGELU, P>(args, st, row0, rows_here, col, b0, b1); break;
-              case MAGMA_EPI_ACCUMULATE: epi_rows<TC, MAGMA_EPI_ACCUMULATE, P>(args, st, row0, rows_here, col, b0, b1); break;
-              case MAGMA_EPI_BIAS_RELU: epi_rows<TC, MAGMA_EPI_BIAS_RELU, P>(args, st, row0, rows_here, col, b0, b1); break;
-              default: epi_rows<TC, MAGMA_EPI_DRELU, P>(args, st, row0, rows_here, col, b0, b1); break;
-            }
-          } else {
-            for (int rr = 0; rr < rows_here; ++rr) {
-              const float2 v = *reinterpret_cast<const float2*>(st + rr * P);
-              epi_store2<TC>(args, row0 + rr, col, v.x, v.y, b0, b1, false);
-            }
           }
+          __syncwarp();
         }
-        __syncwarp();
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
@@ -595,10 +641,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
   sm100::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) sm100::cluster_sync();
   if (warp == 1) {
     __syncwarp();
     sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR) sm100::tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else sm100::tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -606,33 +654,59 @@ struct TcPlan {
   int bn;
   int splits;
   int kb_per_split;
+  bool pair;
 };
 
-// Picks the tile width BN and the K-split count from a cost model: the time of
-// a persistent launch is (waves over the SMs) x (k-blocks per unit) x (cost
-// of one k-block: BN=128 is ~15% less efficient per FLOP than BN=256), plus,
-// when splitting, the HBM time to write and re-read the F32 partials.
+// Override for measurements: MAGMA_GEMM_MODE = 1sm | 2sm | 1sm128 | 1sm256 |
+// 2sm128 | 2sm256 restricts the plan to those tile options (default: all).
+// Returns a bit mask over the options {1sm128, 1sm256, 2sm128, 2sm256}.
+int gemm_option_mask() {
+  static int mask = [] {
+    const char* v = getenv("MAGMA_GEMM_MODE");
+    if (v == nullptr) return 0xF;
+    if (strcmp(v, "1sm") == 0) return 0x3;
+    if (strcmp(v, "2sm") == 0) return 0xC;
+    if (strcmp(v, "1sm128") == 0) return 0x1;
+    if (strcmp(v, "1sm256") == 0) return 0x2;
+    if (strcmp(v, "2sm128") == 0) return 0x4;
+    if (strcmp(v, "2sm256") == 0) return 0x8;
+    return 0xF;
+  }();
+  return mask;
+}
+
+// Picks CTA pairing, tile width BN and the K-split count from a cost model:
+// the time of a persistent launch is (waves over the SMs, or over SM pairs)
+// x (k-blocks per unit) x (time of one k-block for that tile shape, measured),
+// plus, when splitting, the HBM time to write and re-read the F32 partials.
 TcPlan choose_plan(int64_t M, int64_t N, int64_t K) {
   const int sms = num_sms();
   const int kblocks = (int)ceil_div(K, kBK);
-  const double kb_us[2] = {0.27 * 0.5 * 1.15, 0.27};  // BN=128, BN=256 (one k-block)
-  TcPlan best{256, 1, kblocks};
+  // us per k-block (64 deep) of one unit: 1-CTA 128x128, 1-CTA 128x256,
+  // pair 256x128, pair 256x256
+  const double kb_us[4] = {0.375, 0.6, 0.34, 0.5};
+  const int allowed = gemm_option_mask();
+  TcPlan best{256, 1, kblocks, false};
   double best_t = 1e30;
-  for (int bi = 1; bi >= 0; --bi) {
-    const int bn = bi ? 256 : 128;
-    const int64_t tiles = ceil_div(M, kBM) * ceil_div(N, bn);
+  for (int opt = 3; opt >= 0; --opt) {
+    const bool pair = opt >= 2;
+    if (!(allowed & (1 << opt))) continue;
+    if (pair && M < 256) continue;
+    const int bn = (opt & 1) ? 256 : 128;
+    const int64_t tiles = ceil_div(M, pair ? 256 : kBM) * ceil_div(N, bn);
+    const int slots = pair ? sms / 2 : sms;
     for (int s = 1; s <= 16; ++s) {
       const int kbps = (int)ceil_div(kblocks, s);
       if (s > 1 && kbps < 4) break;
       const int splits = (int)ceil_div(kblocks, kbps);
       if (splits != s) continue;
       const int64_t units = tiles * splits;
-      const double waves = (double)ceil_div(units, sms);
-      double t = waves * kbps * kb_us[bi] + 2.0;
+      const double waves = (double)ceil_div(units, slots);
+      double t = waves * kbps * kb_us[opt] + 2.0;
       if (splits > 1) t += (double)(splits + 1) * M * N * 4.0 / 5.0e6;  // bytes / (5 TB/s) in us
       if (t < best_t * 0.97) {
         best_t = t;
-        best = {bn, splits, kbps};
+        best = {bn, splits, kbps, pair};
       }
     }
   }
@@ -656,11 +730,11 @@ splitk_reduce(const float* __restrict__ ws, int splits, int64_t M, int64_t N, TC
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, typename TC>
+template <int BN, bool A_MN, bool B_MN, typename TC, bool PAIR>
 magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                          int64_t lda, int64_t ldb, const TcArgs& args, cudaStream_t stream) {
   static_assert(BN == 128 || BN == 256, "BN");
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, PAIR>;
   CUtensorMap ta, tb;
   magma_status_t st;
   if (!A_MN)
@@ -671,13 +745,13 @@ magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int
                               CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   if (!B_MN)
-    st = encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, ldb * 2, 64, BN,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
+    st = encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, K, N, ldb * 2, 64,
+                              Cfg::kBRows, CU_TENSOR_MAP_SWIZZLE_128B);
   else
     st = encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, N, K, ldb * 2, 64, 64,
                               CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, TC>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, TC, PAIR>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -688,10 +762,30 @@ magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int
       return s2;
     attr_set[dev] = true;
   }
-  const int64_t units = ceil_div(M, kBM) * ceil_div(N, BN) * args.splits;
-  int grid = num_sms();
-  if (units < grid) grid = (int)units;
-  kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, args);
+  const int64_t units = ceil_div(M, PAIR ? 2 * kBM : kBM) * ceil_div(N, BN) * args.splits;
+  if constexpr (PAIR) {
+    int pairs = num_sms() / 2;
+    if (units < pairs) pairs = (int)units;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (magma_status_t st = cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, args),
+                                        "gemm_tcgen05_pair launch"))
+      return st;
+  } else {
+    int grid = num_sms();
+    if (units < grid) grid = (int)units;
+    kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, args);
+  }
   if (magma_status_t st = check_launch("gemm_tcgen05")) return st;
   if (args.splits > 1) {
     int64_t blocks = ceil_div(M * N, 256);
@@ -703,16 +797,27 @@ magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int
   return MAGMA_OK;
 }
 
-template <int BN, typename TC>
+template <int BN, typename TC, bool PAIR>
 magma_status_t dispatch_major(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
                               int64_t lda, int64_t ldb, int ta, int tb, const TcArgs& args,
                               cudaStream_t s) {
   const bool a_mn = ta != 0;   // A stored [K, M]
   const bool b_mn = tb == 0;   // B stored [K, N]
-  if (!a_mn && !b_mn) return launch_tc<BN, false, false, TC>(a, b, M, N, K, lda, ldb, args, s);
-  if (!a_mn && b_mn) return launch_tc<BN, false, true, TC>(a, b, M, N, K, lda, ldb, args, s);
-  if (a_mn && !b_mn) return launch_tc<BN, true, false, TC>(a, b, M, N, K, lda, ldb, args, s);
-  return launch_tc<BN, true, true, TC>(a, b, M, N, K, lda, ldb, args, s);
+  if (!a_mn && !b_mn) return launch_tc<BN, false, false, TC, PAIR>(a, b, M, N, K, lda, ldb, args, s);
+  if (!a_mn && b_mn) return launch_tc<BN, false, true, TC, PAIR>(a, b, M, N, K, lda, ldb, args, s);
+  if (a_mn && !b_mn) return launch_tc<BN, true, false, TC, PAIR>(a, b, M, N, K, lda, ldb, args, s);
+  return launch_tc<BN, true, true, TC, PAIR>(a, b, M, N, K, lda, ldb, args, s);
+}
+
+template <typename TC>
+magma_status_t dispatch_plan(const TcPlan& plan, const void* a, const void* b, int64_t M,
+                             int64_t N, int64_t K, int64_t lda, int64_t ldb, int ta, int tb,
+                             const TcArgs& args, cudaStream_t s) {
+  if (plan.pair)
+    return plan.bn == 256 ? dispatch_major<256, TC, true>(a, b, M, N, K, lda, ldb, ta, tb, args, s)
+                          : dispatch_major<128, TC, true>(a, b, M, N, K, lda, ldb, ta, tb, args, s);
+  return plan.bn == 256 ? dispatch_major<256, TC, false>(a, b, M, N, K, lda, ldb, ta, tb, args, s)
+                        : dispatch_major<128, TC, false>(a, b, M, N, K, lda, ldb, ta, tb, args, s);
 }
 
 template <typename TA, typename TC>
@@ -784,18 +889,13 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
     // Split-K only with a large enough caller workspace; otherwise one pass.
     const size_t need = plan.splits > 1 ? (size_t)plan.splits * m * n * sizeof(float) : 0;
     if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
-      plan = {plan.bn, 1, (int)ceil_div(k, kBK)};
+      plan = {plan.bn, 1, (int)ceil_div(k, kBK), plan.pair};
     const int vec8_ok = (ldc % 8) == 0 && aligned16(c);
     TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, vec8_ok, plan.splits,
                 plan.kb_per_split, static_cast<float*>(workspace)};
-    const int bn = plan.bn;
-    if (bn == 256)
-      return c32 ? dispatch_major<256, float>(a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
-                 : dispatch_major<256, __nv_bfloat16>(a, b, m, n, k, lda, ldb, trans_a, trans_b,
-                                                      args, s);
-    return c32 ? dispatch_major<128, float>(a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
-               : dispatch_major<128, __nv_bfloat16>(a, b, m, n, k, lda, ldb, trans_a, trans_b,
-                                                    args, s);
+    return c32 ? dispatch_plan<float>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
+               : dispatch_plan<__nv_bfloat16>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b,
+                                              args, s);
   }
   if (ab_dtype == MAGMA_DTYPE_F32)
     return c32 ? launch_simt<float, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e, s)

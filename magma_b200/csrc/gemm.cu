@@ -27,6 +27,7 @@
 // TMA cannot describe.
 #include <cuda.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 
@@ -660,35 +661,80 @@ struct TcPlan {
 // Override for measurements: MAGMA_GEMM_MODE = 1sm | 2sm | 1sm128 | 1sm256 |
 // 2sm128 | 2sm256 restricts the plan to those tile options (default: all).
 // Returns a bit mask over the options {1sm128, 1sm256, 2sm128, 2sm256}.
+// MAGMA_GEMM_MODE restricts the plan search (1sm, 2sm, 1sm128, 1sm256,
+// 2sm128, 2sm256); read on every call so a process can compare options.
 int gemm_option_mask() {
-  static int mask = [] {
-    const char* v = getenv("MAGMA_GEMM_MODE");
-    if (v == nullptr) return 0xF;
-    if (strcmp(v, "1sm") == 0) return 0x3;
-    if (strcmp(v, "2sm") == 0) return 0xC;
-    if (strcmp(v, "1sm128") == 0) return 0x1;
-    if (strcmp(v, "1sm256") == 0) return 0x2;
-    if (strcmp(v, "2sm128") == 0) return 0x4;
-    if (strcmp(v, "2sm256") == 0) return 0x8;
-    return 0xF;
-  }();
-  return mask;
+  const char* v = getenv("MAGMA_GEMM_MODE");
+  if (v == nullptr) return 0xF;
+  if (strcmp(v, "1sm") == 0) return 0x3;
+  if (strcmp(v, "2sm") == 0) return 0xC;
+  if (strcmp(v, "1sm128") == 0) return 0x1;
+  if (strcmp(v, "1sm256") == 0) return 0x2;
+  if (strcmp(v, "2sm128") == 0) return 0x4;
+  if (strcmp(v, "2sm256") == 0) return 0x8;
+  return 0xF;
 }
 
-// Picks CTA pairing, tile width BN and the K-split count from a cost model:
-// the time of a persistent launch is (waves over the SMs, or over SM pairs)
-// x (k-blocks per unit) x (time of one k-block for that tile shape, measured),
-// plus, when splitting, the HBM time to write and re-read the F32 partials.
-TcPlan choose_plan(int64_t M, int64_t N, int64_t K) {
+// MAGMA_GEMM_PLAN="pair,bn,splits" (e.g. "1,256,3") fixes the plan outright;
+// ignored when it does not fit the shape.
+bool forced_plan(int64_t M, int64_t K, TcPlan* out) {
+  const char* v = getenv("MAGMA_GEMM_PLAN");
+  if (v == nullptr) return false;
+  int pair = 0, bn = 0, splits = 0;
+  if (sscanf(v, "%d,%d,%d", &pair, &bn, &splits) != 3) return false;
+  if ((bn != 128 && bn != 256) || splits < 1 || (pair && M < 256)) return false;
+  const int kblocks = (int)ceil_div(K, kBK);
+  const int kbps = (int)ceil_div(kblocks, splits);
+  *out = {bn, (int)ceil_div(kblocks, kbps), kbps, pair != 0};
+  return true;
+}
+
+// Epilogue cost inputs of the plan model: bytes moved per output element
+// (C plus the auxiliary tensor it reads or writes) and issue time per output
+// element (us per 10^4 elements of one CTA's tile).
+struct EpiCost {
+  double bytes;
+  double us_1e4;
+};
+EpiCost epi_cost(int epi, bool c32) {
+  const double c = c32 ? 4.0 : 2.0;
+  switch (epi) {
+    case MAGMA_EPI_BIAS_RESIDUAL: return {c + 4.0, 1.71};
+    case MAGMA_EPI_BIAS_GELU:
+    case MAGMA_EPI_BIAS_RELU: return {2.0 * c, 2.33};
+    case MAGMA_EPI_DGELU:
+    case MAGMA_EPI_DRELU: return {2.0 * c, 3.60};
+    case MAGMA_EPI_ACCUMULATE: return {2.0 * c, 2.33};
+    default: return {c, c32 ? 2.53 : 1.95};   // direct row stores
+  }
+}
+
+// Picks CTA pairing, tile width BN and the K-split count from a cost model
+// fitted to measured B200 times of every option on the GPT-2 training shapes:
+// a unit (one output tile, or one K-slice of it) costs the largest of its
+// tensor-core time (k-blocks x time per 64-deep k-block), its L2->SMEM load
+// time plus output traffic at the per-SM L2 bandwidth, and its epilogue (the
+// epilogue of one tile overlaps the next tile's main loop); the launch costs
+// waves x unit + one exposed epilogue, plus the cluster set-up for CTA pairs
+// and, when splitting, the reduce pass over the F32 partials.
+TcPlan choose_plan(int64_t M, int64_t N, int64_t K, int epi, bool c32) {
+  TcPlan forced;
+  if (forced_plan(M, K, &forced)) return forced;
   const int sms = num_sms();
   const int kblocks = (int)ceil_div(K, kBK);
-  // us per k-block (64 deep) of one unit: 1-CTA 128x128, 1-CTA 128x256,
-  // pair 256x128, pair 256x256
-  const double kb_us[4] = {0.375, 0.6, 0.34, 0.5};
+  // per option {1-CTA 128x128, 1-CTA 128x256, pair 256x128, pair 256x256}:
+  const double kb_us[4] = {0.300, 0.515, 0.311, 0.335};    // tensor time per k-block
+  const double kb_bytes[4] = {32768, 49152, 24576, 32768};  // SMEM fill per k-block per CTA
+  const double l2_bytes_per_us[4] = {96.0e3, 94.7e3, 75.5e3, 87.9e3};  // per SM
+  const double pair_setup_us = 1.8, split_setup_us = 0.26, reduce_bytes_per_us = 2.87e6;
+  const EpiCost ec = epi_cost(epi, c32);
+  const EpiCost ep = epi_cost(MAGMA_EPI_NONE, true);  // F32 partial stores
   const int allowed = gemm_option_mask();
-  TcPlan best{256, 1, kblocks, false};
-  double best_t = 1e30;
-  for (int opt = 3; opt >= 0; --opt) {
+  // Best unsplit and best split plan; a split plan has to win by 10% (it
+  // also costs workspace traffic the model does not see in the next kernel).
+  TcPlan best1{256, 1, kblocks, false}, bests{256, 1, kblocks, false};
+  double t1 = 1e30, ts = 1e30;
+  for (int opt = 0; opt < 4; ++opt) {
     const bool pair = opt >= 2;
     if (!(allowed & (1 << opt))) continue;
     if (pair && M < 256) continue;
@@ -700,16 +746,28 @@ TcPlan choose_plan(int64_t M, int64_t N, int64_t K) {
       if (s > 1 && kbps < 4) break;
       const int splits = (int)ceil_div(kblocks, kbps);
       if (splits != s) continue;
-      const int64_t units = tiles * splits;
-      const double waves = (double)ceil_div(units, slots);
-      double t = waves * kbps * kb_us[opt] + 2.0;
-      if (splits > 1) t += (double)(splits + 1) * M * N * 4.0 / 5.0e6;  // bytes / (5 TB/s) in us
-      if (t < best_t * 0.97) {
-        best_t = t;
-        best = {bn, splits, kbps, pair};
+      const EpiCost& e = splits > 1 ? ep : ec;
+      const double elems = (double)kBM * bn;  // output elements per CTA tile
+      const double epi_us = e.us_1e4 * elems * 1e-4;
+      const double load_us = (kbps * kb_bytes[opt] + e.bytes * elems) / l2_bytes_per_us[opt];
+      double unit = kbps * kb_us[opt];
+      if (load_us > unit) unit = load_us;
+      if (epi_us > unit) unit = epi_us;
+      const double waves = (double)ceil_div(tiles * splits, slots);
+      double t = waves * unit + epi_us + (pair ? pair_setup_us : 0.0);
+      if (splits > 1) {
+        t += split_setup_us + ((splits + 1) * 4.0 + ec.bytes) * M * N / reduce_bytes_per_us;
+        if (t < ts) {
+          ts = t;
+          bests = {bn, splits, kbps, pair};
+        }
+      } else if (t < t1) {
+        t1 = t;
+        best1 = {bn, 1, kbps, pair};
       }
     }
   }
+  const TcPlan best = ts < 0.9 * t1 ? bests : best1;
   return best;
 }
 
@@ -717,16 +775,43 @@ TcPlan choose_plan(int64_t M, int64_t N, int64_t K) {
 template <typename TC>
 __global__ void __launch_bounds__(256)
 splitk_reduce(const float* __restrict__ ws, int splits, int64_t M, int64_t N, TC* __restrict__ C,
-              EpiArgs e) {
-  const int64_t total = M * N;
-  const int64_t plane = total;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float acc = ws[i];
-    for (int s = 1; s < splits; ++s) acc += ws[(int64_t)s * plane + i];
-    const int64_t row = i / N, col = i - row * N;
-    const int64_t off = row * e.ldc + col;
-    C[off] = from_f32<TC>(epi_value<TC>(e, C, off, col, acc));
+              EpiArgs e, int vec_c) {
+  // Thread = 4 consecutive columns of one row when N % 4 == 0 (16-byte loads
+  // of every partial plane), else one column. Planes are added in split order.
+  const int64_t plane = M * N;
+  const bool v4 = (N & 3) == 0;
+  const int64_t per_row = v4 ? N >> 2 : N;
+  for (int64_t row = blockIdx.y; row < M; row += gridDim.y) {
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < per_row;
+         c += (int64_t)gridDim.x * blockDim.x) {
+      if (v4) {
+        const int64_t i = row * N + c * 4;
+        float acc[4];
+        load4(ws + i, acc);
+        for (int sp = 1; sp < splits; ++sp) {
+          float t[4];
+          load4(ws + (int64_t)sp * plane + i, t);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc[k] += t[k];
+        }
+        const int64_t off = row * e.ldc + c * 4;
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = epi_value<TC>(e, C, off + k, c * 4 + k, acc[k]);
+        if (vec_c) {
+          store4(C + off, o);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) C[off + k] = from_f32<TC>(o[k]);
+        }
+      } else {
+        const int64_t i = row * N + c;
+        float acc = ws[i];
+        for (int sp = 1; sp < splits; ++sp) acc += ws[(int64_t)sp * plane + i];
+        const int64_t off = row * e.ldc + c;
+        C[off] = from_f32<TC>(epi_value<TC>(e, C, off, c, acc));
+      }
+    }
   }
 }
 
@@ -788,10 +873,15 @@ magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int
   }
   if (magma_status_t st = check_launch("gemm_tcgen05")) return st;
   if (args.splits > 1) {
-    int64_t blocks = ceil_div(M * N, 256);
-    if (blocks > 8LL * num_sms()) blocks = 8LL * num_sms();
-    splitk_reduce<TC><<<(int)blocks, 256, 0, stream>>>(args.ws, args.splits, M, N,
-                                                       static_cast<TC*>(args.C), args.e);
+    const int64_t per_row = (N & 3) == 0 ? N / 4 : N;
+    int64_t gx = ceil_div(per_row, 256);
+    if (gx > 16) gx = 16;
+    int64_t gy = (8LL * num_sms() + gx - 1) / gx;
+    if (gy > M) gy = M;
+    if (gy > 65535) gy = 65535;
+    const int vec_c = (args.e.ldc % 4) == 0 && aligned16(args.C);
+    splitk_reduce<TC><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, stream>>>(
+        args.ws, args.splits, M, N, static_cast<TC*>(args.C), args.e, vec_c);
     return check_launch("gemm_splitk_reduce");
   }
   return MAGMA_OK;
@@ -844,8 +934,18 @@ extern "C" {
 
 size_t magma_gemm_workspace_size(int64_t m, int64_t n, int64_t k, magma_dtype_t ab_dtype) {
   if (ab_dtype != MAGMA_DTYPE_BF16 || m <= 0 || n <= 0 || k <= 0) return 0;
-  const TcPlan p = choose_plan(m, n, k);
-  return p.splits > 1 ? (size_t)p.splits * (size_t)m * (size_t)n * sizeof(float) : 0;
+  // The plan depends on the epilogue and output type, which this query does
+  // not take: return the largest split workspace over the epilogue classes.
+  static const int kEpis[] = {MAGMA_EPI_NONE, MAGMA_EPI_BIAS_RESIDUAL, MAGMA_EPI_BIAS_GELU,
+                              MAGMA_EPI_DGELU};
+  size_t need = 0;
+  for (int epi : kEpis)
+    for (int c32 = 0; c32 < 2; ++c32) {
+      const TcPlan p = choose_plan(m, n, k, epi, c32 != 0);
+      const size_t w = p.splits > 1 ? (size_t)p.splits * (size_t)m * (size_t)n * sizeof(float) : 0;
+      if (w > need) need = w;
+    }
+  return need;
 }
 
 magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
@@ -885,7 +985,7 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
   if (tc_ok) {
     auto al8 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
     const int vec_ok = (ldc % 2) == 0 && al8(c) && al8(aux_in) && al8(aux_out);
-    TcPlan plan = choose_plan(m, n, k);
+    TcPlan plan = choose_plan(m, n, k, epilogue, c32);
     // Split-K only with a large enough caller workspace; otherwise one pass.
     const size_t need = plan.splits > 1 ? (size_t)plan.splits * m * n * sizeof(float) : 0;
     if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))

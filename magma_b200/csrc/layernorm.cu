@@ -10,91 +10,160 @@
 // forward (vjpDivide/vjpSqrt/vjpMeanDims/vjpMultiply with sumAlongBroadcastDims,
 // Sources/Core/Autodiff.swift:57-94,221-257,351-370; Optimizer.swift:627-633).
 //
-// Both kernels are HBM-bound row kernels: a warp owns whole rows (two at a
-// time, their loads issued before any arithmetic), 8 elements per lane per
-// step via 128-bit loads (BF16) or 2x128-bit loads (F32), rows held in
-// registers between the reduction and the store, warp-shuffle reductions in a
-// fixed butterfly order (deterministic). dgamma/dbeta are accumulated per warp
-// in shared memory, summed over the CTA's warps in warp order into per-CTA
-// partial rows in the caller's workspace, then over CTAs in CTA order by a
-// second kernel.
+// Both directions are HBM-bound row kernels. The main path (D % 8 == 0,
+// D <= 1024, 16-byte aligned rows) is a persistent grid of one CTA per SM in
+// which every warp streams its rows through a small ring of row buffers in
+// shared memory: lane 0 fills a buffer with untiled bulk copies
+// (cp.async.bulk) that complete on that buffer's mbarrier, so the next rows
+// of every warp are in flight while it reduces the current one. Lane l works
+// on the 4-element groups 4l + 128c of a row: 16-byte conflict-free shared
+// reads, 512-byte coalesced global stores per warp instruction. Reductions
+// are warp-shuffle butterflies in a fixed order (deterministic). dgamma/dbeta
+// partials stay in registers (each lane owns fixed columns), are summed over
+// the CTA's warps in warp order into one partial row per CTA in the caller's
+// workspace, then over CTAs in CTA order by a second kernel. Other shapes use
+// scalar generic kernels.
 #include <mutex>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace magma {
 namespace {
 
-constexpr int kWarps = 8;            // warps per CTA (one row per warp at a time)
-constexpr int kMaxChunks = 4;        // cached 8-element chunks per lane: D <= 1024
+using sm100::bulk_load;
+using sm100::fence_barrier_init;
+using sm100::mbar_expect_tx;
+using sm100::mbar_init;
+using sm100::mbar_wait;
+using sm100::smem_u32;
+
+constexpr int kWarps = 8;            // warps per CTA of the generic kernels
 constexpr int kMaxBwdBlocks = 592;   // cap on per-CTA partial rows (4 x 148 SMs)
 
-// D = 8*32*CPL' (CPL' <= CPL chunks per lane), RPW rows per warp: the loads of
-// all RPW rows are issued before any reduction so each warp keeps
-// RPW x 8 x CPL elements in flight (memory-level parallelism for an
-// HBM-bound kernel with one wave of warps).
-template <int CPL, int RPW, typename TX, typename TY>
-__global__ void __launch_bounds__(kWarps * 32)
-ln_fwd_rows(const TX* __restrict__ x, const float* __restrict__ gamma,
-            const float* __restrict__ beta, TY* __restrict__ y, float* __restrict__ mean_out,
-            float* __restrict__ rstd_out, int64_t rows, int dim, float eps) {
+// Row-streaming kernels.
+constexpr int kMaxGroups = 8;               // 4-element groups per lane: D <= 1024
+constexpr int kStreamSmem = 200 * 1024;     // dynamic shared memory for the rings
+constexpr int kBarBytes = 1024;             // mbarrier area at the start of it
+constexpr int kFwdRing = 3;                 // row buffers per warp, forward
+constexpr int kBwdRing = 2;                 // row buffers per warp, backward
+// Forward warps per CTA (128 registers per thread at 16; the widest rows,
+// G = 8, run 12).
+constexpr int fwd_max_warps(int groups) { return groups > 6 ? 12 : 16; }
+// Backward warps per CTA: 12 keep 170 registers per thread; the widest rows
+// (G = 8) need more and run 8 warps.
+constexpr int bwd_max_warps(int groups) { return groups > 6 ? 8 : 12; }
+
+bool stream_ok(int dim) { return dim % 8 == 0 && dim <= kMaxGroups * 128; }
+
+// Warps per CTA whose rings fit the shared-memory budget (0: none fit).
+int stream_warps(int ring, size_t row_bytes, int max_warps) {
+  int w = (int)((kStreamSmem - kBarBytes) / ((size_t)ring * row_bytes));
+  if (w > max_warps) w = max_warps;
+  if (w * ring * 8 > kBarBytes) w = kBarBytes / (ring * 8);
+  return w < 4 ? 0 : w;
+}
+
+// After a failed wait: one more bounded wait on each row copy still in flight
+// (rows j0 .. j1-1 of the warp) so the CTA does not leave while bulk copies
+// still target its shared memory.
+template <int RING>
+__device__ void drain_ring(const uint64_t* bars, int64_t j0, int64_t j1, int* err) {
+  for (int64_t k = j0; k < j1; ++k)
+    mbar_wait(smem_u32(bars + k % RING), (uint32_t)((k / RING) & 1), err);
+}
+
+// Forward, streaming: G 4-element groups per lane (D <= 128*G).
+template <int G, typename TX, typename TY>
+__global__ void __launch_bounds__(fwd_max_warps(G) * 32, 1)
+ln_fwd_stream(const TX* __restrict__ x, const float* __restrict__ gamma,
+              const float* __restrict__ beta, TY* __restrict__ y, float* __restrict__ mean_out,
+              float* __restrict__ rstd_out, int64_t rows, int dim, float eps, int* err) {
+  extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int chunks = dim >> 3;
-  for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + warp) * RPW; r0 < rows;
-       r0 += (int64_t)gridDim.x * kWarps * RPW) {
-    float v[RPW][CPL][8];
+  const int nwarps = blockDim.x >> 5;
+  const uint32_t row_bytes = (uint32_t)dim * sizeof(TX);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kFwdRing;
+  unsigned char* ring = smem + kBarBytes + (size_t)warp * kFwdRing * row_bytes;
+  const int64_t stride = (int64_t)gridDim.x * nwarps;
+  const int64_t first = (int64_t)blockIdx.x * nwarps + warp;
+  const int64_t n = first < rows ? (rows - first + stride - 1) / stride : 0;
+  if (lane == 0) {
+    for (int b = 0; b < kFwdRing; ++b) mbar_init(smem_u32(bars + b), 1);
+    fence_barrier_init();
+    for (int64_t j = 0; j < n && j < kFwdRing; ++j) {
+      const uint32_t bar = smem_u32(bars + j);
+      mbar_expect_tx(bar, row_bytes);
+      bulk_load(smem_u32(ring + j * row_bytes), x + (first + j * stride) * dim, row_bytes, bar);
+    }
+  }
+  __syncwarp();
+  float g[G][4], bt[G][4];
 #pragma unroll
-    for (int q = 0; q < RPW; ++q) {
-      const int64_t row = r0 + q;
+  for (int c = 0; c < G; ++c) {
+    const int e = 128 * c + 4 * lane;
+    if (e < dim) {
+      load4(gamma + e, g[c]);
+      load4(beta + e, bt[c]);
+    }
+  }
+  for (int64_t j = 0; j < n; ++j) {
+    const int slot = (int)(j % kFwdRing);
+    const int64_t row = first + j * stride;
+    if (!mbar_wait(smem_u32(bars + slot), (uint32_t)((j / kFwdRing) & 1), err)) {
+      drain_ring<kFwdRing>(bars, j, n < j + kFwdRing ? n : j + kFwdRing, err);
+      return;
+    }
+    const TX* src = reinterpret_cast<const TX*>(ring + slot * row_bytes);
+    float v[G][4];
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int chunk = lane + c * 32;
-        if (row < rows && chunk < chunks) load8(x + row * dim + chunk * 8, v[q][c]);
+    for (int c = 0; c < G; ++c) {
+      const int e = 128 * c + 4 * lane;
+      if (e < dim) load4(src + e, v[c]);
+    }
+    __syncwarp();
+    if (lane == 0 && j + kFwdRing < n) {
+      const uint32_t bar = smem_u32(bars + slot);
+      mbar_expect_tx(bar, row_bytes);
+      bulk_load(smem_u32(ring + slot * row_bytes), x + (row + kFwdRing * stride) * dim,
+                row_bytes, bar);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < G; ++c)
+      if (128 * c + 4 * lane < dim)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s += v[c][i];
+    s = warp_sum(s);
+    const float mean = __fdiv_rn(s, (float)dim);
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < G; ++c)
+      if (128 * c + 4 * lane < dim)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float d = __fsub_rn(v[c][i], mean);
+          v[c][i] = d;
+          ss += d * d;
+        }
+    ss = warp_sum(ss);
+    const float stdv = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+    TY* yr = y + row * dim;
+#pragma unroll
+    for (int c = 0; c < G; ++c) {
+      const int e = 128 * c + 4 * lane;
+      if (e < dim) {
+        float o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o[i] = __fadd_rn(__fmul_rn(__fdiv_rn(v[c][i], stdv), g[c][i]), bt[c][i]);
+        store4(yr + e, o);
       }
     }
-#pragma unroll
-    for (int q = 0; q < RPW; ++q) {
-      const int64_t row = r0 + q;
-      if (row >= rows) break;
-      float s = 0.f;
-#pragma unroll
-      for (int c = 0; c < CPL; ++c)
-        if (lane + c * 32 < chunks)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) s += v[q][c][i];
-      s = warp_sum(s);
-      const float mean = __fdiv_rn(s, (float)dim);
-      float ss = 0.f;
-#pragma unroll
-      for (int c = 0; c < CPL; ++c)
-        if (lane + c * 32 < chunks)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float d = __fsub_rn(v[q][c][i], mean);
-            v[q][c][i] = d;
-            ss += d * d;
-          }
-      ss = warp_sum(ss);
-      const float stdv = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
-      TY* yr = y + row * dim;
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int chunk = lane + c * 32;
-        if (chunk < chunks) {
-          float g[8], b[8], o[8];
-          load8(gamma + chunk * 8, g);
-          load8(beta + chunk * 8, b);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            o[i] = __fadd_rn(__fmul_rn(__fdiv_rn(v[q][c][i], stdv), g[i]), b[i]);
-          store8(yr + chunk * 8, o);
-        }
-      }
-      if (lane == 0) {
-        if (mean_out) mean_out[row] = mean;
-        if (rstd_out) rstd_out[row] = __fdiv_rn(1.0f, stdv);
-      }
+    if (lane == 0) {
+      if (mean_out) mean_out[row] = mean;
+      if (rstd_out) rstd_out[row] = __fdiv_rn(1.0f, stdv);
     }
   }
 }
@@ -133,93 +202,127 @@ ln_fwd_generic(const TX* __restrict__ x, const float* __restrict__ gamma,
   }
 }
 
-// Backward, D % 8 == 0, D <= 256*CPL: RPW rows per warp with their loads
-// issued up front; each warp accumulates its dgamma/dbeta partials in its own
-// shared-memory row (no atomics), the 8 warp rows are then summed in warp
-// order into the CTA's partial row part[blockIdx.x] = [dgamma | dbeta].
-template <int CPL, int RPW, typename TDY, typename TX, typename TDX>
-__global__ void __launch_bounds__(kWarps * 32, 2)
-ln_bwd_rows(const TDY* __restrict__ dy, const TX* __restrict__ x,
-            const float* __restrict__ gamma, const float* __restrict__ mean_in,
-            const float* __restrict__ rstd_in, TDX* __restrict__ dx,
-            float* __restrict__ part, int64_t rows, int dim, int accumulate_dx) {
-  extern __shared__ float smem[];  // [kWarps][2*dim]
+// Backward, streaming: each ring buffer holds [x | dy | dx] of one row (dx
+// only when accumulating into it). dgamma/dbeta partials live in registers
+// (lane l owns columns 4l + 128c) and are summed over the warps of the CTA in
+// warp order into part[blockIdx.x] = [dgamma | dbeta].
+template <int G, typename TDY, typename TX, typename TDX>
+__global__ void __launch_bounds__(bwd_max_warps(G) * 32, 1)
+ln_bwd_stream(const TDY* __restrict__ dy, const TX* __restrict__ x,
+              const float* __restrict__ gamma, const float* __restrict__ mean_in,
+              const float* __restrict__ rstd_in, TDX* __restrict__ dx,
+              float* __restrict__ part, int64_t rows, int dim, int accumulate_dx, int* err) {
+  extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int chunks = dim >> 3;
-  float* wp = smem + (size_t)warp * 2 * dim;
-  for (int i = lane; i < 2 * dim; i += 32) wp[i] = 0.f;
+  const int nwarps = blockDim.x >> 5;
+  const uint32_t bx = (uint32_t)dim * sizeof(TX);
+  const uint32_t bdy = (uint32_t)dim * sizeof(TDY);
+  const uint32_t bdx = accumulate_dx ? (uint32_t)dim * sizeof(TDX) : 0u;
+  const uint32_t stage = bx + bdy + bdx;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kBwdRing;
+  unsigned char* ring = smem + kBarBytes + (size_t)warp * kBwdRing * stage;
+  const int64_t stride = (int64_t)gridDim.x * nwarps;
+  const int64_t first = (int64_t)blockIdx.x * nwarps + warp;
+  const int64_t n = first < rows ? (rows - first + stride - 1) / stride : 0;
+  auto issue = [&](int slot, int64_t row) {
+    const uint32_t bar = smem_u32(bars + slot);
+    const uint32_t dst = smem_u32(ring + (size_t)slot * stage);
+    mbar_expect_tx(bar, stage);
+    bulk_load(dst, x + row * dim, bx, bar);
+    bulk_load(dst + bx, dy + row * dim, bdy, bar);
+    if (bdx) bulk_load(dst + bx + bdy, dx + row * dim, bdx, bar);
+  };
+  if (lane == 0) {
+    for (int b = 0; b < kBwdRing; ++b) mbar_init(smem_u32(bars + b), 1);
+    fence_barrier_init();
+    for (int64_t j = 0; j < n && j < kBwdRing; ++j) issue((int)j, first + j * stride);
+  }
   __syncwarp();
-  for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + warp) * RPW; r0 < rows;
-       r0 += (int64_t)gridDim.x * kWarps * RPW) {
-    float xv[RPW][CPL][8], dv[RPW][CPL][8];
+  float g[G][4], dg[G][4], db[G][4];
 #pragma unroll
-    for (int q = 0; q < RPW; ++q) {
-      const int64_t row = r0 + q;
+  for (int c = 0; c < G; ++c) {
+    const int e = 128 * c + 4 * lane;
+    if (e < dim) load4(gamma + e, g[c]);
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int chunk = lane + c * 32;
-        if (row < rows && chunk < chunks) {
-          load8(x + row * dim + chunk * 8, xv[q][c]);
-          load8(dy + row * dim + chunk * 8, dv[q][c]);
+    for (int i = 0; i < 4; ++i) dg[c][i] = db[c][i] = 0.f;
+  }
+  bool ok = true;
+  for (int64_t j = 0; j < n; ++j) {
+    const int slot = (int)(j % kBwdRing);
+    const int64_t row = first + j * stride;
+    const float mean = mean_in[row];
+    const float rstd = rstd_in[row];
+    if (!mbar_wait(smem_u32(bars + slot), (uint32_t)((j / kBwdRing) & 1), err)) {
+      drain_ring<kBwdRing>(bars, j, n < j + kBwdRing ? n : j + kBwdRing, err);
+      ok = false;
+      break;
+    }
+    const unsigned char* st = ring + (size_t)slot * stage;
+    const TX* xs = reinterpret_cast<const TX*>(st);
+    const TDY* dys = reinterpret_cast<const TDY*>(st + bx);
+    float xv[G][4], dv[G][4];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < G; ++c) {
+      const int e = 128 * c + 4 * lane;
+      if (e < dim) {
+        load4(xs + e, xv[c]);
+        load4(dys + e, dv[c]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float xhat = (xv[c][i] - mean) * rstd;
+          const float gg = dv[c][i] * g[c][i];
+          dg[c][i] += dv[c][i] * xhat;
+          db[c][i] += dv[c][i];
+          xv[c][i] = xhat;
+          dv[c][i] = gg;
+          s1 += gg;
+          s2 += gg * xhat;
         }
       }
     }
+    s1 = warp_sum(s1) / (float)dim;
+    s2 = warp_sum(s2) / (float)dim;
+    const float* dxs = reinterpret_cast<const float*>(st + bx + bdy);
+    TDX* dst = dx + row * dim;
 #pragma unroll
-    for (int q = 0; q < RPW; ++q) {
-      const int64_t row = r0 + q;
-      if (row >= rows) break;
-      const float mean = mean_in[row];
-      const float rstd = rstd_in[row];
-      float s1 = 0.f, s2 = 0.f;
+    for (int c = 0; c < G; ++c) {
+      const int e = 128 * c + 4 * lane;
+      if (e < dim) {
+        float o[4];
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int chunk = lane + c * 32;
-        if (chunk < chunks) {
-          float gm[8];
-          load8(gamma + chunk * 8, gm);
-          float* pg = wp + chunk * 8;
-          float* pb = wp + dim + chunk * 8;
+        for (int i = 0; i < 4; ++i) o[i] = rstd * (dv[c][i] - s1 - xv[c][i] * s2);
+        if (accumulate_dx) {
+          float prev[4];
+          load4(dxs + e, prev);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float xhat = (xv[q][c][i] - mean) * rstd;
-            const float gg = dv[q][c][i] * gm[i];
-            pg[i] += dv[q][c][i] * xhat;
-            pb[i] += dv[q][c][i];
-            xv[q][c][i] = xhat;
-            dv[q][c][i] = gg;
-            s1 += gg;
-            s2 += gg * xhat;
-          }
+          for (int i = 0; i < 4; ++i) o[i] += prev[i];
         }
+        store4(dst + e, o);
       }
-      s1 = warp_sum(s1) / (float)dim;
-      s2 = warp_sum(s2) / (float)dim;
+    }
+    __syncwarp();
+    if (lane == 0 && j + kBwdRing < n) issue(slot, row + kBwdRing * stride);
+  }
+  // This warp's ring (all its copies have landed) now holds its partials.
+  float* red = reinterpret_cast<float*>(ring);
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const int chunk = lane + c * 32;
-        if (chunk < chunks) {
-          float o[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] = rstd * (dv[q][c][i] - s1 - xv[q][c][i] * s2);
-          TDX* dst = dx + row * dim + chunk * 8;
-          if (accumulate_dx) {
-            float prev[8];
-            load8(dst, prev);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] += prev[i];
-          }
-          store8(dst, o);
-        }
-      }
+  for (int c = 0; c < G; ++c) {
+    const int e = 128 * c + 4 * lane;
+    if (e < dim) {
+      store4(red + e, dg[c]);
+      store4(red + dim + e, db[c]);
     }
   }
   __syncthreads();
+  if (!ok) return;
   float* out = part + (int64_t)blockIdx.x * 2 * dim;
+  const size_t wstride = (size_t)kBwdRing * stage / sizeof(float);
+  const float* base = reinterpret_cast<const float*>(smem + kBarBytes);
   for (int i = threadIdx.x; i < 2 * dim; i += blockDim.x) {
-    float t = smem[i];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) t += smem[(size_t)w * 2 * dim + i];
+    float t = base[i];
+    for (int w = 1; w < nwarps; ++w) t += base[(size_t)w * wstride + i];
     out[i] = t;
   }
 }
@@ -305,34 +408,56 @@ int bwd_blocks(int64_t rows) {
   return (int)b;
 }
 
-// Launches ln_bwd_rows; *blocks (in: upper bound on the CTA count the caller's
-// partial buffer holds; out: CTAs launched = partial rows written).
-template <typename TDY, typename TX, typename TDX>
-magma_status_t launch_bwd_rows(const void* dy, const void* x, const float* gamma,
-                               const float* mean, const float* rstd, void* dx, int64_t rows,
-                               int dim, int acc_dx, float* part, int* blocks,
-                               cudaStream_t stream) {
-  int64_t b = ceil_div(rows, kWarps * 2);
-  const int64_t cap = 2LL * num_sms();
+// CTAs of a streaming launch: one per SM at most, no more than the rows need,
+// and no more than the partial rows the backward workspace holds.
+int stream_blocks(int64_t rows, int warps) {
+  int64_t b = ceil_div(rows, warps);
+  if (b > num_sms()) b = num_sms();
+  int64_t cap = ceil_div(rows, kWarps);
+  if (cap > kMaxBwdBlocks) cap = kMaxBwdBlocks;
   if (b > cap) b = cap;
-  if (b > *blocks) b = *blocks;
-  if (b < 1) b = 1;
-  *blocks = (int)b;
-  const size_t smem = (size_t)kWarps * 2 * dim * sizeof(float);
-  const int cpl = (dim + 255) / 256;
-#define LN_BWD_ROWS(C)                                                                         \
-  do {                                                                                         \
-    auto kern = ln_bwd_rows<C, (C <= 3 ? 2 : 1), TDY, TX, TDX>;                                \
-    if (smem > 48 * 1024)                                                                      \
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);      \
-    kern<<<(int)b, kWarps * 32, smem, stream>>>((const TDY*)dy, (const TX*)x, gamma, mean, rstd, \
-                                                 (TDX*)dx, part, rows, dim, acc_dx);           \
+  return b < 1 ? 1 : (int)b;
+}
+
+template <typename K>
+void set_dynamic_smem(K kern, size_t bytes) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// Backward through ln_bwd_stream when the shape and alignment allow it
+// (*launched false otherwise). *blocks: CTAs launched = partial rows written;
+// at most `max_blocks`.
+template <typename TDY, typename TX, typename TDX>
+magma_status_t launch_bwd_stream(const void* dy, const void* x, const float* gamma,
+                                 const float* mean, const float* rstd, void* dx, int64_t rows,
+                                 int dim, int acc_dx, float* part, int max_blocks, int* blocks,
+                                 bool* launched, cudaStream_t stream) {
+  *launched = false;
+  if (!stream_ok(dim) || !aligned16(x) || !aligned16(dy) || !aligned16(dx) || !aligned16(gamma))
+    return MAGMA_OK;
+  const size_t stage =
+      (size_t)dim * (sizeof(TX) + sizeof(TDY) + (acc_dx ? sizeof(TDX) : 0));
+  const int groups = ((dim + 255) / 256) * 2;
+  const int warps = stream_warps(kBwdRing, stage, bwd_max_warps(groups));
+  if (warps == 0) return MAGMA_OK;
+  int b = stream_blocks(rows, warps);
+  if (b > max_blocks) b = max_blocks;
+  *blocks = b;
+  const size_t smem = kBarBytes + (size_t)warps * kBwdRing * stage;
+#define LN_BWD_STREAM(G)                                                                        \
+  do {                                                                                          \
+    auto kern = ln_bwd_stream<G, TDY, TX, TDX>;                                                 \
+    set_dynamic_smem(kern, smem);                                                               \
+    kern<<<b, warps * 32, smem, stream>>>((const TDY*)dy, (const TX*)x, gamma, mean, rstd,      \
+                                          (TDX*)dx, part, rows, dim, acc_dx,                    \
+                                          device_error_word());                                 \
   } while (0)
-  if (cpl == 1) LN_BWD_ROWS(1);
-  else if (cpl == 2) LN_BWD_ROWS(2);
-  else if (cpl == 3) LN_BWD_ROWS(3);
-  else LN_BWD_ROWS(4);
-#undef LN_BWD_ROWS
+  if (groups == 2) LN_BWD_STREAM(2);
+  else if (groups == 4) LN_BWD_STREAM(4);
+  else if (groups == 6) LN_BWD_STREAM(6);
+  else LN_BWD_STREAM(8);
+#undef LN_BWD_STREAM
+  *launched = true;
   return check_launch("layernorm_bwd");
 }
 
@@ -340,30 +465,34 @@ template <typename TX, typename TY>
 magma_status_t launch_fwd(const void* x, const float* gamma, const float* beta, void* y,
                           float* mean, float* rstd, int64_t rows, int dim, float eps,
                           cudaStream_t stream) {
-  int64_t blocks = ceil_div(rows, kWarps);
-  int64_t cap = 16LL * num_sms();
-  if (blocks > cap) blocks = cap;
-  bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(y) &&
-             aligned16(gamma) && aligned16(beta);
-  if (vec) {
-    const int cpl = (dim + 255) / 256;
-    int64_t b2 = ceil_div(rows, kWarps * 2);
-    if (b2 > cap) b2 = cap;
-    if (cpl == 1)
-      ln_fwd_rows<1, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
-          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
-    else if (cpl == 2)
-      ln_fwd_rows<2, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
-          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
-    else if (cpl == 3)
-      ln_fwd_rows<3, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
-          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
-    else
-      ln_fwd_rows<4, 2, TX, TY><<<(int)b2, kWarps * 32, 0, stream>>>(
-          (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
-  } else
+  const bool vec = stream_ok(dim) && aligned16(x) && aligned16(y) && aligned16(gamma) &&
+                   aligned16(beta);
+  const int groups = ((dim + 255) / 256) * 2;
+  const int warps =
+      vec ? stream_warps(kFwdRing, (size_t)dim * sizeof(TX), fwd_max_warps(groups)) : 0;
+  if (warps > 0) {
+    int64_t b = ceil_div(rows, warps);
+    if (b > num_sms()) b = num_sms();
+    const size_t smem = kBarBytes + (size_t)warps * kFwdRing * dim * sizeof(TX);
+#define LN_FWD_STREAM(G)                                                                        \
+  do {                                                                                          \
+    auto kern = ln_fwd_stream<G, TX, TY>;                                                       \
+    set_dynamic_smem(kern, smem);                                                               \
+    kern<<<(int)b, warps * 32, smem, stream>>>((const TX*)x, gamma, beta, (TY*)y, mean, rstd,   \
+                                               rows, dim, eps, device_error_word());            \
+  } while (0)
+    if (groups == 2) LN_FWD_STREAM(2);
+    else if (groups == 4) LN_FWD_STREAM(4);
+    else if (groups == 6) LN_FWD_STREAM(6);
+    else LN_FWD_STREAM(8);
+#undef LN_FWD_STREAM
+  } else {
+    int64_t blocks = ceil_div(rows, kWarps);
+    const int64_t cap = 16LL * num_sms();
+    if (blocks > cap) blocks = cap;
     ln_fwd_generic<TX, TY><<<(int)blocks, kWarps * 32, 0, stream>>>(
         (const TX*)x, gamma, beta, (TY*)y, mean, rstd, rows, dim, eps);
+  }
   return check_launch("layernorm_fwd");
 }
 
@@ -373,13 +502,12 @@ magma_status_t launch_bwd(const void* dy, const void* x, const float* gamma, con
                           int64_t rows, int dim, int acc_dx, int acc_params, float* part,
                           cudaStream_t stream) {
   int blocks = bwd_blocks(rows);
-  bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(dy) &&
-             aligned16(dx) && aligned16(gamma);
-  if (vec) {
-    if (magma_status_t st = launch_bwd_rows<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, rows, dim,
-                                                          acc_dx, part, &blocks, stream))
-      return st;
-  } else {
+  bool streamed = false;
+  if (magma_status_t st = launch_bwd_stream<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, rows, dim,
+                                                          acc_dx, part, kMaxBwdBlocks, &blocks,
+                                                          &streamed, stream))
+    return st;
+  if (!streamed) {
     ln_bwd_generic<TDY, TX, TDX><<<blocks, kWarps * 32, 0, stream>>>(
         (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
   }
@@ -434,13 +562,12 @@ magma_status_t launch_bwd_noalloc(const void* dy, const void* x, const float* ga
                                   float* part, cudaStream_t stream) {
   int blocks = bwd_blocks(rows);
   if (blocks > kNoAllocMaxBlocks) blocks = kNoAllocMaxBlocks;
-  const bool vec = (dim % 8 == 0) && dim <= kMaxChunks * 256 && aligned16(x) && aligned16(dy) &&
-                   aligned16(dx) && aligned16(gamma);
-  if (vec) {
-    if (magma_status_t st = launch_bwd_rows<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, rows, dim,
-                                                          acc_dx, part, &blocks, stream))
-      return st;
-  } else {
+  bool streamed = false;
+  if (magma_status_t st = launch_bwd_stream<TDY, TX, TDX>(dy, x, gamma, mean, rstd, dx, rows, dim,
+                                                          acc_dx, part, kNoAllocMaxBlocks,
+                                                          &blocks, &streamed, stream))
+    return st;
+  if (!streamed) {
     ln_bwd_generic<TDY, TX, TDX><<<blocks, kWarps * 32, 0, stream>>>(
         (const TDY*)dy, (const TX*)x, gamma, mean, rstd, (TDX*)dx, part, rows, dim, acc_dx);
   }

@@ -52,7 +52,11 @@ def bf16_round(a):
 
 
 # --------------------------------------------------------------------- LayerNorm
-@pytest.mark.parametrize("rows,dim", [(8192, 768), (1000, 384), (37, 100), (1, 1024), (5, 2048)])
+# (8192, 768): GPT-2 rows; 384/136/1024: partial and full last lane groups of
+# the streaming kernels; 20000 rows: many passes around each warp's row ring;
+# 100 and 2048: the generic kernels.
+@pytest.mark.parametrize("rows,dim", [(8192, 768), (1000, 384), (2500, 136), (20000, 256),
+                                      (37, 100), (1, 1024), (5, 2048)])
 def test_layernorm_f32(cuda, oracle, rows, dim):
     from magma_b200 import ops
 
@@ -73,11 +77,11 @@ def test_layernorm_f32(cuda, oracle, rows, dim):
     close(db.cpu(), rdb, 1e-5)
 
 
-def test_layernorm_bf16_io_and_accumulate(cuda, oracle):
+@pytest.mark.parametrize("rows,dim", [(2048, 768), (3000, 1024), (777, 136)])
+def test_layernorm_bf16_io_and_accumulate(cuda, oracle, rows, dim):
     from magma_b200 import ops
 
     rng = np.random.default_rng(7)
-    rows, dim = 2048, 768
     x = rng.standard_normal((rows, dim)).astype(np.float32)
     g = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
     b = (0.02 * rng.standard_normal(dim)).astype(np.float32)

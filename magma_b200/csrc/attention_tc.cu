@@ -120,235 +120,317 @@ __device__ __forceinline__ uint32_t align1024(uint8_t* raw, uint8_t** aligned_pt
 }
 
 // =============================================================== forward
-constexpr int kFwdKvStages = 3;
-constexpr int kFwdQ = 0;
-constexpr int kFwdKv = kFwdQ + kTileBytes;                          // K,V per stage
-constexpr int kFwdP = kFwdKv + kFwdKvStages * 2 * kTileBytes;      // 2 x 32 KB
-constexpr int kFwdBar = kFwdP + 2 * 2 * kTileBytes;
-// q_full, kv_full[3], kv_empty[3], s_full[2], s_empty[2], p_full[2], pv_done[2], done
-constexpr int kFwdNumBars = 16;
+// One CTA per pair of 128-query tiles (t = 0, 1: query rows q0 .. q0+255),
+// heaviest causal pairs first. Warps 0-3 run the softmax of tile 0, warps 4-7
+// that of tile 1, warp 8 is the TMA producer, warp 9 allocates TMEM and issues
+// the MMAs. Both tiles stream the same K/V tiles, so while one warpgroup
+// turns S_t into P_t the tensor cores work on the other tile:
+//   MMA order: S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) ...
+// TMEM: S_t at columns 128t (F32 128x128); P_t is written back as BF16 over
+// the first 64 columns of S_t and is the A operand of PV_t = P_t V_j, which
+// accumulates into O_t at columns 256 + 64t. tcgen05.mma executes in issue
+// order, so S_t(j+1), issued after PV_t(j), cannot overwrite P_t(j) early, and
+// the commit that reports S_t(j+1) done also covers PV_t(j). O_t and the row
+// sum are rescaled only when a row maximum grows by more than 2^8 (otherwise
+// the stale maximum is kept: P <= 2^8, exact after the final division).
+constexpr int kFwdStages = 3;
+constexpr int kFwdThreads = 320;                 // 8 softmax warps + producer + MMA
+constexpr int kFwdQ = 0;                         // Q tiles 0, 1 (2 x 16 KB)
+constexpr int kFwdKv = 2 * kTileBytes;           // K, V per stage
+constexpr int kFwdBar = kFwdKv + kFwdStages * 2 * kTileBytes;
+// q_full, kv_full[3], kv_empty[3], s_full[2], p_full[2], pv_done[2], done
+constexpr int kFwdNumBars = 14;
 constexpr int kFwdSmem = kFwdBar + kFwdNumBars * 8 + 16 + 1024;
+constexpr float kRescaleLog2 = 8.0f;
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, AttnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sp;
   const uint32_t base = align1024(smem_raw, &sp);
-  const uint32_t sQ = base + kFwdQ;
+  auto sQ = [&](int t) { return base + kFwdQ + t * kTileBytes; };
   auto sK = [&](int st) { return base + kFwdKv + st * 2 * kTileBytes; };
   auto sV = [&](int st) { return base + kFwdKv + st * 2 * kTileBytes + kTileBytes; };
-  auto sP = [&](int b) { return base + kFwdP + b * 2 * kTileBytes; };
   const uint32_t bars = base + kFwdBar;
   const uint32_t q_full = bars;
-  auto kv_full = [&](int s) { return bars + 8u * (1 + s); };
-  auto kv_empty = [&](int s) { return bars + 8u * (4 + s); };
-  auto s_full = [&](int b) { return bars + 8u * (7 + b); };
-  auto s_empty = [&](int b) { return bars + 8u * (9 + b); };
-  auto p_full = [&](int b) { return bars + 8u * (11 + b); };
-  auto pv_done = [&](int b) { return bars + 8u * (13 + b); };
-  const uint32_t done_bar = bars + 8u * 15;
+  auto kv_full = [&](int st) { return bars + 8u * (1 + st); };
+  auto kv_empty = [&](int st) { return bars + 8u * (4 + st); };
+  auto s_full = [&](int t) { return bars + 8u * (7 + t); };
+  auto p_full = [&](int t) { return bars + 8u * (9 + t); };
+  auto pv_done = [&](int t) { return bars + 8u * (11 + t); };
+  const uint32_t done_bar = bars + 8u * 13;
   const uint32_t tslot = bars + 8u * kFwdNumBars;
   uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kFwdBar + 8 * kFwdNumBars);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (a.S + kTile - 1) / kTile;
-  const int qt = n_qt - 1 - (int)blockIdx.x;
+  const int n_pairs = (n_qt + 1) / 2;
+  const int qt0 = 2 * (n_pairs - 1 - (int)blockIdx.x);
+  const bool has1 = qt0 + 1 < n_qt;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qt * kTile;
-  const int n_kv = a.causal ? qt + 1 : n_qt;
+  // key tiles visited by query tile t
+  const int nk0 = a.causal ? qt0 + 1 : n_qt;
+  const int nk1 = has1 ? (a.causal ? qt0 + 2 : n_qt) : 0;
+  const int n_kv = nk0 > nk1 ? nk0 : nk1;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
     mbar_init(q_full, 1);
-    for (int s = 0; s < kFwdKvStages; ++s) {
-      mbar_init(kv_full(s), 1);
-      mbar_init(kv_empty(s), 1);
+    for (int st = 0; st < kFwdStages; ++st) {
+      mbar_init(kv_full(st), 1);
+      mbar_init(kv_empty(st), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full(i), 1);
-      mbar_init(s_empty(i), 4);
-      mbar_init(p_full(i), 4);
-      mbar_init(pv_done(i), 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(p_full(t), 4);
+      mbar_init(pv_done(t), 1);
     }
     mbar_init(done_bar, 1);
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(tslot, 512);
+  if (warp == 9) tmem_alloc(tslot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
-  const uint32_t tS = tmem;          // S buffers at columns 0, 128
-  const uint32_t tO = tmem + 256;    // PV partial buffers at columns 256, 320
+  auto tS = [&](int t) { return tmem + (uint32_t)(t * kTile); };
+  auto tO = [&](int t) { return tmem + 256u + (uint32_t)(t * kHd); };
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       bool ok = true;
-      mbar_expect_tx(q_full, kTileBytes);
-      tma_load_4d(sQ, &tmQ, 0, q0, h, b, q_full);
+      mbar_expect_tx(q_full, (has1 ? 2 : 1) * kTileBytes);
+      tma_load_4d(sQ(0), &tmQ, 0, qt0 * kTile, h, b, q_full);
+      if (has1) tma_load_4d(sQ(1), &tmQ, 0, (qt0 + 1) * kTile, h, b, q_full);
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % kFwdKvStages;
-        const uint32_t ph = (uint32_t)((j / kFwdKvStages) & 1);
-        if (!mbar_wait(kv_empty(st), ph ^ 1u, a.err)) { ok = false; break; }
+        const int st = j % kFwdStages;
+        if (!mbar_wait(kv_empty(st), (uint32_t)(((j / kFwdStages) & 1) ^ 1), a.err)) {
+          ok = false;
+          break;
+        }
         mbar_expect_tx(kv_full(st), 2 * kTileBytes);
         tma_load_4d(sK(st), &tmK, 0, j * kTile, h, b, kv_full(st));
         tma_load_4d(sV(st), &tmV, 0, j * kTile, h, b, kv_full(st));
       }
       // every stage issued above has been consumed before the producer leaves
-      for (int j = n_kv; j < n_kv + kFwdKvStages && ok; ++j) {
-        const int st = j % kFwdKvStages;
-        const uint32_t ph = (uint32_t)((j / kFwdKvStages) & 1);
-        if (!mbar_wait(kv_empty(st), ph ^ 1u, a.err)) ok = false;
+      for (int j = n_kv; j < n_kv + kFwdStages && ok; ++j) {
+        const int st = j % kFwdStages;
+        if (!mbar_wait(kv_empty(st), (uint32_t)(((j / kFwdStages) & 1) ^ 1), a.err)) ok = false;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
       constexpr uint32_t idPV = idesc_bf16_f32(kTile, kHd, 0, 1);
       bool ok = mbar_wait(q_full, 0, a.err);
-      auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1, st = i % kFwdKvStages;
-        if (!mbar_wait(p_full(pb), (uint32_t)((i >> 1) & 1), a.err)) return false;
+      int kv_ready = -1;  // highest key tile whose K/V have been waited for
+      auto wait_kv = [&](int j) -> bool {
+        if (j <= kv_ready) return true;
+        kv_ready = j;
+        if (!mbar_wait(kv_full(j % kFwdStages), (uint32_t)((j / kFwdStages) & 1), a.err))
+          return false;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint64_t ad = desc_k(sP(pb) + (kk >> 2) * 16384 + (kk & 3) * 32);
-          const uint64_t bd = desc_mn(sV(st) + kk * 2048);
-          mma_bf16_ss(tO + pb * kHd, ad, bd, idPV, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(pv_done(pb));
-        mma_commit(kv_empty(st));
         return true;
       };
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % kFwdKvStages, sb = j & 1;
-        if (!mbar_wait(kv_full(st), (uint32_t)((j / kFwdKvStages) & 1), a.err)) { ok = false; break; }
-        if (!mbar_wait(s_empty(sb), (uint32_t)(((j >> 1) & 1) ^ 1), a.err)) { ok = false; break; }
-        tc_fence_after();
+      auto issue_s = [&](int t, int j) {
+        const int st = j % kFwdStages;
 #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk)
-          mma_bf16_ss(tS + sb * kTile, desc_k(sQ + kk * 32), desc_k(sK(st) + kk * 32), idS,
+          mma_bf16_ss(tS(t), desc_k(sQ(t) + kk * 32), desc_k(sK(st) + kk * 32), idS,
                       kk > 0 ? 1u : 0u);
-        mma_commit(s_full(sb));
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        mma_commit(s_full(t));
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait(p_full(t), (uint32_t)(j & 1), a.err)) return false;
+        tc_fence_after();
+        const int st = j % kFwdStages;
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_bf16_ts(tO(t), tS(t) + kk * 8, desc_mn(sV(st) + kk * 2048), idPV,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(pv_done(t));
+        return true;
+      };
+      if (ok && n_kv > 0) {
+        ok = wait_kv(0);
+        if (ok) {
+          issue_s(0, 0);
+          if (nk1 > 0) issue_s(1, 0);
+        }
       }
-      if (ok && n_kv >= 1) issue_pv(n_kv - 1);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          const int nk = t ? nk1 : nk0;
+          if (j >= nk) continue;
+          if (!issue_pv(t, j)) { ok = false; break; }
+          if (j + 1 < nk) {
+            if (!wait_kv(j + 1)) { ok = false; break; }
+            issue_s(t, j + 1);
+          }
+        }
+        if (ok) mma_commit(kv_empty(j % kFwdStages));
+      }
       mma_commit(done_bar);
       mbar_wait(done_bar, 0, a.err);
     }
   } else {
-    // ------------------------------ row threads ------------------------------
-    const int r = warp * 32 + lane;
-    const int qg = q0 + r;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ---------------------------- softmax warpgroups ----------------------------
+    const int t = warp >> 2;
+    const int nk = t ? nk1 : nk0;
+    const int qt = qt0 + t;
+    const int r = (warp & 3) * 32 + lane;
+    const int qg = qt * kTile + r;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t srow = tS(t) + lane_off;
+    const uint32_t orow = tO(t) + lane_off;
     const float sl2 = a.scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f;
-    float o[kHd];
-#pragma unroll
-    for (int i = 0; i < kHd; ++i) o[i] = 0.f;
-    float ring0 = 0.f, ring1 = 0.f;  // rescale factor pending for PV buffer 0 / 1
     bool ok = true;
-    auto absorb = [&](int i) -> bool {
-      const int pb = i & 1;
-      if (!mbar_wait(pv_done(pb), (uint32_t)((i >> 1) & 1), a.err)) return false;
-      tc_fence_after();
-      uint32_t v0[32], v1[32];
-      tmem_ld32(tO + pb * kHd + lane_off, v0);
-      tmem_ld32(tO + pb * kHd + 32 + lane_off, v1);
-      tmem_wait_ld();
-      const float al = pb ? ring1 : ring0;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        o[c] = o[c] * al + __uint_as_float(v0[c]);
-        o[32 + c] = o[32 + c] * al + __uint_as_float(v1[c]);
-      }
-      return true;
-    };
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(s_full(sb), (uint32_t)((j >> 1) & 1), a.err)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t srow = tS + sb * kTile + lane_off;
+    // The two warpgroups take turns on the exponential pass (MUFU is the
+    // bottleneck unit): tile 0 step j, tile 1 step j, tile 0 step j+1, ...
+    // Named barrier 1 + t hands the turn to warpgroup t. A warpgroup that hit
+    // a wait limit keeps the turn protocol (skipping its work) so the other
+    // one is never left at a named barrier.
+    const int nk_other = t ? nk0 : nk1;
+    for (int j = 0; j < nk; ++j) {
+      // waits for the other warpgroup's step j-1 (t = 0) or step j (t = 1)
+      const bool wait_turn = t ? (j < nk_other) : (j >= 1 && j - 1 < nk_other);
+      // hands over after step j to its step j (t = 0) or step j+1 (t = 1)
+      const bool give_turn = t ? (j + 1 < nk_other) : (j < nk_other);
       const int k0 = j * kTile;
-      const bool diag = a.causal && (k0 + kTile > q0);
-      const bool tail = k0 + kTile > a.S;
       // Only the diagonal tile (causal) and a ragged last tile need masking;
-      // every other tile takes the mask-free loops (warp-uniform branch).
+      // every other tile takes the mask-free path (warp-uniform branch).
+      const bool diag = a.causal && j == qt;
+      const bool tail = k0 + kTile > a.S;
       const bool masked_tile = diag || tail;
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(srow + c * 32, v);
-        tmem_wait_ld();
-        if (!masked_tile) {
+      int lim = 127;  // last unmasked column of this row
+      if (diag) lim = qg - k0;
+      if (tail && a.S - 1 - k0 < lim) lim = a.S - 1 - k0;
+      if (ok && !mbar_wait(s_full(t), (uint32_t)(j & 1), a.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform for the collective TMEM ops
+      if (ok) {
+        tc_fence_after();
+        // pass 1: row maximum (S read from TMEM in two 64-column halves; eight
+        // independent max chains)
+        float mx8[8];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
-        } else {
+        for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int kg = k0 + c * 32 + e;
-            const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
-            if (!masked) mx = fmaxf(mx, __uint_as_float(v[e]));
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t v[2][32];
+          tmem_ld32(srow + hh * 64, v[0]);
+          tmem_ld32(srow + hh * 64 + 32, v[1]);
+          tmem_wait_ld();
+          if (!masked_tile) {
+#pragma unroll
+            for (int e = 0; e < 64; ++e)
+              mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(v[e >> 5][e & 31]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 64; ++e)
+              if (hh * 64 + e <= lim)
+                mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(v[e >> 5][e & 31]));
           }
         }
-      }
-      const float m_new = fmaxf(m_run, mx * sl2);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2_approx(m_run - m_use);
-      if (j >= 2 && !absorb(j - 2)) { ok = false; break; }
-      if (sb) ring1 = alpha; else ring0 = alpha;
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(srow + c * 32, v);
-        tmem_wait_ld();
-        float p[32];
-        if (!masked_tile) {
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float m_new = fmaxf(m_run, mx * sl2);
+        if (j == 0) {
+          m_run = m_new == -INFINITY ? 0.f : m_new;
+        } else if (__any_sync(0xffffffffu, m_new > m_run + kRescaleLog2)) {
+          // O_t holds PV_t(0 .. j-1) (complete: covered by the S_t(j) commit).
+          const float alpha = ex2_approx(m_run - m_new);
+          m_run = m_new;
+          l_run *= alpha;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            p[e] = ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -m_use));
-            rs += p[e];
-          }
-        } else {
+          for (int half = 0; half < 2; ++half) {
+            uint32_t o[32];
+            tmem_ld32(orow + half * 32, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int kg = k0 + c * 32 + e;
-            const bool masked = (diag && kg > qg) || (tail && kg >= a.S);
-            p[e] = masked ? 0.f : ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -m_use));
-            rs += p[e];
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st32(orow + half * 32, o);
           }
+          tmem_wait_st();
         }
-        store_row32(sP(sb), r, c, p);
       }
-      l_run = l_run * alpha + rs;
-      m_run = m_use;
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_empty(sb));
-        mbar_arrive(p_full(sb));
+      if (wait_turn) named_barrier(1 + t, 256);
+      if (ok) {
+        // pass 2: P = exp2(S * scale * log2(e) - m), written back over S as BF16
+        float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t v[2][32];
+          tmem_ld32(srow + hh * 64, v[0]);
+          tmem_ld32(srow + hh * 64 + 32, v[1]);
+          tmem_wait_ld();
+          uint32_t pk[32];
+          if (!masked_tile) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int c0 = 2 * e;
+              const float p0 = ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][c0 & 31]), sl2, -m_run));
+              const float p1 =
+                  ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][(c0 + 1) & 31]), sl2, -m_run));
+              rs4[e & 3] += p0 + p1;
+              pk[e] = pack_bf16(p0, p1);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int c0 = 2 * e;
+              float p0 = ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][c0 & 31]), sl2, -m_run));
+              float p1 = ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][(c0 + 1) & 31]), sl2, -m_run));
+              if (hh * 64 + c0 > lim) p0 = 0.f;
+              if (hh * 64 + c0 + 1 > lim) p1 = 0.f;
+              rs4[e & 3] += p0 + p1;
+              pk[e] = pack_bf16(p0, p1);
+            }
+          }
+          // columns [32*hh, 32*hh+32) of the BF16 view: S columns already read
+          tmem_st32(srow + hh * 32, pk);
+        }
+        const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+        l_run += rs;
+        tmem_wait_st();
+      }
+      if (give_turn) named_barrier_arrive(2 - t, 256);
+      if (ok) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(t));
       }
     }
-    if (ok) {
-      for (int i = (n_kv >= 2 ? n_kv - 2 : 0); i < n_kv && ok; ++i) ok = absorb(i);
-    }
-    if (ok && qg < a.S) {
-      const float inv = 1.0f / l_run;
-      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.o) + (int64_t)b * a.os0 +
-                           (int64_t)h * a.os1 + (int64_t)qg * a.os2;
-      store_global_row64(dst, o, inv);
-      if (a.lse != nullptr) a.lse[((int64_t)b * a.H + h) * a.S + qg] = m_run * kLn2 + logf(l_run);
+    if (ok && nk > 0 && !mbar_wait(pv_done(t), (uint32_t)((nk - 1) & 1), a.err)) ok = false;
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && nk > 0) {
+      tc_fence_after();
+      uint32_t o0[32], o1[32];
+      tmem_ld32(orow, o0);
+      tmem_ld32(orow + 32, o1);
+      tmem_wait_ld();
+      if (qg < a.S) {
+        float of[kHd];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          of[c] = __uint_as_float(o0[c]);
+          of[32 + c] = __uint_as_float(o1[c]);
+        }
+        const float inv = 1.0f / l_run;
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.o) + (int64_t)b * a.os0 +
+                             (int64_t)h * a.os1 + (int64_t)qg * a.os2;
+        store_global_row64(dst, of, inv);
+        if (a.lse != nullptr)
+          a.lse[((int64_t)b * a.H + h) * a.S + qg] = m_run * kLn2 + logf(l_run);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -815,8 +897,8 @@ magma_status_t attention_fwd_tc(const void* q, const void* k, const void* v, voi
   a.qs0 = qs[0]; a.qs1 = qs[1]; a.qs2 = qs[2];
   a.err = device_error_word();
   if (magma_status_t st = set_smem_attr<0>(attn_fwd_tc, kFwdSmem)) return st;
-  dim3 grid((unsigned)ceil_div(S, kTile), (unsigned)H, (unsigned)B);
-  attn_fwd_tc<<<grid, kThreads, kFwdSmem, s>>>(mq, mk, mv, a);
+  dim3 grid((unsigned)ceil_div(ceil_div(S, kTile), 2), (unsigned)H, (unsigned)B);
+  attn_fwd_tc<<<grid, kFwdThreads, kFwdSmem, s>>>(mq, mk, mv, a);
   return check_launch("attention_fwd_tcgen05");
 }
 

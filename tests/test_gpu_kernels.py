@@ -306,9 +306,13 @@ def test_attention_f32(cuda, oracle, shape, causal):
     close(dv.cpu(), rdv, 1e-4)
 
 
+# Query tiles are processed in pairs: 320 and 64 leave the last pair with one
+# tile; 450 puts the causal diagonal and the ragged end in the same tile of a
+# full pair; 333 is a ragged non-causal pair.
 @pytest.mark.parametrize("shape,causal", [((1, 12, 1024, 64), True), ((2, 2, 320, 64), True),
                                           ((1, 1, 64, 64), True), ((1, 2, 256, 64), False),
-                                          ((1, 3, 200, 64), False)])
+                                          ((1, 3, 200, 64), False), ((1, 2, 450, 64), True),
+                                          ((2, 1, 333, 64), False)])
 def test_attention_bf16(cuda, oracle, shape, causal):
     """BF16, head_dim 64: the tcgen05 kernels."""
     from magma_b200 import ops

@@ -357,47 +357,53 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           tmem_wait_st();
         }
       }
+      // pass 2: P = exp2(S * scale * log2(e) - m), written back over S as
+      // BF16. The first half of the row is read from TMEM before the turn
+      // starts, the second half while the first is exponentiated; the turn is
+      // handed on as soon as the last exponential is issued.
+      uint32_t va[2][32];
+      if (ok) {
+        tmem_ld32(srow, va[0]);
+        tmem_ld32(srow + 32, va[1]);
+        tmem_wait_ld();
+      }
       if (wait_turn) named_barrier(1 + t, 256);
       if (ok) {
-        // pass 2: P = exp2(S * scale * log2(e) - m), written back over S as BF16
         float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+        // Exponentiates 32 columns starting at column c of S (v) into 16
+        // packed BF16 pairs stored over BF16 columns [c/2, c/2 + 16) (S
+        // columns already read).
+        auto exp32 = [&](const uint32_t (&v)[32], int c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t v[2][32];
-          tmem_ld32(srow + hh * 64, v[0]);
-          tmem_ld32(srow + hh * 64 + 32, v[1]);
-          tmem_wait_ld();
-          uint32_t pk[32];
-          if (!masked_tile) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int c0 = 2 * e;
-              const float p0 = ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][c0 & 31]), sl2, -m_run));
-              const float p1 =
-                  ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][(c0 + 1) & 31]), sl2, -m_run));
-              rs4[e & 3] += p0 + p1;
-              pk[e] = pack_bf16(p0, p1);
+          for (int e = 0; e < 16; ++e) {
+            float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), sl2, -m_run));
+            float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), sl2, -m_run));
+            if (masked_tile) {
+              if (c + 2 * e > lim) p0 = 0.f;
+              if (c + 2 * e + 1 > lim) p1 = 0.f;
             }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int c0 = 2 * e;
-              float p0 = ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][c0 & 31]), sl2, -m_run));
-              float p1 = ex2_approx(fmaf(__uint_as_float(v[c0 >> 5][(c0 + 1) & 31]), sl2, -m_run));
-              if (hh * 64 + c0 > lim) p0 = 0.f;
-              if (hh * 64 + c0 + 1 > lim) p1 = 0.f;
-              rs4[e & 3] += p0 + p1;
-              pk[e] = pack_bf16(p0, p1);
-            }
+            rs4[e & 3] += p0 + p1;
+            pk[e] = pack_bf16(p0, p1);
           }
-          // columns [32*hh, 32*hh+32) of the BF16 view: S columns already read
-          tmem_st32(srow + hh * 32, pk);
-        }
-        const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-        l_run += rs;
+          tmem_st16(srow + c / 2, pk);
+        };
+        uint32_t vb[32];
+        tmem_ld32(srow + 64, vb);  // lands while columns 0-63 are exponentiated
+        exp32(va[0], 0);
+        exp32(va[1], 32);
+        tmem_wait_ld();
+        uint32_t vc[32];
+        tmem_ld32(srow + 96, vc);
+        exp32(vb, 64);
+        tmem_wait_ld();
+        exp32(vc, 96);
+        if (give_turn) named_barrier_arrive(2 - t, 256);
+        l_run += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         tmem_wait_st();
+      } else if (give_turn) {
+        named_barrier_arrive(2 - t, 256);
       }
-      if (give_turn) named_barrier_arrive(2 - t, 256);
       if (ok) {
         tc_fence_before();
         __syncwarp();

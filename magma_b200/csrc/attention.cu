@@ -19,10 +19,13 @@ bool attention_tc_supported(const void* q, const void* k, const void* v, const v
 magma_status_t attention_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse,
                                 int64_t B, int64_t H, int64_t S, const int64_t* qs,
                                 const int64_t* os, float scale, int causal, cudaStream_t s);
+size_t attention_bwd_tc_partials_bytes(int64_t B, int64_t H, int64_t S, int causal);
+size_t attention_bwd_tc_delta_bytes(int64_t B, int64_t H, int64_t S);
 magma_status_t attention_bwd_tc(const void* q, const void* k, const void* v, const void* o,
                                 const void* d_o, const float* lse, void* dq, void* dk, void* dv,
-                                float* delta, int64_t B, int64_t H, int64_t S, const int64_t* qs,
-                                const int64_t* os, float scale, int causal, cudaStream_t s);
+                                void* workspace, size_t ws_bytes, int64_t B, int64_t H, int64_t S,
+                                const int64_t* qs, const int64_t* os, float scale, int causal,
+                                cudaStream_t s);
 }  // namespace magma
 
 using namespace magma;
@@ -67,10 +70,17 @@ magma_status_t magma_attention_fwd(const void* q, const void* k, const void* v, 
 
 size_t magma_attention_bwd_workspace_size(int64_t batch, int64_t heads, int64_t seq,
                                           int64_t head_dim, magma_dtype_t dtype) {
-  (void)head_dim;
-  (void)dtype;
   if (batch <= 0 || heads <= 0 || seq <= 0) return 0;
-  return (size_t)(batch * heads * seq) * sizeof(float);
+  const size_t delta = attention_bwd_tc_delta_bytes(batch, heads, seq);
+  // BF16 head_dim 64 runs the fused tensor-core backward, which also keeps one
+  // F32 dQ partial tile per (query tile, key tile) pair (the non-causal count,
+  // an upper bound for causal); capped at 4 GiB, beyond which it falls back to
+  // the two-pass kernels that need only delta.
+  if (dtype == MAGMA_DTYPE_BF16 && head_dim == 64) {
+    const size_t part = attention_bwd_tc_partials_bytes(batch, heads, seq, 0);
+    if (part <= (4ull << 30)) return delta + part;
+  }
+  return delta;
 }
 
 magma_status_t magma_attention_bwd(const void* q, const void* k, const void* v, const void* o,
@@ -85,15 +95,18 @@ magma_status_t magma_attention_bwd(const void* q, const void* k, const void* v, 
   if (batch == 0 || heads == 0 || seq == 0) return MAGMA_OK;
   MAGMA_REQUIRE(q && k && v && o && d_o && lse && dq && dk && dv,
                 "magma_attention_bwd: NULL pointer");
-  size_t need = magma_attention_bwd_workspace_size(batch, heads, seq, head_dim, dtype);
+  // Minimum: the row terms delta (two-pass kernels); the size the query
+  // returns also lets BF16 head_dim 64 take the fused kernel.
+  const size_t need = attention_bwd_tc_delta_bytes(batch, heads, seq);
   MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= need,
-                "magma_attention_bwd: workspace of %zu bytes needed, %zu given", need,
+                "magma_attention_bwd: workspace of at least %zu bytes needed, %zu given", need,
                 workspace_bytes);
   if (attention_tc_supported(q, k, v, o, head_dim, qkv_strides, o_strides, dtype, batch, heads,
                              seq) &&
       aligned16(d_o) && aligned16(dq) && aligned16(dk) && aligned16(dv))
-    return attention_bwd_tc(q, k, v, o, d_o, lse, dq, dk, dv, (float*)workspace, batch, heads, seq,
-                            qkv_strides, o_strides, scale, causal, (cudaStream_t)stream);
+    return attention_bwd_tc(q, k, v, o, d_o, lse, dq, dk, dv, workspace, workspace_bytes, batch,
+                            heads, seq, qkv_strides, o_strides, scale, causal,
+                            (cudaStream_t)stream);
   return attention_bwd_simt(q, k, v, o, d_o, lse, dq, dk, dv, (float*)workspace, batch, heads, seq,
                             head_dim, qkv_strides, o_strides, scale, causal, dtype,
                             (cudaStream_t)stream);

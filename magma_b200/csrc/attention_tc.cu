@@ -29,13 +29,12 @@
 // kernel winds down instead of hanging).
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
 namespace magma {
-magma_status_t attention_bwd_delta(const void* o, const void* d_o, float* delta, int64_t batch,
-                                   int64_t heads, int64_t seq, int64_t hd, const int64_t* os,
-                                   magma_dtype_t dtype, cudaStream_t s);
 
 namespace {
 
@@ -844,6 +843,355 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   }
 }
 
+// ===================================================== backward, fused
+// One CTA per 128-key tile j (heaviest causal tiles first), looping over the
+// query tiles i that see it. Per (i, j):
+//   S^T = K_j Q_i^T, dP^T = V_j dO_i^T                     (TMEM)
+//   P^T = exp2(S^T*scale*log2e - lse_i*log2e), dS^T = P^T (dP^T - delta_i)
+//   dV_j += P^T dO_i, dK_j += dS^T Q_i                     (TMEM accumulators)
+//   dQ_ij = dS K_j -> F32 partial tile in the workspace      (TMEM, drained)
+// P^T and dS^T go to 128-byte-swizzled shared memory as BF16; the dS^T buffer
+// is the K-major A operand of dK and, read MN-major, the A operand of dQ. The
+// dQ partials are summed over j in a fixed order by attn_dq_reduce
+// (deterministic; no atomics).
+// Warps 0-7: element math, thread = key row (TMEM lane quarter warp % 4) x
+// one half of the 128 query columns (warp / 4); warp 8: TMA producer;
+// warp 9: TMEM allocator and MMA issuer.
+constexpr int kBwThreads = 320;
+constexpr int kBwK = 0;
+constexpr int kBwV = kTileBytes;
+constexpr int kBwQdo = 2 * kTileBytes;                      // 2 stages x (Q, dO)
+constexpr int kBwPT = kBwQdo + 2 * 2 * kTileBytes;          // 32 KB
+constexpr int kBwDST = kBwPT + 2 * kTileBytes;              // 32 KB
+constexpr int kBwStats = kBwDST + 2 * kTileBytes;           // lse2[2][128], delta[2][128]
+constexpr int kBwBar = kBwStats + 4 * kTile * 4;
+// kv_full, qdo_full[2], qdo_empty[2], st_full, pds_full, dq_full, dq_free, final
+constexpr int kBwNumBars = 10;
+constexpr int kBwSmem = kBwBar + kBwNumBars * 8 + 16 + 1024;
+constexpr int kDqTileFloats = kTile * kHd;                  // one F32 dQ partial tile
+
+// Index of the dQ partial of (query tile i, key tile j) among a head's slots.
+__host__ __device__ __forceinline__ int64_t dq_slot(int i, int j, int n_t, int causal) {
+  return causal ? (int64_t)i * (i + 1) / 2 + j : (int64_t)i * n_t + j;
+}
+__host__ __device__ __forceinline__ int64_t dq_slots(int n_t, int causal) {
+  return causal ? (int64_t)n_t * (n_t + 1) / 2 : (int64_t)n_t * n_t;
+}
+
+__global__ void __launch_bounds__(kBwThreads, 1)
+attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+            AttnTcArgs a, float* __restrict__ dq_part) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sp;
+  const uint32_t base = align1024(smem_raw, &sp);
+  const uint32_t sK = base + kBwK, sV = base + kBwV;
+  auto sQ = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes; };
+  auto sdO = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes + kTileBytes; };
+  const uint32_t sPT = base + kBwPT, sDST = base + kBwDST;
+  float* lse_s = reinterpret_cast<float*>(sp + kBwStats);           // [2][128], log2 units
+  float* delta_s = reinterpret_cast<float*>(sp + kBwStats + 2 * kTile * 4);
+  const uint32_t bars = base + kBwBar;
+  const uint32_t kv_full = bars;
+  auto qdo_full = [&](int st) { return bars + 8u * (1 + st); };
+  auto qdo_empty = [&](int st) { return bars + 8u * (3 + st); };
+  const uint32_t st_full = bars + 8u * 5;
+  const uint32_t pds_full = bars + 8u * 6;
+  const uint32_t dq_full = bars + 8u * 7;
+  const uint32_t dq_free = bars + 8u * 8;
+  const uint32_t final_bar = bars + 8u * 9;
+  const uint32_t tslot = bars + 8u * kBwNumBars;
+  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kBwBar + 8 * kBwNumBars);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_t = (a.S + kTile - 1) / kTile;
+  const int kt = (int)blockIdx.x;  // tile 0 has the most query tiles under causal
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int k0 = kt * kTile;
+  const int first_q = a.causal ? kt : 0;
+  const int n_it = n_t - first_q;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmdO);
+    mbar_init(kv_full, 1);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(qdo_full(st), 1);
+      mbar_init(qdo_empty(st), 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(pds_full, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 8);
+    mbar_init(final_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 9) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
+  const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320,
+                 tDQ = tmem + 384;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_expect_tx(kv_full, 2 * kTileBytes);
+      tma_load_4d(sK, &tmK, 0, k0, h, b, kv_full);
+      tma_load_4d(sV, &tmV, 0, k0, h, b, kv_full);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it & 1;
+        const int q0 = (first_q + it) * kTile;
+        if (!mbar_wait(qdo_empty(st), (uint32_t)(((it >> 1) & 1) ^ 1), a.err)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(qdo_full(st), 2 * kTileBytes);
+        tma_load_4d(sQ(st), &tmQ, 0, q0, h, b, qdo_full(st));
+        tma_load_4d(sdO(st), &tmdO, 0, q0, h, b, qdo_full(st));
+      }
+      for (int it = n_it; it < n_it + 2 && ok; ++it) {
+        const int st = it & 1;
+        if (!mbar_wait(qdo_empty(st), (uint32_t)(((it >> 1) & 1) ^ 1), a.err)) ok = false;
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
+      constexpr uint32_t idG = idesc_bf16_f32(kTile, kHd, 0, 1);   // A K-major, B MN-major
+      constexpr uint32_t idQ = idesc_bf16_f32(kTile, kHd, 1, 1);   // A MN-major (dS from dS^T)
+      bool ok = mbar_wait(kv_full, 0, a.err);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it & 1;
+        if (!mbar_wait(qdo_full(st), (uint32_t)((it >> 1) & 1), a.err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kHd / 16; ++kk) {
+          mma_bf16_ss(tST, desc_k(sK + kk * 32), desc_k(sQ(st) + kk * 32), idS, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tDPT, desc_k(sV + kk * 32), desc_k(sdO(st) + kk * 32), idS,
+                      kk > 0 ? 1u : 0u);
+        }
+        mma_commit(st_full);
+        if (!mbar_wait(pds_full, (uint32_t)(it & 1), a.err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_bf16_ss(tDV, desc_k(sPT + aoff), desc_mn(sdO(st) + kk * 2048), idG,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tDK, desc_k(sDST + aoff), desc_mn(sQ(st) + kk * 2048), idG,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(qdo_empty(st));
+        if (it > 0 && !mbar_wait(dq_free, (uint32_t)((it - 1) & 1), a.err)) { ok = false; break; }
+        tc_fence_after();
+        // dQ_ij = dS K_j: A = dS^T read MN-major (query blocks of 64 are 16 KB
+        // apart), B = K_j MN-major; 16 keys per step = 16 rows of 128 bytes.
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_bf16_ss(tDQ, smem_desc_sw128(sDST + kk * 2048, 16384, 1024),
+                      desc_mn(sK + kk * 2048), idQ, kk > 0 ? 1u : 0u);
+        mma_commit(dq_full);
+      }
+      mma_commit(final_bar);
+      mbar_wait(final_bar, 0, a.err);
+    }
+  } else {
+    // ------------------------------ element math ------------------------------
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;  // key row within the tile / dQ row
+    const int kg = k0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int cbase = half * 64;        // this thread's query columns [cbase, cbase + 64)
+    const float sl2 = a.scale * kLog2e;
+    const int64_t bh = (int64_t)b * a.H + h;
+    float* part_base = dq_part + bh * dq_slots(n_t, a.causal) * kDqTileFloats;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int st = it & 1;
+      const int qt = first_q + it;
+      const int q0 = qt * kTile;
+      {
+        const int t = threadIdx.x;  // 0..255
+        const int qi = q0 + (t & 127);
+        if (t < 128)
+          lse_s[st * kTile + t] = qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
+        else
+          delta_s[st * kTile + (t - 128)] = qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
+      }
+      named_barrier(1, 256);
+      if (ok && !mbar_wait(st_full, (uint32_t)(it & 1), a.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) continue;  // every warp still takes each named barrier
+      tc_fence_after();
+      const bool diag = a.causal && qt == kt;
+      const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
+      const bool masked_tile = diag || tail;
+      // P^T and dS^T for this thread's 64 query columns, 32 at a time; the
+      // masked variant only runs on the diagonal tile and a ragged edge.
+      auto chunk = [&](auto masked_c, int col) {
+        constexpr bool kMasked = decltype(masked_c)::value;
+        uint32_t vs[32], vd[32];
+        tmem_ld32(tST + lane_off + col, vs);
+        tmem_ld32(tDPT + lane_off + col, vd);
+        const float4* l4 = reinterpret_cast<const float4*>(lse_s + st * kTile + col);
+        const float4* d4 = reinterpret_cast<const float4*>(delta_s + st * kTile + col);
+        tmem_wait_ld();
+        float p[32], ds[32];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          const float4 lv = l4[g], dv4 = d4[g];
+          const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
+          const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int e = 4 * g + u;
+            float pe = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
+            if (kMasked) {
+              const int qg = q0 + col + e;
+              if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe = 0.f;
+            }
+            p[e] = pe;
+            ds[e] = pe * (__uint_as_float(vd[e]) - dl[u]);
+          }
+        }
+        store_row32(sPT, r, col >> 5, p);
+        store_row32(sDST, r, col >> 5, ds);
+      };
+      if (masked_tile) {
+        chunk(std::true_type{}, cbase);
+        chunk(std::true_type{}, cbase + 32);
+      } else {
+        chunk(std::false_type{}, cbase);
+        chunk(std::false_type{}, cbase + 32);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_full);
+      // drain dQ_ij: row r, columns [32*half, 32*half + 32)
+      if (!mbar_wait(dq_full, (uint32_t)(it & 1), a.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) continue;  // every warp still takes each named barrier
+      tc_fence_after();
+      {
+        uint32_t v[32];
+        tmem_ld32(tDQ + lane_off + half * 32, v);
+        tmem_wait_ld();
+        float4* dst = reinterpret_cast<float4*>(
+            part_base + dq_slot(qt, kt, n_t, a.causal) * kDqTileFloats + r * kHd + half * 32);
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          dst[g] = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                               __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    if (ok && !mbar_wait(final_bar, 0, a.err)) ok = false;
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tDV + lane_off + half * 32, v0);
+      tmem_ld32(tDK + lane_off + half * 32, v1);
+      tmem_wait_ld();
+      if (kg < a.S) {
+        const int64_t off =
+            (int64_t)b * a.qs0 + (int64_t)h * a.qs1 + (int64_t)kg * a.qs2 + half * 32;
+        __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.dv) + off;
+        __nv_bfloat16* dkp = static_cast<__nv_bfloat16*>(a.dk) + off;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 u, w;
+          u.x = pack_bf16(__uint_as_float(v0[8 * g + 0]), __uint_as_float(v0[8 * g + 1]));
+          u.y = pack_bf16(__uint_as_float(v0[8 * g + 2]), __uint_as_float(v0[8 * g + 3]));
+          u.z = pack_bf16(__uint_as_float(v0[8 * g + 4]), __uint_as_float(v0[8 * g + 5]));
+          u.w = pack_bf16(__uint_as_float(v0[8 * g + 6]), __uint_as_float(v0[8 * g + 7]));
+          w.x = pack_bf16(__uint_as_float(v1[8 * g + 0]) * a.scale,
+                          __uint_as_float(v1[8 * g + 1]) * a.scale);
+          w.y = pack_bf16(__uint_as_float(v1[8 * g + 2]) * a.scale,
+                          __uint_as_float(v1[8 * g + 3]) * a.scale);
+          w.z = pack_bf16(__uint_as_float(v1[8 * g + 4]) * a.scale,
+                          __uint_as_float(v1[8 * g + 5]) * a.scale);
+          w.w = pack_bf16(__uint_as_float(v1[8 * g + 6]) * a.scale,
+                          __uint_as_float(v1[8 * g + 7]) * a.scale);
+          reinterpret_cast<uint4*>(dvp)[g] = u;
+          reinterpret_cast<uint4*>(dkp)[g] = w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[b, h, s] = sum_d dO * O over a row of 64 (BF16): 8 threads per row,
+// 16-byte loads, 32 rows per CTA; grid (ceil(S / 32), H, B).
+__global__ void __launch_bounds__(256)
+attn_delta_tc(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
+              float* __restrict__ delta, int S, int H, int64_t os0, int64_t os1, int64_t os2) {
+  const int row = blockIdx.x * 32 + (threadIdx.x >> 3);
+  const int part = threadIdx.x & 7;
+  const int h = blockIdx.y, b = blockIdx.z;
+  float acc = 0.f;
+  if (row < S) {
+    const int64_t off = (int64_t)b * os0 + (int64_t)h * os1 + (int64_t)row * os2 + part * 8;
+    float x[8], y[8];
+    load8(o + off, x);
+    load8(d_o + off, y);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += x[i] * y[i];
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  if (part == 0 && row < S) delta[((int64_t)b * H + h) * S + row] = acc;
+}
+
+// dQ[b, h, q] = scale * sum over key tiles j (in order) of the F32 partials
+// of query tile i -> BF16 (caller's strided layout). One CTA per (i, h, b);
+// thread = 4 consecutive columns of 8 rows.
+__global__ void __launch_bounds__(256)
+attn_dq_reduce(const float* __restrict__ dq_part, __nv_bfloat16* __restrict__ dq, int S, int H,
+               int causal, float scale, int64_t qs0, int64_t qs1, int64_t qs2) {
+  const int n_t = (S + kTile - 1) / kTile;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int64_t bh = (int64_t)b * H + h;
+  const float* base = dq_part + bh * dq_slots(n_t, causal) * kDqTileFloats;
+  const int j_end = causal ? qt + 1 : n_t;
+#pragma unroll 1
+  for (int g = threadIdx.x; g < kDqTileFloats / 4; g += blockDim.x) {
+    const int row = g / (kHd / 4), col = (g % (kHd / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < j_end; ++j) {
+      const float4 t = reinterpret_cast<const float4*>(
+          base + dq_slot(qt, j, n_t, causal) * kDqTileFloats)[g];
+      acc.x += t.x;
+      acc.y += t.y;
+      acc.z += t.z;
+      acc.w += t.w;
+    }
+    const int q = qt * kTile + row;
+    if (q < S) {
+      uint2 u;
+      u.x = pack_bf16(acc.x * scale, acc.y * scale);
+      u.y = pack_bf16(acc.z * scale, acc.w * scale);
+      *reinterpret_cast<uint2*>(dq + (int64_t)b * qs0 + (int64_t)h * qs1 + (int64_t)q * qs2 +
+                                col) = u;
+    }
+  }
+}
+
 // 4-D tensor map over a [B, H, S, 64] BF16 view with element strides
 // (sb, sh, ss), box [128 rows x 64] with 128-byte swizzle.
 magma_status_t head_map(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t S,
@@ -908,12 +1256,26 @@ magma_status_t attention_fwd_tc(const void* q, const void* k, const void* v, voi
   return check_launch("attention_fwd_tcgen05");
 }
 
+// Workspace of the fused backward: delta (B*H*S floats), then the F32 dQ
+// partial tiles (query tile x key tile pairs of every head).
+size_t attention_bwd_tc_partials_bytes(int64_t B, int64_t H, int64_t S, int causal) {
+  const int n_t = (int)ceil_div(S, kTile);
+  return (size_t)(B * H) * (size_t)dq_slots(n_t, causal) * kDqTileFloats * sizeof(float);
+}
+size_t attention_bwd_tc_delta_bytes(int64_t B, int64_t H, int64_t S) {
+  return ((size_t)(B * H * S) * sizeof(float) + 255) & ~(size_t)255;
+}
+
 magma_status_t attention_bwd_tc(const void* q, const void* k, const void* v, const void* o,
                                 const void* d_o, const float* lse, void* dq, void* dk, void* dv,
-                                float* delta, int64_t B, int64_t H, int64_t S, const int64_t* qs,
-                                const int64_t* os, float scale, int causal, cudaStream_t s) {
-  if (magma_status_t st = attention_bwd_delta(o, d_o, delta, B, H, S, kHd, os, MAGMA_DTYPE_BF16, s))
-    return st;
+                                void* workspace, size_t ws_bytes, int64_t B, int64_t H, int64_t S,
+                                const int64_t* qs, const int64_t* os, float scale, int causal,
+                                cudaStream_t s) {
+  float* delta = static_cast<float*>(workspace);
+  attn_delta_tc<<<dim3((unsigned)ceil_div(S, 32), (unsigned)H, (unsigned)B), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(d_o), delta, (int)S,
+      (int)H, os[0], os[1], os[2]);
+  if (magma_status_t st = check_launch("attention_bwd_delta")) return st;
   CUtensorMap mq, mk, mv, mdo;
   if (magma_status_t st = head_map(&mq, q, B, H, S, qs[0], qs[1], qs[2])) return st;
   if (magma_status_t st = head_map(&mk, k, B, H, S, qs[0], qs[1], qs[2])) return st;
@@ -926,9 +1288,20 @@ magma_status_t attention_bwd_tc(const void* q, const void* k, const void* v, con
   a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
   a.qs0 = qs[0]; a.qs1 = qs[1]; a.qs2 = qs[2];
   a.err = device_error_word();
+  dim3 grid((unsigned)ceil_div(S, kTile), (unsigned)H, (unsigned)B);
+  const size_t dbytes = attention_bwd_tc_delta_bytes(B, H, S);
+  if (ws_bytes >= dbytes + attention_bwd_tc_partials_bytes(B, H, S, causal)) {
+    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dbytes);
+    if (magma_status_t st = set_smem_attr<3>(attn_bwd_tc, kBwSmem)) return st;
+    attn_bwd_tc<<<grid, kBwThreads, kBwSmem, s>>>(mq, mk, mv, mdo, a, part);
+    if (magma_status_t st = check_launch("attention_bwd_tcgen05")) return st;
+    attn_dq_reduce<<<grid, 256, 0, s>>>(part, static_cast<__nv_bfloat16*>(dq), (int)S, (int)H,
+                                        causal, scale, qs[0], qs[1], qs[2]);
+    return check_launch("attention_bwd_dq_reduce");
+  }
+  // Without room for the partials: dK/dV and dQ in two passes.
   if (magma_status_t st = set_smem_attr<1>(attn_bwd_dkdv_tc, kKvSmem)) return st;
   if (magma_status_t st = set_smem_attr<2>(attn_bwd_dq_tc, kDqSmem)) return st;
-  dim3 grid((unsigned)ceil_div(S, kTile), (unsigned)H, (unsigned)B);
   attn_bwd_dkdv_tc<<<grid, kThreads, kKvSmem, s>>>(mq, mk, mv, mdo, a);
   if (magma_status_t st = check_launch("attention_bwd_dkdv_tcgen05")) return st;
   attn_bwd_dq_tc<<<grid, kThreads, kDqSmem, s>>>(mq, mk, mv, mdo, a);

@@ -6,6 +6,7 @@ F32 attention/GEMM rel 1e-4, BF16 rel 2e-2, where "rel" is elementwise
 from demanding more than the tensor's own scale allows. Integer/index outputs
 are compared exactly.
 """
+import ctypes
 import math
 
 import numpy as np
@@ -334,6 +335,39 @@ def test_attention_bf16(cuda, oracle, shape, causal):
     close_norm(dq.float().cpu(), rdq, 2e-2)
     close_norm(dk.float().cpu(), rdk, 2e-2)
     close_norm(dv.float().cpu(), rdv, 2e-2)
+
+
+@pytest.mark.parametrize("shape,causal", [((2, 3, 384, 64), True), ((1, 2, 200, 64), False)])
+def test_attention_bf16_bwd_two_pass_fallback(cuda, oracle, shape, causal):
+    """With a workspace that only holds the row terms (no room for the dQ
+    partial tiles), the backward takes the two-pass kernels; both paths match
+    the oracle."""
+    from magma_b200 import lib, ops
+
+    rng = np.random.default_rng(sum(shape) + 7)
+    q, k, v, do = qkv(rng, shape, torch.bfloat16)
+    scale = 1 / math.sqrt(shape[-1])
+    bt = lambda a: t(a, torch.bfloat16)  # noqa: E731
+    tq, tk, tv, tdo = bt(q), bt(k), bt(v), bt(do)
+    o, lse = ops.attention_fwd(tq, tk, tv, scale, causal)
+    B, H, S, D = shape
+    full = lib.query("magma_attention_bwd_workspace_size", B, H, S, D, lib.BF16)
+    small = (B * H * S * 4 + 255) // 256 * 256
+    assert full > small
+    ws = torch.empty(small, dtype=torch.uint8, device="cuda")
+    dq, dk, dv = (torch.empty_like(tq) for _ in range(3))
+    lib.call("magma_attention_bwd", tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), o.data_ptr(),
+             tdo.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+             B, H, S, D, (ctypes.c_int64 * 3)(*tq.stride()[:3]), (ctypes.c_int64 * 3)(*o.stride()[:3]),
+             scale, int(causal), lib.BF16, ws.data_ptr(), small,
+             torch.cuda.current_stream().cuda_stream)
+    fq, fk, fv = ops.attention_bwd(tq, tk, tv, o, tdo, lse, scale, causal)
+    torch.cuda.synchronize()
+    assert ops.device_error_check() == 0
+    rdq, rdk, rdv = oracle.attention_bwd(q, k, v, do, scale, causal)
+    for got, fused, want in ((dq, fq, rdq), (dk, fk, rdk), (dv, fv, rdv)):
+        close_norm(got.float().cpu(), want, 2e-2)
+        close_norm(fused.float().cpu(), want, 2e-2)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])

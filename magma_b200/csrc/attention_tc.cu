@@ -861,13 +861,14 @@ constexpr int kBwThreads = 320;
 constexpr int kBwK = 0;
 constexpr int kBwV = kTileBytes;
 constexpr int kBwQdo = 2 * kTileBytes;                      // 2 stages x (Q, dO)
-constexpr int kBwPT = kBwQdo + 2 * 2 * kTileBytes;          // 32 KB
-constexpr int kBwDST = kBwPT + 2 * kTileBytes;              // 32 KB
-constexpr int kBwStats = kBwDST + 2 * kTileBytes;           // lse2[2][128], delta[2][128]
-constexpr int kBwBar = kBwStats + 4 * kTile * 4;
-// kv_full, qdo_full[2], qdo_empty[2], st_full, pds_full, dq_full, dq_free, final
-constexpr int kBwNumBars = 10;
+constexpr int kBwPT = kBwQdo + 2 * 2 * kTileBytes;          // 2 buffers x 32 KB
+constexpr int kBwDST = kBwPT + 2 * 2 * kTileBytes;          // 2 buffers x 32 KB
+constexpr int kBwStats = kBwDST + 2 * 2 * kTileBytes;       // lse2[128], delta[128]
+constexpr int kBwBar = kBwStats + 2 * kTile * 4;
+// kv_full, qdo_full[2], qdo_empty[2], st_full, pds_full, dq_full[2], dq_free[2], final
+constexpr int kBwNumBars = 12;
 constexpr int kBwSmem = kBwBar + kBwNumBars * 8 + 16 + 1024;
+static_assert(kBwSmem <= 232448, "attention backward shared memory");
 constexpr int kDqTileFloats = kTile * kHd;                  // one F32 dQ partial tile
 
 // Index of the dQ partial of (query tile i, key tile j) among a head's slots.
@@ -878,6 +879,12 @@ __host__ __device__ __forceinline__ int64_t dq_slots(int n_t, int causal) {
   return causal ? (int64_t)n_t * (n_t + 1) / 2 : (int64_t)n_t * n_t;
 }
 
+// Pipeline over query tiles it = 0, 1, ... (P^T/dS^T buffers and dQ TMEM
+// buffers alternate with it):
+//   MMA warp:  S(0) | [P(it) ready] S(it+1) dQ(it) dV(it) dK(it) | ...
+//   math warps: softmax(it) -> P(it) ready -> drain dQ(it-1) -> softmax(it+1)
+// so the tensor cores run dQ/dV/dK of one tile under the exponentials of the
+// next; S(it+1) is issued first so that the next softmax can start early.
 __global__ void __launch_bounds__(kBwThreads, 1)
 attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -888,18 +895,19 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   const uint32_t sK = base + kBwK, sV = base + kBwV;
   auto sQ = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes; };
   auto sdO = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes + kTileBytes; };
-  const uint32_t sPT = base + kBwPT, sDST = base + kBwDST;
-  float* lse_s = reinterpret_cast<float*>(sp + kBwStats);           // [2][128], log2 units
-  float* delta_s = reinterpret_cast<float*>(sp + kBwStats + 2 * kTile * 4);
+  auto sPT = [&](int pb) { return base + kBwPT + pb * 2 * kTileBytes; };
+  auto sDST = [&](int pb) { return base + kBwDST + pb * 2 * kTileBytes; };
+  float* lse_s = reinterpret_cast<float*>(sp + kBwStats);           // [128], log2 units
+  float* delta_s = reinterpret_cast<float*>(sp + kBwStats + kTile * 4);
   const uint32_t bars = base + kBwBar;
   const uint32_t kv_full = bars;
   auto qdo_full = [&](int st) { return bars + 8u * (1 + st); };
   auto qdo_empty = [&](int st) { return bars + 8u * (3 + st); };
   const uint32_t st_full = bars + 8u * 5;
   const uint32_t pds_full = bars + 8u * 6;
-  const uint32_t dq_full = bars + 8u * 7;
-  const uint32_t dq_free = bars + 8u * 8;
-  const uint32_t final_bar = bars + 8u * 9;
+  auto dq_full = [&](int db) { return bars + 8u * (7 + db); };
+  auto dq_free = [&](int db) { return bars + 8u * (9 + db); };
+  const uint32_t final_bar = bars + 8u * 11;
   const uint32_t tslot = bars + 8u * kBwNumBars;
   uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kBwBar + 8 * kBwNumBars);
 
@@ -920,11 +928,11 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     for (int st = 0; st < 2; ++st) {
       mbar_init(qdo_full(st), 1);
       mbar_init(qdo_empty(st), 1);
+      mbar_init(dq_full(st), 1);
+      mbar_init(dq_free(st), 8);
     }
     mbar_init(st_full, 1);
     mbar_init(pds_full, 8);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_free, 8);
     mbar_init(final_bar, 1);
     fence_barrier_init();
   }
@@ -933,8 +941,8 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
-  const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320,
-                 tDQ = tmem + 384;
+  const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320;
+  auto tDQ = [&](int db) { return tmem + 384u + (uint32_t)(db * kHd); };
 
   if (warp == 8) {
     if (lane == 0) {
@@ -963,10 +971,9 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
       constexpr uint32_t idG = idesc_bf16_f32(kTile, kHd, 0, 1);   // A K-major, B MN-major
       constexpr uint32_t idQ = idesc_bf16_f32(kTile, kHd, 1, 1);   // A MN-major (dS from dS^T)
-      bool ok = mbar_wait(kv_full, 0, a.err);
-      for (int it = 0; it < n_it && ok; ++it) {
+      auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
-        if (!mbar_wait(qdo_full(st), (uint32_t)((it >> 1) & 1), a.err)) { ok = false; break; }
+        if (!mbar_wait(qdo_full(st), (uint32_t)((it >> 1) & 1), a.err)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk) {
@@ -975,26 +982,38 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                       kk > 0 ? 1u : 0u);
         }
         mma_commit(st_full);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, a.err);
+      if (ok && n_it > 0) ok = issue_s(0);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it & 1, pb = it & 1;
         if (!mbar_wait(pds_full, (uint32_t)(it & 1), a.err)) { ok = false; break; }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_bf16_ss(tDV, desc_k(sPT + aoff), desc_mn(sdO(st) + kk * 2048), idG,
-                      (it > 0 || kk > 0) ? 1u : 0u);
-          mma_bf16_ss(tDK, desc_k(sDST + aoff), desc_mn(sQ(st) + kk * 2048), idG,
-                      (it > 0 || kk > 0) ? 1u : 0u);
+        // S(it+1) overwrites S/dP(it), which the math warps have finished reading
+        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
+        // dQ buffer pb was last used by dQ(it-2); its drain must be done
+        if (it >= 2 && !mbar_wait(dq_free(pb), (uint32_t)(((it - 2) >> 1) & 1), a.err)) {
+          ok = false;
+          break;
         }
-        mma_commit(qdo_empty(st));
-        if (it > 0 && !mbar_wait(dq_free, (uint32_t)((it - 1) & 1), a.err)) { ok = false; break; }
         tc_fence_after();
         // dQ_ij = dS K_j: A = dS^T read MN-major (query blocks of 64 are 16 KB
         // apart), B = K_j MN-major; 16 keys per step = 16 rows of 128 bytes.
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          mma_bf16_ss(tDQ, smem_desc_sw128(sDST + kk * 2048, 16384, 1024),
+          mma_bf16_ss(tDQ(pb), smem_desc_sw128(sDST(pb) + kk * 2048, 16384, 1024),
                       desc_mn(sK + kk * 2048), idQ, kk > 0 ? 1u : 0u);
-        mma_commit(dq_full);
+        mma_commit(dq_full(pb));
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_bf16_ss(tDV, desc_k(sPT(pb) + aoff), desc_mn(sdO(st) + kk * 2048), idG,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tDK, desc_k(sDST(pb) + aoff), desc_mn(sQ(st) + kk * 2048), idG,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(qdo_empty(st));
       }
       mma_commit(final_bar);
       mbar_wait(final_bar, 0, a.err);
@@ -1009,89 +1028,97 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const float sl2 = a.scale * kLog2e;
     const int64_t bh = (int64_t)b * a.H + h;
     float* part_base = dq_part + bh * dq_slots(n_t, a.causal) * kDqTileFloats;
+    const int t = threadIdx.x;  // 0..255: lse (t < 128) or delta of query row t & 127
+    auto load_stat = [&](int it) -> float {
+      const int qi = (first_q + it) * kTile + (t & 127);
+      if (t < 128) return qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
+      return qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
+    };
+    // Drains dQ(it) (TMEM buffer it & 1): row r, columns [32*half, 32*half+32)
+    // into the (query tile, key tile) partial slot.
+    auto drain = [&](int it, bool ok) -> bool {
+      const int db = it & 1;
+      if (ok && !mbar_wait(dq_full(db), (uint32_t)((it >> 1) & 1), a.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) return false;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld32(tDQ(db) + lane_off + half * 32, v);
+      tmem_wait_ld();
+      float4* dst = reinterpret_cast<float4*>(
+          part_base + dq_slot(first_q + it, kt, n_t, a.causal) * kDqTileFloats + r * kHd +
+          half * 32);
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        dst[g] = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                             __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free(db));
+      return true;
+    };
     bool ok = true;
+    float stat = n_it > 0 ? load_stat(0) : 0.f;
     for (int it = 0; it < n_it; ++it) {
-      const int st = it & 1;
+      const int pb = it & 1;
       const int qt = first_q + it;
       const int q0 = qt * kTile;
-      {
-        const int t = threadIdx.x;  // 0..255
-        const int qi = q0 + (t & 127);
-        if (t < 128)
-          lse_s[st * kTile + t] = qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
-        else
-          delta_s[st * kTile + (t - 128)] = qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
-      }
+      (t < 128 ? lse_s[t] : delta_s[t - 128]) = stat;
+      if (it + 1 < n_it) stat = load_stat(it + 1);  // lands during this tile
       named_barrier(1, 256);
       if (ok && !mbar_wait(st_full, (uint32_t)(it & 1), a.err)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) continue;  // every warp still takes each named barrier
-      tc_fence_after();
-      const bool diag = a.causal && qt == kt;
-      const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
-      const bool masked_tile = diag || tail;
-      // P^T and dS^T for this thread's 64 query columns, 32 at a time; the
-      // masked variant only runs on the diagonal tile and a ragged edge.
-      auto chunk = [&](auto masked_c, int col) {
-        constexpr bool kMasked = decltype(masked_c)::value;
-        uint32_t vs[32], vd[32];
-        tmem_ld32(tST + lane_off + col, vs);
-        tmem_ld32(tDPT + lane_off + col, vd);
-        const float4* l4 = reinterpret_cast<const float4*>(lse_s + st * kTile + col);
-        const float4* d4 = reinterpret_cast<const float4*>(delta_s + st * kTile + col);
-        tmem_wait_ld();
-        float p[32], ds[32];
+      if (ok) {
+        tc_fence_after();
+        const bool diag = a.causal && qt == kt;
+        const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
+        // P^T and dS^T for this thread's 64 query columns, 32 at a time; the
+        // masked variant only runs on the diagonal tile and a ragged edge.
+        auto chunk = [&](auto masked_c, int col) {
+          constexpr bool kMasked = decltype(masked_c)::value;
+          uint32_t vs[32], vd[32];
+          tmem_ld32(tST + lane_off + col, vs);
+          tmem_ld32(tDPT + lane_off + col, vd);
+          const float4* l4 = reinterpret_cast<const float4*>(lse_s + col);
+          const float4* d4 = reinterpret_cast<const float4*>(delta_s + col);
+          tmem_wait_ld();
+          float p[32], ds[32];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const float4 lv = l4[g], dv4 = d4[g];
-          const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
-          const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
+          for (int g = 0; g < 8; ++g) {
+            const float4 lv = l4[g], dv4 = d4[g];
+            const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
+            const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int e = 4 * g + u;
-            float pe = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
-            if (kMasked) {
-              const int qg = q0 + col + e;
-              if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe = 0.f;
+            for (int u = 0; u < 4; ++u) {
+              const int e = 4 * g + u;
+              float pe = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
+              float de = pe * (__uint_as_float(vd[e]) - dl[u]);
+              if (kMasked) {
+                const int qg = q0 + col + e;
+                if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe = de = 0.f;
+              }
+              p[e] = pe;
+              ds[e] = de;
             }
-            p[e] = pe;
-            ds[e] = pe * (__uint_as_float(vd[e]) - dl[u]);
           }
+          store_row32(sPT(pb), r, col >> 5, p);
+          store_row32(sDST(pb), r, col >> 5, ds);
+        };
+        if (diag || tail) {
+          chunk(std::true_type{}, cbase);
+          chunk(std::true_type{}, cbase + 32);
+        } else {
+          chunk(std::false_type{}, cbase);
+          chunk(std::false_type{}, cbase + 32);
         }
-        store_row32(sPT, r, col >> 5, p);
-        store_row32(sDST, r, col >> 5, ds);
-      };
-      if (masked_tile) {
-        chunk(std::true_type{}, cbase);
-        chunk(std::true_type{}, cbase + 32);
-      } else {
-        chunk(std::false_type{}, cbase);
-        chunk(std::false_type{}, cbase + 32);
+        fence_proxy_async_smem();
+        tc_fence_before();
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pds_full);
-      // drain dQ_ij: row r, columns [32*half, 32*half + 32)
-      if (!mbar_wait(dq_full, (uint32_t)(it & 1), a.err)) ok = false;
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) continue;  // every warp still takes each named barrier
-      tc_fence_after();
-      {
-        uint32_t v[32];
-        tmem_ld32(tDQ + lane_off + half * 32, v);
-        tmem_wait_ld();
-        float4* dst = reinterpret_cast<float4*>(
-            part_base + dq_slot(qt, kt, n_t, a.causal) * kDqTileFloats + r * kHd + half * 32);
-#pragma unroll
-        for (int g = 0; g < 8; ++g)
-          dst[g] = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
-                               __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
+      named_barrier(2, 256);  // every thread is done with the row terms of this tile
+      if (ok && lane == 0) mbar_arrive(pds_full);
+      if (it >= 1) ok = drain(it - 1, ok) && ok;
     }
+    if (n_it >= 1) ok = drain(n_it - 1, ok) && ok;
     if (ok && !mbar_wait(final_bar, 0, a.err)) ok = false;
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {

@@ -861,14 +861,12 @@ constexpr int kBwThreads = 320;
 constexpr int kBwK = 0;
 constexpr int kBwV = kTileBytes;
 constexpr int kBwQdo = 2 * kTileBytes;                      // 2 stages x (Q, dO)
-constexpr int kBwPT = kBwQdo + 2 * 2 * kTileBytes;          // 2 buffers x 32 KB
-constexpr int kBwDST = kBwPT + 2 * 2 * kTileBytes;          // 2 buffers x 32 KB
+constexpr int kBwDST = kBwQdo + 2 * 2 * kTileBytes;         // 2 buffers x 32 KB
 constexpr int kBwStats = kBwDST + 2 * 2 * kTileBytes;       // lse2[128], delta[128]
 constexpr int kBwBar = kBwStats + 2 * kTile * 4;
 // kv_full, qdo_full[2], qdo_empty[2], st_full, pds_full, dq_full[2], dq_free[2], final
 constexpr int kBwNumBars = 12;
 constexpr int kBwSmem = kBwBar + kBwNumBars * 8 + 16 + 1024;
-static_assert(kBwSmem <= 232448, "attention backward shared memory");
 constexpr int kDqTileFloats = kTile * kHd;                  // one F32 dQ partial tile
 
 // Index of the dQ partial of (query tile i, key tile j) among a head's slots.
@@ -878,13 +876,29 @@ __host__ __device__ __forceinline__ int64_t dq_slot(int i, int j, int n_t, int c
 __host__ __device__ __forceinline__ int64_t dq_slots(int n_t, int causal) {
   return causal ? (int64_t)n_t * (n_t + 1) / 2 : (int64_t)n_t * n_t;
 }
+// A partial tile is stored as 16 column groups of 4 floats x 128 rows, i.e.
+// float4 index (column / 4) * 128 + row, so that a warp's stores of one column
+// group over its 32 rows are 512 contiguous bytes.
 
-// Pipeline over query tiles it = 0, 1, ... (P^T/dS^T buffers and dQ TMEM
-// buffers alternate with it):
-//   MMA warp:  S(0) | [P(it) ready] S(it+1) dQ(it) dV(it) dK(it) | ...
+// Writes 32 packed BF16 pairs (64 columns) of row r at columns [64*half,
+// 64*half+64) of a [128 x 128] K-major SW128 tile.
+__device__ __forceinline__ void store_row_packed(uint32_t base, int r, int c32,
+                                                 const uint32_t* pk) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    st_shared_v4(swz_chunk_addr(base, r, c32 * 4 + q), pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                 pk[4 * q + 3]);
+}
+
+// Pipeline over query tiles it = 0, 1, ...:
+//   MMA warp:   S(0) | [P(it) ready] dV(it) dK(it) S(it+1) dQ(it) | ...
 //   math warps: softmax(it) -> P(it) ready -> drain dQ(it-1) -> softmax(it+1)
-// so the tensor cores run dQ/dV/dK of one tile under the exponentials of the
-// next; S(it+1) is issued first so that the next softmax can start early.
+// P^T and dS^T are written back into TMEM over the S^T and dP^T columns each
+// thread has read (thread half h: columns [64h, 64h+32)) and are the A
+// operands of dV and dK, read from TMEM; dS^T also goes to shared memory as
+// the MN-major A operand of dQ. dQ alternates between two TMEM buffers, dS^T
+// between two shared buffers, so dQ(it) and the drain of dQ(it-1) run under
+// the exponentials of tile it+1.
 __global__ void __launch_bounds__(kBwThreads, 1)
 attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -895,7 +909,6 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   const uint32_t sK = base + kBwK, sV = base + kBwV;
   auto sQ = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes; };
   auto sdO = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes + kTileBytes; };
-  auto sPT = [&](int pb) { return base + kBwPT + pb * 2 * kTileBytes; };
   auto sDST = [&](int pb) { return base + kBwDST + pb * 2 * kTileBytes; };
   float* lse_s = reinterpret_cast<float*>(sp + kBwStats);           // [128], log2 units
   float* delta_s = reinterpret_cast<float*>(sp + kBwStats + kTile * 4);
@@ -990,7 +1003,18 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const int st = it & 1, pb = it & 1;
         if (!mbar_wait(pds_full, (uint32_t)(it & 1), a.err)) { ok = false; break; }
         tc_fence_after();
-        // S(it+1) overwrites S/dP(it), which the math warps have finished reading
+        // dV += P^T dO, dK += dS^T Q with P^T / dS^T read from TMEM: queries
+        // [0, 64) at columns [0, 32), queries [64, 128) at columns [64, 96).
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          const uint32_t acol = (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
+          mma_bf16_ts(tDV, tST + acol, desc_mn(sdO(st) + kk * 2048), idG,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tDK, tDPT + acol, desc_mn(sQ(st) + kk * 2048), idG,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(qdo_empty(st));
+        // S(it+1) overwrites P^T / dS^T(it): issued after the MMAs reading them
         if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
         // dQ buffer pb was last used by dQ(it-2); its drain must be done
         if (it >= 2 && !mbar_wait(dq_free(pb), (uint32_t)(((it - 2) >> 1) & 1), a.err)) {
@@ -1005,15 +1029,6 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           mma_bf16_ss(tDQ(pb), smem_desc_sw128(sDST(pb) + kk * 2048, 16384, 1024),
                       desc_mn(sK + kk * 2048), idQ, kk > 0 ? 1u : 0u);
         mma_commit(dq_full(pb));
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_bf16_ss(tDV, desc_k(sPT(pb) + aoff), desc_mn(sdO(st) + kk * 2048), idG,
-                      (it > 0 || kk > 0) ? 1u : 0u);
-          mma_bf16_ss(tDK, desc_k(sDST(pb) + aoff), desc_mn(sQ(st) + kk * 2048), idG,
-                      (it > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(qdo_empty(st));
       }
       mma_commit(final_bar);
       mbar_wait(final_bar, 0, a.err);
@@ -1034,8 +1049,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       if (t < 128) return qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
       return qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
     };
-    // Drains dQ(it) (TMEM buffer it & 1): row r, columns [32*half, 32*half+32)
-    // into the (query tile, key tile) partial slot.
+    // Drains dQ(it) (TMEM buffer it & 1): row r, column groups 8*half .. +8.
     auto drain = [&](int it, bool ok) -> bool {
       const int db = it & 1;
       if (ok && !mbar_wait(dq_full(db), (uint32_t)((it >> 1) & 1), a.err)) ok = false;
@@ -1046,12 +1060,12 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tmem_ld32(tDQ(db) + lane_off + half * 32, v);
       tmem_wait_ld();
       float4* dst = reinterpret_cast<float4*>(
-          part_base + dq_slot(first_q + it, kt, n_t, a.causal) * kDqTileFloats + r * kHd +
-          half * 32);
+          part_base + dq_slot(first_q + it, kt, n_t, a.causal) * kDqTileFloats);
 #pragma unroll
       for (int g = 0; g < 8; ++g)
-        dst[g] = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
-                             __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+        dst[(half * 8 + g) * kTile + r] =
+            make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                        __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free(db));
@@ -1074,43 +1088,51 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
         // P^T and dS^T for this thread's 64 query columns, 32 at a time; the
         // masked variant only runs on the diagonal tile and a ragged edge.
-        auto chunk = [&](auto masked_c, int col) {
+        auto chunk = [&](auto masked_c, int c) {
           constexpr bool kMasked = decltype(masked_c)::value;
+          const int col = cbase + 32 * c;
           uint32_t vs[32], vd[32];
           tmem_ld32(tST + lane_off + col, vs);
           tmem_ld32(tDPT + lane_off + col, vd);
           const float4* l4 = reinterpret_cast<const float4*>(lse_s + col);
           const float4* d4 = reinterpret_cast<const float4*>(delta_s + col);
           tmem_wait_ld();
-          float p[32], ds[32];
+          uint32_t pp[16], pd[16];
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
             const float4 lv = l4[g], dv4 = d4[g];
             const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
             const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
+            float pe[4], de[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int e = 4 * g + u;
-              float pe = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
-              float de = pe * (__uint_as_float(vd[e]) - dl[u]);
+              pe[u] = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
+              de[u] = pe[u] * (__uint_as_float(vd[e]) - dl[u]);
               if (kMasked) {
                 const int qg = q0 + col + e;
-                if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe = de = 0.f;
+                if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe[u] = de[u] = 0.f;
               }
-              p[e] = pe;
-              ds[e] = de;
             }
+            pp[2 * g] = pack_bf16(pe[0], pe[1]);
+            pp[2 * g + 1] = pack_bf16(pe[2], pe[3]);
+            pd[2 * g] = pack_bf16(de[0], de[1]);
+            pd[2 * g + 1] = pack_bf16(de[2], de[3]);
           }
-          store_row32(sPT(pb), r, col >> 5, p);
-          store_row32(sDST(pb), r, col >> 5, ds);
+          // BF16 columns [64*half + 16*c, +16): S^T / dP^T columns this thread
+          // has already read
+          tmem_st16(tST + lane_off + cbase + 16 * c, pp);
+          tmem_st16(tDPT + lane_off + cbase + 16 * c, pd);
+          store_row_packed(sDST(pb), r, col >> 5, pd);
         };
         if (diag || tail) {
-          chunk(std::true_type{}, cbase);
-          chunk(std::true_type{}, cbase + 32);
+          chunk(std::true_type{}, 0);
+          chunk(std::true_type{}, 1);
         } else {
-          chunk(std::false_type{}, cbase);
-          chunk(std::false_type{}, cbase + 32);
+          chunk(std::false_type{}, 0);
+          chunk(std::false_type{}, 1);
         }
+        tmem_wait_st();
         fence_proxy_async_smem();
         tc_fence_before();
       }
@@ -1198,7 +1220,7 @@ attn_dq_reduce(const float* __restrict__ dq_part, __nv_bfloat16* __restrict__ dq
   const int j_end = causal ? qt + 1 : n_t;
 #pragma unroll 1
   for (int g = threadIdx.x; g < kDqTileFloats / 4; g += blockDim.x) {
-    const int row = g / (kHd / 4), col = (g % (kHd / 4)) * 4;
+    const int row = g % kTile, col = (g / kTile) * 4;  // column-group-major tiles
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < j_end; ++j) {
       const float4 t = reinterpret_cast<const float4*>(

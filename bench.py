@@ -23,6 +23,7 @@ import argparse
 import json
 import math
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -47,6 +48,20 @@ def load_peaks() -> tuple[dict, str]:
         except Exception:
             pass
     return dict(PEAKS_FALLBACK), "fallback"
+
+
+GEMM_TRAFFIC_PROFILE = ROOT / "profiles" / "gemm_bf16_gpt2_small_dram.txt"
+
+
+def gemm_traffic_per_launch() -> int | None:
+    """DRAM bytes (read + write) per GEMM launch of one step, averaged over the
+    step's 147 GEMM launches, from the committed ncu capture of those shapes
+    (dram__bytes_read.sum + dram__bytes_write.sum); None if it is absent."""
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", GEMM_TRAFFIC_PROFILE.read_text())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
 
 
 def workload_config(world: int, batch: int) -> dict:
@@ -191,9 +206,22 @@ def classify(name, args, cfg, tr):
         dxb = 4 if args[12] == 10 else 2
         acc = dxb if args[13] else 0
         return "layernorm", rows * dim * (dyb + xb + dxb + acc) + rows * 8
+    if name == "magma_layernorm_bwd_residual":
+        rows, dim = args[10], args[11]
+        dyb = 4 if args[12] == 10 else 2
+        acc = 4 if args[13] else 0
+        copy = 2 if args[6] else 0
+        return "layernorm", rows * dim * (dyb + 4 + 4 + acc + copy) + rows * 8
     if name == "magma_adam_step":
         n = args[5]
         return "adam", n * (28 + (2 if args[4] else 0))
+    if name == "magma_cross_entropy_fwd_bwd":
+        rows, ld = args[3], args[5]
+        esz = 4 if args[7] == 10 else 2
+        return "cross_entropy", 2.0 * rows * ld * esz  # one read, one write of the logits
+    if name == "magma_cross_entropy_fwd_bwd_rowstats":
+        rows, classes, ld = args[4], args[5], args[6]
+        return "cross_entropy", 2.0 * rows * ld * 2 + rows * ((classes + 63) // 64) * 8
     return "other", 0.0
 
 
@@ -402,9 +430,11 @@ def main() -> None:
     roof = dict(gemm) if gemm else {}
     roof.update({"kernel": "gemm_tcgen05 (all GEMMs of one step)",
                  "peak_source": f"{peak_src} bf16_tflops_sustained (kernels timed inside a step)",
-                 "traffic": None})
+                 "traffic": gemm_traffic_per_launch(),
+                 "traffic_unit": "bytes per launch (ncu DRAM read + write, GEMM shapes of one step)"})
     others = {k: entry(k, b) for k, b in (("attention_fwd", "tensor"), ("attention_bwd", "tensor"),
-                                           ("layernorm", "hbm"), ("adam", "hbm"))}
+                                           ("layernorm", "hbm"), ("adam", "hbm"),
+                                           ("cross_entropy", "hbm"))}
     if rank != 0:
         if world > 1:
             dist.barrier()

@@ -74,6 +74,13 @@ typedef int32_t magma_dtype_t;
 #define MAGMA_EPI_ACCUMULATE 5    /* c = c + acc  (c must be f32)              */
 #define MAGMA_EPI_BIAS_RELU 6     /* aux_out = acc + bias; c = relu(aux_out)   */
 #define MAGMA_EPI_DRELU 7         /* c = acc * (aux_in > 0)                    */
+#define MAGMA_EPI_ROWSTATS 8      /* c = acc; aux_out: softmax partials (below) */
+/* MAGMA_EPI_ROWSTATS (BF16 operands, tensor-core path, no K split): besides
+ * storing c, writes for every row r and every 64-column chunk j of c the pair
+ * (max_j, sum over the chunk of exp(c - max_j)), computed from c as stored
+ * (rounded to c's dtype), to aux_out as float2 [ceil(n / 64)][m] (chunk-major).
+ * magma_cross_entropy_fwd_bwd_rowstats consumes them: the lm-head GEMM and the
+ * softmax cross-entropy then read the logits once instead of twice. */
 
 /* ---- errors (PJRTSimpleWrapper.h:86-99) ------------------------------------ */
 
@@ -164,6 +171,26 @@ MAGMA_API magma_status_t magma_layernorm_bwd_noalloc(const void* dy, const void*
                                    magma_dtype_t dx_dtype,
                                    int32_t accumulate_dx, int32_t accumulate_params,
                                    void* stream);
+
+/* LayerNorm backward into a pre-LN residual stream (no single counterpart in
+ * the reference; it fuses three of the ops its traced GPT step emits after the
+ * LayerNorm VJP: the gradient add into the residual branch, the BF16 cast of
+ * that gradient for the next matmuls, and the bias-gradient column sum of the
+ * Linear whose output the residual stream receives, Autodiff.swift:221-257).
+ * As magma_layernorm_bwd with x and dx F32, plus:
+ *   dx_bf16 (optional, [rows, dim] BF16): a copy of the final dx;
+ *   dcol (optional, [dim] F32): column sums of the final dx over the rows,
+ *   written or (accumulate_params) added like dgamma and dbeta.
+ * dim % 8 == 0, dim <= 1024, 16-byte aligned dy, x, gamma, dx, dx_bf16.
+ * Workspace: magma_layernorm_bwd_residual_workspace_size(rows, dim). */
+MAGMA_API size_t magma_layernorm_bwd_residual_workspace_size(int64_t rows, int64_t dim);
+MAGMA_API magma_status_t magma_layernorm_bwd_residual(const void* dy, const float* x,
+                                   const float* gamma, const float* mean, const float* rstd,
+                                   float* dx, void* dx_bf16, float* dgamma, float* dbeta,
+                                   float* dcol, int64_t rows, int64_t dim,
+                                   magma_dtype_t dy_dtype, int32_t accumulate_dx,
+                                   int32_t accumulate_params, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 
 /* ---- Linear contraction (GEMM) ------------------------------------------------
  * Replaces Tensor.matmul -> stablehlo.dot (Sources/Core/Tensor.swift:1102-1121,
@@ -274,6 +301,15 @@ MAGMA_API magma_status_t magma_embedding_bwd(const int32_t* tokens, const float*
 MAGMA_API magma_status_t magma_cross_entropy_fwd_bwd(void* logits, const int32_t* targets, float* losses,
                                            int64_t rows, int64_t classes, int64_t ld,
                                            float grad_scale, magma_dtype_t dtype, void* stream);
+
+/* As magma_cross_entropy_fwd_bwd for logits written by a MAGMA_EPI_ROWSTATS
+ * GEMM with n = classes: row maxima and sums come from the GEMM's softmax
+ * partials `stats` (float2 [ceil(classes / 64)][rows]), so each row is read
+ * once (and written once with the gradient). Same outputs, BF16 logits. */
+MAGMA_API magma_status_t magma_cross_entropy_fwd_bwd_rowstats(void* logits, const void* stats,
+                                   const int32_t* targets, float* losses, int64_t rows,
+                                   int64_t classes, int64_t ld, float grad_scale,
+                                   magma_dtype_t dtype, void* stream);
 
 /* Deterministic sum of n F32 values into out[0] (e.g. the mean loss with
  * scale = 1/n). */

@@ -215,6 +215,10 @@ struct TcArgs {
   int splits;
   int kb_per_split;
   float* ws;
+  // Tile raster: 0 walks M fastest (concurrent CTAs share a B tile), 1 walks
+  // N fastest (they share an A block: used when A is far larger than L2 and
+  // would otherwise be re-read once per N tile).
+  int n_fast;
 };
 
 // Epilogue on two consecutive columns (col, col+1) of one row; b0/b1 are the
@@ -306,6 +310,40 @@ __device__ __forceinline__ void direct_store64(TO* dst_row, const float* bias, i
         if (col + i < N) dst_row[col + i] = from_f32<TO>(v[i]);
     }
   }
+}
+
+// Softmax partials of one row over 64 consecutive columns (ra: the first 32,
+// rb: the next 32) of c as stored (rounded to TO): (max, sum of exp(c - max))
+// over the columns below N, into *out.
+template <typename TO>
+__device__ __forceinline__ void row_stats64(const uint32_t (&ra)[32], const uint32_t (&rb)[32],
+                                            int64_t col0, int64_t N, float2* out) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int valid = (int)(N - col0 < 64 ? N - col0 : 64);
+  auto val = [&](int j) {
+    return to_f32(from_f32<TO>(__uint_as_float(j < 32 ? ra[j] : rb[j - 32])));
+  };
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+  if (valid == 64) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) m4[j & 3] = fmaxf(m4[j & 3], val(j));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (j < valid) m4[j & 3] = fmaxf(m4[j & 3], val(j));
+  }
+  const float m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+  const float ml = m * kLog2e;
+  if (valid == 64) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) s4[j & 3] += sm100::ex2_approx(fmaf(val(j), kLog2e, -ml));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (j < valid) s4[j & 3] += sm100::ex2_approx(fmaf(val(j), kLog2e, -ml));
+  }
+  *out = make_float2(m, (s4[0] + s4[1]) + (s4[2] + s4[3]));
 }
 
 // One 32-column chunk of one warp's 32 tile rows: this lane handles the
@@ -445,8 +483,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     };
     for (int unit = ustart; unit < num_units && ok; unit += ustride) {
       const int tile = unit % num_tiles, split = unit / num_tiles;
-      const int a_row0 = (tile % tiles_m) * kTM + (int)rank * kBM;
-      const int b_row0 = (tile / tiles_m) * BN + (int)rank * Cfg::kBRows;
+      const int tm = args.n_fast ? tile / tiles_n : tile % tiles_m;
+      const int tn = args.n_fast ? tile % tiles_n : tile / tiles_m;
+      const int a_row0 = tm * kTM + (int)rank * kBM;
+      const int b_row0 = tn * BN + (int)rank * Cfg::kBRows;
       const int kb0 = split * args.kb_per_split;
       const int kb1 = min(kblocks, kb0 + args.kb_per_split);
       for (int kb = kb0; kb < kb1; ++kb) {
@@ -549,7 +589,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const bool ws_vec8 = (N % 8) == 0;
     const bool c_vec8 = args.vec8_ok != 0;
     const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
-                        args.e.epi == MAGMA_EPI_BIAS;
+                        args.e.epi == MAGMA_EPI_BIAS || args.e.epi == MAGMA_EPI_ROWSTATS;
+    const bool rowstats = args.splits == 1 && args.e.epi == MAGMA_EPI_ROWSTATS;
     const bool has_bias = args.e.bias != nullptr &&
                           (args.e.epi == MAGMA_EPI_BIAS || args.e.epi == MAGMA_EPI_BIAS_GELU ||
                            args.e.epi == MAGMA_EPI_BIAS_RESIDUAL || args.e.epi == MAGMA_EPI_BIAS_RELU);
@@ -557,8 +598,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t acc_phase = 0;
     for (int unit = ustart; unit < num_units; unit += ustride) {
       const int tile = unit % num_tiles, split = unit / num_tiles;
-      const int m0 = (tile % tiles_m) * kTM + (int)rank * kBM;
-      const int n0 = (tile / tiles_m) * BN + half * kCols;
+      const int tm = args.n_fast ? tile / tiles_n : tile % tiles_m;
+      const int tn = args.n_fast ? tile % tiles_n : tile / tiles_m;
+      const int m0 = tm * kTM + (int)rank * kBM;
+      const int n0 = tn * BN + half * kCols;
       if (!sm100::mbar_wait(tfull_bar(acc), acc_phase, args.err)) break;
       sm100::tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) +
@@ -590,6 +633,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               direct_store64<TC>(static_cast<TC*>(args.C) + row * args.e.ldc,
                                  has_bias ? args.e.bias : nullptr, (int64_t)n0 + c0, N, ra, rb,
                                  c_vec8);
+            if (rowstats)
+              row_stats64<TC>(ra, rb, (int64_t)n0 + c0, N,
+                              static_cast<float2*>(args.e.aux_out) + ((n0 + c0) >> 6) * M + row);
           }
         }
       } else {
@@ -959,8 +1005,11 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
   MAGMA_REQUIRE(is_float_dtype(ab_dtype) && is_float_dtype(c_dtype),
                 "magma_gemm: unsupported dtypes ab=%s c=%s", dtype_name(ab_dtype),
                 dtype_name(c_dtype));
-  MAGMA_REQUIRE(epilogue >= MAGMA_EPI_NONE && epilogue <= MAGMA_EPI_DRELU,
+  MAGMA_REQUIRE(epilogue >= MAGMA_EPI_NONE && epilogue <= MAGMA_EPI_ROWSTATS,
                 "magma_gemm: unknown epilogue %d", epilogue);
+  MAGMA_REQUIRE(epilogue != MAGMA_EPI_ROWSTATS || (aux_out != nullptr && ab_dtype == MAGMA_DTYPE_BF16 &&
+                                                   (reinterpret_cast<uintptr_t>(aux_out) & 7u) == 0),
+                "magma_gemm: ROWSTATS needs BF16 operands and an 8-byte aligned aux_out");
   MAGMA_REQUIRE(lda >= (trans_a ? m : k) && ldb >= (trans_b ? k : n) && ldc >= n,
                 "magma_gemm: leading dimensions too small (lda=%lld ldb=%lld ldc=%lld)",
                 (long long)lda, (long long)ldb, (long long)ldc);
@@ -988,15 +1037,23 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
     TcPlan plan = choose_plan(m, n, k, epilogue, c32);
     // Split-K only with a large enough caller workspace; otherwise one pass.
     const size_t need = plan.splits > 1 ? (size_t)plan.splits * m * n * sizeof(float) : 0;
-    if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
+    if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace) ||
+                            epilogue == MAGMA_EPI_ROWSTATS))
       plan = {plan.bn, 1, (int)ceil_div(k, kBK), plan.pair};
     const int vec8_ok = (ldc % 8) == 0 && aligned16(c);
+    // A larger than L2 and several N tiles: walk N fastest so the CTAs that
+    // share an A block run together and it is read from HBM once.
+    const double a_bytes = 2.0 * (double)m * (double)k, b_bytes = 2.0 * (double)n * (double)k;
+    const int n_fast = (a_bytes > 64e6 && a_bytes >= b_bytes && n > (plan.pair ? 256 : 128)) ? 1 : 0;
     TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, vec8_ok, plan.splits,
-                plan.kb_per_split, static_cast<float*>(workspace)};
+                plan.kb_per_split, static_cast<float*>(workspace), n_fast};
     return c32 ? dispatch_plan<float>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
                : dispatch_plan<__nv_bfloat16>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b,
                                               args, s);
   }
+  MAGMA_REQUIRE(epilogue != MAGMA_EPI_ROWSTATS,
+                "magma_gemm: ROWSTATS needs the tensor-core path (16-byte aligned operands, "
+                "lda and ldb multiples of 8)");
   if (ab_dtype == MAGMA_DTYPE_F32)
     return c32 ? launch_simt<float, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e, s)
                : launch_simt<float, __nv_bfloat16>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b,

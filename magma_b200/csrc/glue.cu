@@ -5,6 +5,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace magma {
 namespace {
@@ -224,6 +225,76 @@ ce_block_vec_kernel(T* __restrict__ logits, const int32_t* __restrict__ targets,
   }
 }
 
+// Softmax cross-entropy from the lm-head GEMM's per-row softmax partials
+// (MAGMA_EPI_ROWSTATS: float2 (max, sum exp) per 64-column chunk, chunk-major
+// [nchunks][rows]): merge the partials, then one pass over the row writes the
+// gradient in place (one read, one write, one exp per element).
+template <typename T>
+__global__ void __launch_bounds__(512)
+ce_rowstats_kernel(T* __restrict__ logits, const float2* __restrict__ stats,
+                   const int32_t* __restrict__ targets, float* __restrict__ losses, int64_t rows,
+                   int classes, int64_t ld, float grad_scale, int* err) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  __shared__ float red_m[16], red_s[16];
+  __shared__ float bm, bs, bxt;
+  const int tid = threadIdx.x;
+  const int nw = blockDim.x >> 5;
+  const int nvec = (int)(ld >> 3);
+  const int nchunks = (classes + 63) >> 6;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    T* row = logits + r * ld;
+    float m = -INFINITY, s = 0.f;
+    for (int c = tid; c < nchunks; c += blockDim.x) {
+      const float2 p = stats[(int64_t)c * rows + r];
+      online_merge(m, s, p.x, p.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      online_merge(m, s, m2, s2);
+    }
+    if ((tid & 31) == 0) {
+      red_m[tid >> 5] = m;
+      red_s[tid >> 5] = s;
+    }
+    const int32_t t = targets[r];
+    const bool bad = t < 0 || t >= classes;
+    if (tid == 0) bxt = bad ? 0.f : to_f32(row[t]);
+    __syncthreads();
+    if (tid < 32) {
+      float mm = tid < nw ? red_m[tid] : -INFINITY;
+      float ss = tid < nw ? red_s[tid] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, mm, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, ss, o);
+        online_merge(mm, ss, m2, s2);
+      }
+      if (tid == 0) {
+        bm = mm;
+        bs = ss;
+        if (bad) set_device_error(err, kDevErrBadIndex);
+        losses[r] = -(((bad ? mm : bxt) - mm) - logf(ss));
+      }
+    }
+    __syncthreads();  // row[t] read and the row terms published before the row is overwritten
+    const float ml = bm * kLog2e, inv = grad_scale / bs;
+    for (int vi = tid; vi < nvec; vi += blockDim.x) {
+      float v[8];
+      load8(row + vi * 8, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = vi * 8 + i;
+        const float p = sm100::ex2_approx(fmaf(v[i], kLog2e, -ml)) * inv;
+        v[i] = c < classes ? p - (c == t ? grad_scale : 0.f) : 0.f;
+      }
+      store8(row + vi * 8, v);
+    }
+    __syncthreads();
+  }
+}
+
 // Small class counts: one warp per row.
 template <typename T>
 __global__ void ce_warp_kernel(T* __restrict__ logits, const int32_t* __restrict__ targets,
@@ -323,6 +394,41 @@ __global__ void bias_grad_partial(const T* __restrict__ dy, float* __restrict__ 
   float s = 0.f;
   for (int64_t r = r0; r < r1; ++r) s += to_f32(dy[r * ld + c]);
   part[(int64_t)blockIdx.y * cols + c] = s;
+}
+
+// Vectorised partial column sums (cols % 8 == 0, 16-byte aligned rows): a
+// 256-thread CTA covers 256 columns (32 groups of 8) x rows_per_block rows;
+// thread (group g, phase y) sums rows r0 + y, r0 + y + 8, ... of its 8 columns
+// with 16-byte loads, then the 8 phases are added in order (deterministic).
+template <typename T>
+__global__ void __launch_bounds__(256)
+bias_grad_partial_vec(const T* __restrict__ dy, float* __restrict__ part, int64_t rows, int cols,
+                      int64_t ld, int64_t rows_per_block) {
+  __shared__ float red[8][256 + 4];
+  const int g = threadIdx.x & 31, y = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 256 + g * 8;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+  const int64_t r1 = min(rows, r0 + rows_per_block);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < cols) {
+#pragma unroll 4
+    for (int64_t r = r0 + y; r < r1; r += 8) {
+      float v[8];
+      load8(dy + r * ld + c0, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += v[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[y][g * 8 + i] = acc[i];
+  __syncthreads();
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < cols) {
+    float t = red[0][threadIdx.x];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) t += red[k][threadIdx.x];
+    part[(int64_t)blockIdx.y * cols + c] = t;
+  }
 }
 
 // Sums the partial rows in a fixed order (32 columns x 8 partial phases per
@@ -451,6 +557,30 @@ magma_status_t magma_cross_entropy_fwd_bwd(void* logits, const int32_t* targets,
   return check_launch("cross_entropy_fwd_bwd");
 }
 
+magma_status_t magma_cross_entropy_fwd_bwd_rowstats(void* logits, const void* stats,
+                                                    const int32_t* targets, float* losses,
+                                                    int64_t rows, int64_t classes, int64_t ld,
+                                                    float grad_scale, magma_dtype_t dtype,
+                                                    void* stream) {
+  MAGMA_REQUIRE(rows >= 0 && classes > 0 && ld >= classes && classes < (1LL << 31),
+                "magma_cross_entropy_fwd_bwd_rowstats: bad shape rows=%lld classes=%lld ld=%lld",
+                (long long)rows, (long long)classes, (long long)ld);
+  MAGMA_REQUIRE(dtype == MAGMA_DTYPE_BF16, "magma_cross_entropy_fwd_bwd_rowstats: BF16 logits only");
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(logits && stats && targets && losses,
+                "magma_cross_entropy_fwd_bwd_rowstats: NULL pointer");
+  MAGMA_REQUIRE(ld % 8 == 0 && aligned16(logits) && (reinterpret_cast<uintptr_t>(stats) & 7u) == 0,
+                "magma_cross_entropy_fwd_bwd_rowstats: ld must be a multiple of 8, logits 16-byte "
+                "and stats 8-byte aligned");
+  int64_t g = rows;
+  const int64_t cap = 4LL * num_sms();
+  if (g > cap) g = cap;
+  ce_rowstats_kernel<__nv_bfloat16><<<(int)g, 512, 0, (cudaStream_t)stream>>>(
+      (__nv_bfloat16*)logits, static_cast<const float2*>(stats), targets, losses, rows,
+      (int)classes, ld, grad_scale, device_error_word());
+  return check_launch("cross_entropy_fwd_bwd_rowstats");
+}
+
 magma_status_t magma_reduce_sum(const float* x, float* out, int64_t n, float scale, void* stream) {
   MAGMA_REQUIRE(n >= 0, "magma_reduce_sum: negative size");
   MAGMA_REQUIRE(out != nullptr && (n == 0 || x != nullptr), "magma_reduce_sum: NULL pointer");
@@ -512,7 +642,20 @@ magma_status_t magma_bias_grad(const void* dy, float* dbias, int64_t rows, int64
   int64_t rpb = ceil_div(rows, nb);
   dim3 grid((unsigned)ceil_div(cols, 256), (unsigned)nb);
   float* part = (float*)workspace;
-  if (dtype == MAGMA_DTYPE_F32)
+  const size_t esz = dtype == MAGMA_DTYPE_F32 ? 4 : 2;
+  if (cols % 8 == 0 && ld % 8 == 0 && aligned16(dy) && (ld * esz) % 16 == 0) {
+    // 256-row blocks: enough CTAs to fill the GPU, few partial rows
+    nb = (int)ceil_div(rows, 256);
+    if (nb > kBiasMaxRowBlocks) nb = kBiasMaxRowBlocks;
+    rpb = ceil_div(rows, nb);
+    grid = dim3((unsigned)ceil_div(cols, 256), (unsigned)nb);
+    if (dtype == MAGMA_DTYPE_F32)
+      bias_grad_partial_vec<float><<<grid, 256, 0, s>>>((const float*)dy, part, rows, (int)cols,
+                                                        ld, rpb);
+    else
+      bias_grad_partial_vec<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part,
+                                                                rows, (int)cols, ld, rpb);
+  } else if (dtype == MAGMA_DTYPE_F32)
     bias_grad_partial<float><<<grid, 256, 0, s>>>((const float*)dy, part, rows, (int)cols, ld, rpb);
   else
     bias_grad_partial<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dy, part, rows,

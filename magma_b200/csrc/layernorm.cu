@@ -3,8 +3,10 @@
 // Forward restates nn.LayerNorm.forward (Sources/Core/Module.swift:2754-2791)
 // and the GPT block's layerNorm (Benchmarks/GPT2Shakespeare/Sources/main.swift:
 // 364-375): mean = sum/D, var = sum((x-mean)^2)/D (population), std =
-// sqrt(var+eps), y = ((x-mean)/std)*gamma + beta, with an IEEE divide by std
-// as the reference does (it never multiplies by rsqrt).
+// sqrt(var+eps), y = ((x-mean)/std)*gamma + beta. The reference divides by std
+// (it never multiplies by rsqrt); here the per-element quotient is a multiply
+// by RN(1/std) with one Markstein residual correction, which reproduces the
+// correctly rounded divide except in rare one-ulp cases.
 //
 // Backward is the closed form of the reference's autodiff chain through that
 // forward (vjpDivide/vjpSqrt/vjpMeanDims/vjpMultiply with sumAlongBroadcastDims,
@@ -52,7 +54,9 @@ constexpr int kBwdRing = 2;                 // row buffers per warp, backward
 constexpr int fwd_max_warps(int groups) { return groups > 6 ? 12 : 16; }
 // Backward warps per CTA: 12 keep 170 registers per thread; the widest rows
 // (G = 8) need more and run 8 warps.
-constexpr int bwd_max_warps(int groups) { return groups > 6 ? 8 : 12; }
+constexpr int bwd_max_warps(int groups, bool res = false) {
+  return (groups > 6 || res) ? 8 : 12;
+}
 
 bool stream_ok(int dim) { return dim % 8 == 0 && dim <= kMaxGroups * 128; }
 
@@ -149,6 +153,11 @@ ln_fwd_stream(const TX* __restrict__ x, const float* __restrict__ gamma,
         }
     ss = warp_sum(ss);
     const float stdv = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
+    // (x - mean) / std per element as q = d * (1/std) with one residual
+    // correction (Markstein's method: r = RN(1/std), e = d - q*std exact by
+    // FMA, q' = q + e*r), which gives the correctly rounded quotient of the
+    // reference's divide in all but rare one-ulp cases, on the FMA pipe.
+    const float rinv = __frcp_rn(stdv);
     TY* yr = y + row * dim;
 #pragma unroll
     for (int c = 0; c < G; ++c) {
@@ -156,8 +165,11 @@ ln_fwd_stream(const TX* __restrict__ x, const float* __restrict__ gamma,
       if (e < dim) {
         float o[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[i] = __fadd_rn(__fmul_rn(__fdiv_rn(v[c][i], stdv), g[c][i]), bt[c][i]);
+        for (int i = 0; i < 4; ++i) {
+          const float q = __fmul_rn(v[c][i], rinv);
+          const float q2 = __fmaf_rn(__fmaf_rn(-q, stdv, v[c][i]), rinv, q);
+          o[i] = __fadd_rn(__fmul_rn(q2, g[c][i]), bt[c][i]);
+        }
         store4(yr + e, o);
       }
     }
@@ -206,12 +218,16 @@ ln_fwd_generic(const TX* __restrict__ x, const float* __restrict__ gamma,
 // only when accumulating into it). dgamma/dbeta partials live in registers
 // (lane l owns columns 4l + 128c) and are summed over the warps of the CTA in
 // warp order into part[blockIdx.x] = [dgamma | dbeta].
-template <int G, typename TDY, typename TX, typename TDX>
-__global__ void __launch_bounds__(bwd_max_warps(G) * 32, 1)
+// RES (residual stream, F32 dx): also writes a BF16 copy of the final dx
+// (dx_bf16, optional) and accumulates its column sums as a third partial row
+// [dgamma | dbeta | dcol].
+template <int G, bool RES, typename TDY, typename TX, typename TDX>
+__global__ void __launch_bounds__(bwd_max_warps(G, RES) * 32, 1)
 ln_bwd_stream(const TDY* __restrict__ dy, const TX* __restrict__ x,
               const float* __restrict__ gamma, const float* __restrict__ mean_in,
               const float* __restrict__ rstd_in, TDX* __restrict__ dx,
-              float* __restrict__ part, int64_t rows, int dim, int accumulate_dx, int* err) {
+              __nv_bfloat16* __restrict__ dx_bf16, float* __restrict__ part, int64_t rows,
+              int dim, int accumulate_dx, int* err) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -239,13 +255,16 @@ ln_bwd_stream(const TDY* __restrict__ dy, const TX* __restrict__ x,
     for (int64_t j = 0; j < n && j < kBwdRing; ++j) issue((int)j, first + j * stride);
   }
   __syncwarp();
-  float g[G][4], dg[G][4], db[G][4];
+  float g[G][4], dg[G][4], db[G][4], dc[RES ? G : 1][4];
 #pragma unroll
   for (int c = 0; c < G; ++c) {
     const int e = 128 * c + 4 * lane;
     if (e < dim) load4(gamma + e, g[c]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) dg[c][i] = db[c][i] = 0.f;
+    if (RES)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dc[RES ? c : 0][i] = 0.f;
   }
   bool ok = true;
   for (int64_t j = 0; j < n; ++j) {
@@ -300,6 +319,11 @@ ln_bwd_stream(const TDY* __restrict__ dy, const TX* __restrict__ x,
           for (int i = 0; i < 4; ++i) o[i] += prev[i];
         }
         store4(dst + e, o);
+        if (RES) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dc[RES ? c : 0][i] += o[i];
+          if (dx_bf16 != nullptr) store4(dx_bf16 + row * dim + e, o);
+        }
       }
     }
     __syncwarp();
@@ -313,14 +337,16 @@ ln_bwd_stream(const TDY* __restrict__ dy, const TX* __restrict__ x,
     if (e < dim) {
       store4(red + e, dg[c]);
       store4(red + dim + e, db[c]);
+      if (RES) store4(red + 2 * dim + e, dc[RES ? c : 0]);
     }
   }
   __syncthreads();
   if (!ok) return;
-  float* out = part + (int64_t)blockIdx.x * 2 * dim;
+  const int width = (RES ? 3 : 2) * dim;
+  float* out = part + (int64_t)blockIdx.x * width;
   const size_t wstride = (size_t)kBwdRing * stage / sizeof(float);
   const float* base = reinterpret_cast<const float*>(smem + kBarBytes);
-  for (int i = threadIdx.x; i < 2 * dim; i += blockDim.x) {
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
     float t = base[i];
     for (int w = 1; w < nwarps; ++w) t += base[(size_t)w * wstride + i];
     out[i] = t;
@@ -373,12 +399,13 @@ ln_bwd_generic(const TDY* __restrict__ dy, const TX* __restrict__ x,
   }
 }
 
-// Sums per-CTA partial rows: out[c] (+)= sum_b part[b][c]. A 32 x 8 CTA
-// covers 32 columns; row y of threads sums partials b = y, y+8, ... in order,
-// then the 8 sums are added in y order (fixed order: deterministic).
+// Sums per-CTA partial rows: out_k[c] (+)= sum_b part[b][k*dim + c] for the
+// outputs k = 0, 1, 2 (dgamma, dbeta, dcol; a null output is skipped). A 32 x 8
+// CTA covers 32 columns; row y of threads sums partials b = y, y+8, ... in
+// order, then the 8 sums are added in y order (fixed order: deterministic).
 __global__ void __launch_bounds__(256)
-reduce_partials(const float* __restrict__ part, int nblocks, int width,
-                float* __restrict__ dgamma, float* __restrict__ dbeta, int dim, int accumulate) {
+reduce_partials(const float* __restrict__ part, int nblocks, int width, float* __restrict__ out0,
+                float* __restrict__ out1, float* __restrict__ out2, int dim, int accumulate) {
   __shared__ float red[8][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
@@ -393,8 +420,10 @@ reduce_partials(const float* __restrict__ part, int nblocks, int width,
     float t = red[0][tx];
 #pragma unroll
     for (int y = 1; y < 8; ++y) t += red[y][tx];
-    float* dst = c < dim ? dgamma + c : dbeta + (c - dim);
-    if (dst == nullptr) return;
+    const int k = c / dim;
+    float* out = k == 0 ? out0 : (k == 1 ? out1 : out2);
+    if (out == nullptr) return;
+    float* dst = out + (c - k * dim);
     *dst = accumulate ? *dst + t : t;
   }
 }
@@ -427,18 +456,21 @@ void set_dynamic_smem(K kern, size_t bytes) {
 // Backward through ln_bwd_stream when the shape and alignment allow it
 // (*launched false otherwise). *blocks: CTAs launched = partial rows written;
 // at most `max_blocks`.
-template <typename TDY, typename TX, typename TDX>
+template <typename TDY, typename TX, typename TDX, bool RES = false>
 magma_status_t launch_bwd_stream(const void* dy, const void* x, const float* gamma,
                                  const float* mean, const float* rstd, void* dx, int64_t rows,
                                  int dim, int acc_dx, float* part, int max_blocks, int* blocks,
-                                 bool* launched, cudaStream_t stream) {
+                                 bool* launched, cudaStream_t stream, void* dx_bf16 = nullptr) {
   *launched = false;
-  if (!stream_ok(dim) || !aligned16(x) || !aligned16(dy) || !aligned16(dx) || !aligned16(gamma))
+  if (!stream_ok(dim) || !aligned16(x) || !aligned16(dy) || !aligned16(dx) || !aligned16(gamma) ||
+      !aligned16(dx_bf16))
     return MAGMA_OK;
   const size_t stage =
       (size_t)dim * (sizeof(TX) + sizeof(TDY) + (acc_dx ? sizeof(TDX) : 0));
+  // the partial rows are staged in each warp's ring at the end
+  if (kBwdRing * stage < (size_t)(RES ? 3 : 2) * dim * sizeof(float)) return MAGMA_OK;
   const int groups = ((dim + 255) / 256) * 2;
-  const int warps = stream_warps(kBwdRing, stage, bwd_max_warps(groups));
+  const int warps = stream_warps(kBwdRing, stage, bwd_max_warps(groups, RES));
   if (warps == 0) return MAGMA_OK;
   int b = stream_blocks(rows, warps);
   if (b > max_blocks) b = max_blocks;
@@ -446,11 +478,11 @@ magma_status_t launch_bwd_stream(const void* dy, const void* x, const float* gam
   const size_t smem = kBarBytes + (size_t)warps * kBwdRing * stage;
 #define LN_BWD_STREAM(G)                                                                        \
   do {                                                                                          \
-    auto kern = ln_bwd_stream<G, TDY, TX, TDX>;                                                 \
+    auto kern = ln_bwd_stream<G, RES, TDY, TX, TDX>;                                            \
     set_dynamic_smem(kern, smem);                                                               \
     kern<<<b, warps * 32, smem, stream>>>((const TDY*)dy, (const TX*)x, gamma, mean, rstd,      \
-                                          (TDX*)dx, part, rows, dim, acc_dx,                    \
-                                          device_error_word());                                 \
+                                          (TDX*)dx, (__nv_bfloat16*)dx_bf16, part, rows, dim,   \
+                                          acc_dx, device_error_word());                         \
   } while (0)
   if (groups == 2) LN_BWD_STREAM(2);
   else if (groups == 4) LN_BWD_STREAM(4);
@@ -515,7 +547,7 @@ magma_status_t launch_bwd(const void* dy, const void* x, const float* gamma, con
   if (dgamma != nullptr || dbeta != nullptr) {
     int width = 2 * dim;
     reduce_partials<<<(width + 31) / 32, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
-                                                           dim, acc_params);
+                                                           nullptr, dim, acc_params);
     if (magma_status_t s = check_launch("layernorm_bwd_reduce")) return s;
   }
   return MAGMA_OK;
@@ -575,7 +607,7 @@ magma_status_t launch_bwd_noalloc(const void* dy, const void* x, const float* ga
   if (dgamma != nullptr || dbeta != nullptr) {
     const int width = 2 * dim;
     reduce_partials<<<(width + 31) / 32, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
-                                                           dim, acc_params);
+                                                           nullptr, dim, acc_params);
     if (magma_status_t s = check_launch("layernorm_bwd_noalloc_reduce")) return s;
   }
   return MAGMA_OK;
@@ -693,6 +725,58 @@ magma_status_t magma_layernorm_bwd_noalloc(const void* dy, const void* x, const 
   if (!f_dy && f_x && !f_dx) LN_BWD_NA(__nv_bfloat16, float, __nv_bfloat16);
   LN_BWD_NA(float, __nv_bfloat16, __nv_bfloat16);
 #undef LN_BWD_NA
+}
+
+size_t magma_layernorm_bwd_residual_workspace_size(int64_t rows, int64_t dim) {
+  if (rows <= 0 || dim <= 0) return 0;
+  int64_t b = ceil_div(rows, kWarps);
+  if (b > kMaxBwdBlocks) b = kMaxBwdBlocks;
+  return (size_t)b * 3 * (size_t)dim * sizeof(float);
+}
+
+magma_status_t magma_layernorm_bwd_residual(const void* dy, const float* x, const float* gamma,
+                                            const float* mean, const float* rstd, float* dx,
+                                            void* dx_bf16, float* dgamma, float* dbeta,
+                                            float* dcol, int64_t rows, int64_t dim,
+                                            magma_dtype_t dy_dtype, int32_t accumulate_dx,
+                                            int32_t accumulate_params, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  MAGMA_REQUIRE(rows >= 0 && dim > 0 && dim % 8 == 0 && dim <= kMaxGroups * 128,
+                "magma_layernorm_bwd_residual: dim %lld must be a multiple of 8 and <= %d",
+                (long long)dim, kMaxGroups * 128);
+  MAGMA_REQUIRE(is_float_dtype(dy_dtype), "magma_layernorm_bwd_residual: unsupported dy dtype");
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(dy && x && gamma && mean && rstd && dx,
+                "magma_layernorm_bwd_residual: NULL pointer");
+  MAGMA_REQUIRE(aligned16(dy) && aligned16(x) && aligned16(gamma) && aligned16(dx) &&
+                    aligned16(dx_bf16),
+                "magma_layernorm_bwd_residual: dy, x, gamma, dx, dx_bf16 must be 16-byte aligned");
+  const size_t need = magma_layernorm_bwd_residual_workspace_size(rows, dim);
+  MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+                "magma_layernorm_bwd_residual: workspace of %zu bytes needed, %zu given", need,
+                workspace_bytes);
+  cudaStream_t s = (cudaStream_t)stream;
+  float* part = (float*)workspace;
+  const int d = (int)dim;
+  int blocks = bwd_blocks(rows);
+  bool launched = false;
+  magma_status_t st =
+      dy_dtype == MAGMA_DTYPE_F32
+          ? launch_bwd_stream<float, float, float, true>(dy, x, gamma, mean, rstd, dx, rows, d,
+                                                         accumulate_dx, part, kMaxBwdBlocks,
+                                                         &blocks, &launched, s, dx_bf16)
+          : launch_bwd_stream<__nv_bfloat16, float, float, true>(
+                dy, x, gamma, mean, rstd, dx, rows, d, accumulate_dx, part, kMaxBwdBlocks,
+                &blocks, &launched, s, dx_bf16);
+  if (st) return st;
+  MAGMA_REQUIRE(launched, "magma_layernorm_bwd_residual: shape not supported by the row kernels");
+  if (dgamma != nullptr || dbeta != nullptr || dcol != nullptr) {
+    const int width = 3 * d;
+    reduce_partials<<<(width + 31) / 32, 256, 0, s>>>(part, blocks, width, dgamma, dbeta, dcol, d,
+                                                      accumulate_params);
+    if (magma_status_t s2 = check_launch("layernorm_bwd_residual_reduce")) return s2;
+  }
+  return MAGMA_OK;
 }
 
 }  // extern "C"

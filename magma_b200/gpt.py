@@ -202,6 +202,9 @@ class GPTTrainer:
         self.lnf = torch.empty((T, D), **a)
         self.lnf_stats = torch.empty((2, T), **f)
         self.logits = torch.empty((T, Vp), **a)
+        # per-row softmax partials of the fused lm-head + CE (BF16 mode)
+        self.ce_stats = (torch.empty(((cfg.vocab + 63) // 64) * T * 2, **f)
+                         if self.act_dtype != torch.float32 else None)
         self.losses = torch.empty(T, **f)
         self.loss = torch.empty(1, **f)
         self.dresid = torch.empty((T, D), **f)
@@ -217,6 +220,7 @@ class GPTTrainer:
         ws = max(max(lib.query("magma_gemm_workspace_size", m, n, k, self.DT)
                      for m, n, k in gemm_shapes),
                  lib.query("magma_layernorm_bwd_workspace_size", T, D),
+                 lib.query("magma_layernorm_bwd_residual_workspace_size", T, D),
                  lib.query("magma_attention_bwd_workspace_size", B, H, cfg.seq, cfg.head_dim, self.DT),
                  lib.query("magma_bias_grad_workspace_size", T, 4 * D),
                  lib.query("magma_bias_grad_workspace_size", T, 3 * D))
@@ -238,10 +242,14 @@ class GPTTrainer:
         lib.call("magma_layernorm_fwd", _p(x), _p(w), _p(b), _p(y), _p(mean), _p(rstd), self.T,
                  self.cfg.dim, 1e-5, lib.F32, self.DT, self._s())
 
-    def _ln_bwd(self, dy, x, w, mean, rstd, dw, db):
-        lib.call("magma_layernorm_bwd", _p(dy), _p(x), _p(w), _p(mean), _p(rstd),
-                 _p(self.dresid), _p(dw), _p(db), self.T, self.cfg.dim, self.DT, lib.F32, lib.F32,
-                 1, 0, _p(self.ws), self.ws.numel(), self._s())
+    def _ln_bwd(self, dy, x, w, mean, rstd, dw, db, dcol, accumulate=1, bf16_copy=True):
+        """LayerNorm VJP into the residual gradient self.dresid (added, or written
+        for the final LN), with its BF16 copy for the next GEMMs and its column
+        sums as the bias gradient `dcol` of the Linear feeding the residual."""
+        copy = self.dresid_a if bf16_copy else None
+        lib.call("magma_layernorm_bwd_residual", _p(dy), _p(x), _p(w), _p(mean), _p(rstd),
+                 _p(self.dresid), _p(copy), _p(dw), _p(db), _p(dcol), self.T, self.cfg.dim,
+                 self.DT, accumulate, 0, _p(self.ws), self.ws.numel(), self._s())
 
     def _bias_grad(self, dy, db, cols):
         lib.call("magma_bias_grad", _p(dy), _p(db), self.T, cols, cols,
@@ -284,10 +292,18 @@ class GPTTrainer:
         self._ln_fwd(self.x[L], self.view(P, "lnf_w"), self.view(P, "lnf_b"), self.lnf,
                      self.lnf_stats[0], self.lnf_stats[1])
         head = "wte" if cfg.tied else "lm_head"
-        self._gemm(self.lnf, W(head), self.logits, T, Vp, D, D, D, Vp, 0, 1, E.EPI_NONE)
         # loss and dlogits in place (main.swift:412-433), mean over rows
-        lib.call("magma_cross_entropy_fwd_bwd", _p(self.logits), _p(self.targets), _p(self.losses),
-                 T, V, Vp, 1.0 / T, self.DT, s)
+        if self.ce_stats is not None:
+            # lm-head GEMM over the real vocabulary with per-row softmax
+            # partials in its epilogue; CE then reads the logits once
+            self._gemm(self.lnf, W(head), self.logits, T, V, D, D, D, Vp, 0, 1, E.EPI_ROWSTATS,
+                       aux_out=self.ce_stats)
+            lib.call("magma_cross_entropy_fwd_bwd_rowstats", _p(self.logits), _p(self.ce_stats),
+                     _p(self.targets), _p(self.losses), T, V, Vp, 1.0 / T, self.DT, s)
+        else:
+            self._gemm(self.lnf, W(head), self.logits, T, Vp, D, D, D, Vp, 0, 1, E.EPI_NONE)
+            lib.call("magma_cross_entropy_fwd_bwd", _p(self.logits), _p(self.targets),
+                     _p(self.losses), T, V, Vp, 1.0 / T, self.DT, s)
         lib.call("magma_reduce_sum", _p(self.losses), _p(self.loss), T, 1.0 / T, s)
 
         # ---------------------------------------------------------- backward
@@ -295,11 +311,11 @@ class GPTTrainer:
         self._gemm(self.logits, W(head), self.d_ln, T, D, Vp, Vp, D, D, 0, 0, E.EPI_NONE)
         self._gemm(self.logits, self.lnf, self.view(G, head), Vp, D, T, Vp, D, D, 1, 0, E.EPI_NONE,
                    c_dtype=lib.F32)
-        # final LN: dresid = LN_bwd (written, not accumulated)
-        lib.call("magma_layernorm_bwd", _p(self.d_ln), _p(self.x[L]), _p(self.view(P, "lnf_w")),
-                 _p(self.lnf_stats[0]), _p(self.lnf_stats[1]), _p(self.dresid),
-                 _p(self.view(G, "lnf_w")), _p(self.view(G, "lnf_b")), T, D, self.DT, lib.F32,
-                 lib.F32, 0, 0, _p(self.ws), self.ws.numel(), s)
+        # final LN: dresid = LN_bwd (written, not accumulated); its column sums
+        # are the last block's fcproj bias gradient
+        self._ln_bwd(self.d_ln, self.x[L], self.view(P, "lnf_w"), self.lnf_stats[0],
+                     self.lnf_stats[1], self.view(G, "lnf_w"), self.view(G, "lnf_b"),
+                     self.view(G, f"h{L - 1}.fcproj_b"), accumulate=0)
         for l in reversed(range(L)):
             n = lambda k: f"h{l}.{k}"  # noqa: E731
             st = self.stats[l]
@@ -309,20 +325,19 @@ class GPTTrainer:
                        E.EPI_DGELU, aux_in=self.fc_pre[l])
             self._gemm(dres, self.fc_act[l], self.view(G, n("fcproj_w")), D, 4 * D, T, D, 4 * D,
                        4 * D, 1, 0, E.EPI_NONE, c_dtype=lib.F32)
-            self._bias_grad(self.dresid, self.view(G, n("fcproj_b")), D)
             self._gemm(self.d_fc, W(n("fc_w")), self.d_ln, T, D, 4 * D, 4 * D, D, D, 0, 0,
                        E.EPI_NONE)
             self._gemm(self.d_fc, self.ln2[l], self.view(G, n("fc_w")), 4 * D, D, T, 4 * D, D, D,
                        1, 0, E.EPI_NONE, c_dtype=lib.F32)
             self._bias_grad(self.d_fc, self.view(G, n("fc_b")), 4 * D)
             self._ln_bwd(self.d_ln, self.h[l], self.view(P, n("ln2_w")), st[2], st[3],
-                         self.view(G, n("ln2_w")), self.view(G, n("ln2_b")))
+                         self.view(G, n("ln2_w")), self.view(G, n("ln2_b")),
+                         self.view(G, n("proj_b")))
             dres = self._dresid_operand()
             # attention: h = x + proj(attn(qkv(ln1(x))))
             self._gemm(dres, W(n("proj_w")), self.d_att, T, D, D, D, D, D, 0, 0, E.EPI_NONE)
             self._gemm(dres, self.att[l], self.view(G, n("proj_w")), D, D, T, D, D, D, 1, 0,
                        E.EPI_NONE, c_dtype=lib.F32)
-            self._bias_grad(self.dresid, self.view(G, n("proj_b")), D)
             q = self.qkv[l]
             es = q.element_size()
             dq = self.dqkv
@@ -337,7 +352,9 @@ class GPTTrainer:
                        1, 0, E.EPI_NONE, c_dtype=lib.F32)
             self._bias_grad(self.dqkv, self.view(G, n("qkv_b")), 3 * D)
             self._ln_bwd(self.d_ln, self.x[l], self.view(P, n("ln1_w")), st[0], st[1],
-                         self.view(G, n("ln1_w")), self.view(G, n("ln1_b")))
+                         self.view(G, n("ln1_w")), self.view(G, n("ln1_b")),
+                         self.view(G, f"h{l - 1}.fcproj_b") if l > 0 else None,
+                         bf16_copy=l > 0)
         # embeddings: dwte += scatter(dresid); dwpe = sum over batch
         self.view(G, "wpe").zero_()
         if not cfg.tied:
@@ -346,12 +363,9 @@ class GPTTrainer:
                  _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp, s)
 
     def _dresid_operand(self) -> torch.Tensor:
-        """The residual gradient as a GEMM operand (BF16 copy in bf16 mode)."""
-        if self.dresid_a is None:
-            return self.dresid
-        lib.call("magma_convert", _p(self.dresid), _p(self.dresid_a), self.dresid.numel(),
-                 lib.F32, lib.BF16, self._s())
-        return self.dresid_a
+        """The residual gradient as a GEMM operand: the BF16 copy the last
+        LayerNorm VJP wrote (bf16 mode), or the F32 gradient itself."""
+        return self.dresid if self.dresid_a is None else self.dresid_a
 
     # ---------------------------------------------------------------- Adam
     def optimizer_step(self, grad_scale: float = 1.0) -> None:

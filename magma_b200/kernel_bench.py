@@ -26,6 +26,7 @@ GEMMS = {
     "fc_fwd": (T, 4 * D, D, 0, 1, lib.EPI_BIAS_GELU, torch.bfloat16),
     "fcproj_fwd": (T, D, 4 * D, 0, 1, lib.EPI_BIAS_RESIDUAL, torch.float32),
     "lm_fwd": (T, V, D, 0, 1, lib.EPI_NONE, torch.bfloat16),
+    "lm_fwd_stats": (T, 50257, D, 0, 1, lib.EPI_ROWSTATS, torch.bfloat16),
     "lm_dx": (T, D, V, 0, 0, lib.EPI_NONE, torch.bfloat16),
     "lm_dw": (V, D, T, 1, 0, lib.EPI_NONE, torch.float32),
     "fcproj_dx": (T, 4 * D, D, 0, 0, lib.EPI_DGELU, torch.bfloat16),
@@ -71,6 +72,8 @@ def bench_gemm(only: str | None, reps: int) -> list[dict]:
         b = torch.randn((n, k) if tb else (k, n), device="cuda").to(torch.bfloat16)
         c = torch.empty((m, n), device="cuda", dtype=od)
         kw = {}
+        if epi == lib.EPI_ROWSTATS:
+            kw["aux_out"] = torch.empty(((n + 63) // 64) * m * 2, device="cuda")
         if epi in (lib.EPI_BIAS, lib.EPI_BIAS_GELU, lib.EPI_BIAS_RESIDUAL):
             kw["bias"] = torch.randn(n, device="cuda")
         if epi == lib.EPI_BIAS_GELU:
@@ -141,8 +144,22 @@ def bench_ce(reps: int) -> list[dict]:
     tg = torch.randint(0, 50257, (T,), device="cuda", dtype=torch.int32)
     losses = torch.empty(T, device="cuda")
     ms = _time(lambda: ops.cross_entropy_fwd_bwd(logits, tg, 50257, losses=losses), reps)
-    return [{"kernel": "cross_entropy", "us": round(ms * 1e3, 2),
-             "GBs": round(T * V * 4 / ms / 1e6, 1)}]
+    out = [{"kernel": "cross_entropy", "us": round(ms * 1e3, 2),
+            "GBs": round(T * V * 4 / ms / 1e6, 1)}]
+    # the one-pass CE fed by the lm-head GEMM's softmax partials
+    nch = (50257 + 63) // 64
+    stats = torch.empty(nch * T * 2, device="cuda")
+    x = torch.randn((T, D), device="cuda").to(torch.bfloat16)
+    w = (0.02 * torch.randn((V, D), device="cuda")).to(torch.bfloat16)
+    ops.gemm(x, w[:50257], trans_b=True, out=logits[:, :50257], epilogue=lib.EPI_ROWSTATS,
+             aux_out=stats)
+    st = torch.cuda.current_stream().cuda_stream
+    ms = _time(lambda: lib.call("magma_cross_entropy_fwd_bwd_rowstats", logits.data_ptr(),
+                                stats.data_ptr(), tg.data_ptr(), losses.data_ptr(), T, 50257, V,
+                                1.0 / T, lib.BF16, st), reps)
+    out.append({"kernel": "cross_entropy_rowstats", "us": round(ms * 1e3, 2),
+                "GBs": round((T * V * 4 + nch * T * 8) / ms / 1e6, 1)})
+    return out
 
 
 def main(argv=None) -> None:

@@ -49,6 +49,7 @@ EPI_DGELU = 4
 EPI_ACCUMULATE = 5
 EPI_BIAS_RELU = 6
 EPI_DRELU = 7
+EPI_ROWSTATS = 8
 
 
 class MagmaError(RuntimeError):
@@ -89,6 +90,9 @@ SIGNATURES = {
                                    _i32, _i32, _i32, _vp, _sz, _vp]),
     "magma_layernorm_bwd_noalloc": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                                            _i32, _i32, _i32, _i32, _i32, _vp]),
+    "magma_layernorm_bwd_residual_workspace_size": (_sz, [_i64, _i64]),
+    "magma_layernorm_bwd_residual": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                            _i64, _i64, _i32, _i32, _i32, _vp, _sz, _vp]),
     "magma_gemm_workspace_size": (_sz, [_i64, _i64, _i64, _i32]),
     "magma_gemm": (None, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
                           _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
@@ -105,6 +109,8 @@ SIGNATURES = {
     "magma_embedding_fwd": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "magma_embedding_bwd": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "magma_cross_entropy_fwd_bwd": (None, [_vp, _vp, _vp, _i64, _i64, _i64, _f, _i32, _vp]),
+    "magma_cross_entropy_fwd_bwd_rowstats": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f,
+                                                    _i32, _vp]),
     "magma_reduce_sum": (None, [_vp, _vp, _i64, _f, _vp]),
     "magma_gelu_fwd": (None, [_vp, _vp, _i64, _i32, _vp]),
     "magma_gelu_bwd": (None, [_vp, _vp, _vp, _i64, _i32, _vp]),
@@ -119,10 +125,12 @@ SIGNATURES = {
 # Kernel launches one successful call of each op makes (for launch accounting).
 KERNELS_PER_CALL = {
     "magma_layernorm_fwd": 1, "magma_layernorm_bwd": 2, "magma_layernorm_bwd_noalloc": 2,
+    "magma_layernorm_bwd_residual": 2,
     "magma_gemm": 1,
     "magma_attention_fwd": 1, "magma_attention_bwd": 3, "magma_adam_step": 1,
     "magma_adam_step_multi": 1, "magma_embedding_fwd": 1, "magma_embedding_bwd": 2,
-    "magma_cross_entropy_fwd_bwd": 1, "magma_reduce_sum": 1, "magma_gelu_fwd": 1,
+    "magma_cross_entropy_fwd_bwd": 1,
+    "magma_cross_entropy_fwd_bwd_rowstats": 1, "magma_reduce_sum": 1, "magma_gelu_fwd": 1,
     "magma_gelu_bwd": 1, "magma_relu_fwd": 1, "magma_relu_bwd": 1, "magma_bias_grad": 2,
     "magma_convert": 1, "magma_scale": 1,
 }

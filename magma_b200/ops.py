@@ -93,6 +93,30 @@ def layer_norm_bwd(dy: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor, mean:
     return dx, dgamma, dbeta
 
 
+def layer_norm_bwd_residual(dy: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor,
+                            mean: torch.Tensor, rstd: torch.Tensor, dx: torch.Tensor,
+                            accumulate_dx: bool = True, bf16_copy: bool = True,
+                            col_sums: bool = True):
+    """LayerNorm VJP into an F32 residual gradient dx (added, or written), with
+    the BF16 copy of the final dx and its column sums (the bias gradient of the
+    Linear feeding the residual, Autodiff.swift:221-257) ->
+    (dx, dx_bf16 | None, dgamma, dbeta, dcol | None)."""
+    _check_cuda(dy, x, gamma, mean, rstd, dx)
+    assert x.dtype == torch.float32 and dx.dtype == torch.float32
+    dim = x.shape[-1]
+    rows = x.numel() // dim
+    copy = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device) if bf16_copy else None
+    dgamma = torch.empty(dim, dtype=torch.float32, device=x.device)
+    dbeta = torch.empty(dim, dtype=torch.float32, device=x.device)
+    dcol = torch.empty(dim, dtype=torch.float32, device=x.device) if col_sums else None
+    ws_n = lib.query("magma_layernorm_bwd_residual_workspace_size", rows, dim)
+    ws = workspace(ws_n, x.device)
+    lib.call("magma_layernorm_bwd_residual", _ptr(dy), _ptr(x), _ptr(gamma), _ptr(mean),
+             _ptr(rstd), _ptr(dx), _ptr(copy), _ptr(dgamma), _ptr(dbeta), _ptr(dcol), rows, dim,
+             _dtype(dy), int(accumulate_dx), 0, _ptr(ws), ws.numel(), _stream())
+    return dx, copy, dgamma, dbeta, dcol
+
+
 # ------------------------------------------------------------------------- GEMM
 def gemm(a: torch.Tensor, b: torch.Tensor, *, trans_a: bool = False, trans_b: bool = False,
          out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
@@ -113,9 +137,14 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, trans_a: bool = False, trans_b: bo
     if out is None:
         out = torch.empty((m, n), dtype=out_dtype or a.dtype, device=a.device)
     assert out.shape == (m, n) and out.stride(1) == 1
-    for t in (aux_in, aux_out):
-        if t is not None:
-            assert t.shape == (m, n) and t.stride(0) == out.stride(0)
+    if epilogue == lib.EPI_ROWSTATS:
+        # aux_out: float2 softmax partials [ceil(n / 64)][m]
+        assert aux_out is not None and aux_out.dtype == torch.float32
+        assert aux_out.numel() >= (n + 63) // 64 * m * 2
+    else:
+        for t in (aux_in, aux_out):
+            if t is not None:
+                assert t.shape == (m, n) and t.stride(0) == out.stride(0)
     ws_n = lib.query("magma_gemm_workspace_size", m, n, k, _dtype(a))
     ws = workspace(ws_n, a.device) if ws_n else None
     lib.call("magma_gemm", _ptr(a), _ptr(b), _ptr(out), m, n, k, a.stride(0), b.stride(0),
@@ -230,6 +259,29 @@ def cross_entropy_fwd_bwd(logits: torch.Tensor, targets: torch.Tensor, classes: 
                                                            device=logits.device)
     lib.call("magma_cross_entropy_fwd_bwd", _ptr(logits), _ptr(targets), _ptr(losses), rows,
              classes, logits.stride(0), grad_scale, _dtype(logits), _stream())
+    return losses
+
+
+def lm_head_cross_entropy(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, classes: int,
+                          logits: torch.Tensor, grad_scale: float | None = None,
+                          losses: torch.Tensor | None = None):
+    """Fused lm-head + softmax CE (main.swift:412-433): logits[:, :classes] =
+    x . w[:classes]^T as BF16 with the GEMM's per-row softmax partials, then the
+    loss and dlogits (in place, padded columns zeroed) from one read of the
+    logits. x [rows, D] BF16, w [>= classes, D] BF16, logits [rows, ld] BF16.
+    Returns the per-row losses."""
+    _check_cuda(x, w, targets, logits)
+    rows, d = x.shape
+    ld = logits.stride(0)
+    grad_scale = 1.0 / rows if grad_scale is None else grad_scale
+    losses = losses if losses is not None else torch.empty(rows, dtype=torch.float32,
+                                                           device=x.device)
+    stats = torch.empty((classes + 63) // 64 * rows * 2, dtype=torch.float32, device=x.device)
+    lib.call("magma_gemm", _ptr(x), _ptr(w), _ptr(logits), rows, classes, d, x.stride(0),
+             w.stride(0), ld, 0, 1, lib.BF16, lib.BF16, lib.EPI_ROWSTATS, None, None, _ptr(stats),
+             None, 0, _stream())
+    lib.call("magma_cross_entropy_fwd_bwd_rowstats", _ptr(logits), _ptr(stats), _ptr(targets),
+             _ptr(losses), rows, classes, ld, grad_scale, lib.BF16, _stream())
     return losses
 
 

@@ -106,6 +106,35 @@ def test_layernorm_bf16_io_and_accumulate(cuda, oracle, rows, dim):
     close(dgb.cpu(), r[1], 1e-3)
 
 
+@pytest.mark.parametrize("rows,dim,acc,dy_bf16", [(8192, 768, True, True), (1000, 384, False, True),
+                                                 (777, 136, True, False)])
+def test_layernorm_bwd_residual(cuda, oracle, rows, dim, acc, dy_bf16):
+    """LN VJP added into an F32 residual gradient, with its BF16 copy and
+    column sums (the residual Linear's bias gradient)."""
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(rows + dim)
+    x = rng.standard_normal((rows, dim)).astype(np.float32)
+    g = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+    dy = rng.standard_normal((rows, dim)).astype(np.float32)
+    if dy_bf16:
+        dy = bf16_round(dy)
+    base = rng.standard_normal((rows, dim)).astype(np.float32)
+    _, mean, rstd = ops.layer_norm_fwd(t(x), t(g), t(b))
+    dx = t(base)
+    dxo, copy, dg, db, dcol = ops.layer_norm_bwd_residual(
+        t(dy, torch.bfloat16 if dy_bf16 else torch.float32), t(x), t(g), mean, rstd, dx,
+        accumulate_dx=acc)
+    rdx, rdg, rdb = oracle.layernorm_bwd(dy, x, g)
+    want = (base + rdx) if acc else rdx
+    close(dxo.cpu(), want, 1e-4)
+    close(copy.float().cpu(), bf16_round(dxo.cpu().numpy()), 0)
+    close(dg.cpu(), rdg, 1e-4)
+    close(db.cpu(), rdb, 1e-4)
+    close(dcol.cpu(), want.astype(np.float64).sum(0), 1e-4)
+
+
 def test_layernorm_empty_rows(cuda):
     from magma_b200 import ops
 
@@ -409,6 +438,43 @@ def test_cross_entropy(cuda, oracle, rows, classes, ld):
     assert torch.count_nonzero(buf[:, classes:]).item() == 0
 
 
+@pytest.mark.parametrize("rows,d,classes,ld", [(256, 64, 1000, 1024), (300, 128, 50257, 50304)])
+def test_lm_head_cross_entropy_fused(cuda, oracle, rows, d, classes, ld):
+    """lm-head GEMM with per-row softmax partials in its epilogue + the one-pass
+    CE against the oracle's CE on the same BF16 logits (main.swift:412-433)."""
+    from magma_b200 import lib, ops
+
+    rng = np.random.default_rng(rows + classes)
+    x = bf16_round(rng.standard_normal((rows, d)).astype(np.float32))
+    w = bf16_round((0.5 * rng.standard_normal((ld, d))).astype(np.float32))
+    tg = rng.integers(0, classes, rows).astype(np.int32)
+    logits = torch.full((rows, ld), 7.0, device="cuda", dtype=torch.bfloat16)
+    losses = ops.lm_head_cross_entropy(t(x, torch.bfloat16), t(w, torch.bfloat16),
+                                       t(tg, torch.int32), classes, logits)
+    torch.cuda.synchronize()
+    assert ops.device_error_check() == 0
+    # the logits the GEMM stored are BF16 roundings of x . w^T
+    ref_logits = bf16_round((x.astype(np.float64) @ w[:classes].astype(np.float64).T)
+                            .astype(np.float32))
+    rloss, rd = oracle.cross_entropy(ref_logits, tg)
+    close(losses.cpu().mean().reshape(1), np.array([rloss]), 2e-3)
+    close(logits[:, :classes].float().cpu(), rd, 2e-2)
+    assert torch.count_nonzero(logits[:, classes:]).item() == 0
+    # the partials themselves: chunk maxima and sums of the stored logits
+    stats = torch.empty(((classes + 63) // 64) * rows * 2, device="cuda")
+    c = torch.empty((rows, ld), device="cuda", dtype=torch.bfloat16)
+    lib.call("magma_gemm", t(x, torch.bfloat16).data_ptr(), t(w, torch.bfloat16).data_ptr(),
+             c.data_ptr(), rows, classes, d, d, d, ld, 0, 1, lib.BF16, lib.BF16, lib.EPI_ROWSTATS,
+             None, None, stats.data_ptr(), None, 0, torch.cuda.current_stream().cuda_stream)
+    st = stats.view(-1, rows, 2).cpu().numpy()
+    cv = c[:, :classes].float().cpu().numpy().astype(np.float64)
+    for j in (0, st.shape[0] - 1):
+        chunk = cv[:, 64 * j:64 * j + 64]
+        m = chunk.max(1)
+        close(st[j, :, 0], m, 1e-6)
+        close(st[j, :, 1], np.exp(chunk - m[:, None]).sum(1), 1e-5)
+
+
 def test_cross_entropy_closed_form(cuda):
     from magma_b200 import ops
 
@@ -462,6 +528,11 @@ def test_gelu_relu_bias_convert(cuda, oracle):
     close(ops.relu_bwd(t(x), t(dy)).cpu(), np.where(x > 0, dy, 0), 0)
     m = rng.standard_normal((3001, 77)).astype(np.float32)
     close(ops.bias_grad(t(m)).cpu(), m.astype(np.float64).sum(0), 1e-5)
+    # vectorised path (columns % 8 == 0), F32 and BF16, rows not a multiple of 256
+    m = rng.standard_normal((8195, 3072)).astype(np.float32)
+    close(ops.bias_grad(t(m)).cpu(), m.astype(np.float64).sum(0), 1e-5)
+    mb = bf16_round(m[:, :2304])
+    close(ops.bias_grad(t(mb, torch.bfloat16)).cpu(), mb.astype(np.float64).sum(0), 1e-5)
     dst = torch.empty(10001, dtype=torch.bfloat16, device="cuda")
     ops.convert(t(x), dst)
     assert torch.equal(dst, t(x).to(torch.bfloat16))

@@ -30,6 +30,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -346,6 +347,53 @@ __device__ __forceinline__ void row_stats64(const uint32_t (&ra)[32], const uint
   *out = make_float2(m, (s4[0] + s4[1]) + (s4[2] + s4[3]));
 }
 
+// BF16 output with softmax partials: packs the 64 values once, stores the
+// pairs (16-byte stores when vec8 and the chunk is whole) and takes the
+// partials from the stored BF16 values, unpacked with integer shifts (the
+// conversion unit is shared with the exponentials).
+__device__ __forceinline__ void direct_store64_stats(__nv_bfloat16* dst_row, int64_t col0,
+                                                     int64_t N, const uint32_t (&ra)[32],
+                                                     const uint32_t (&rb)[32], bool vec8,
+                                                     float2* out) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int valid = (int)(N - col0 < 64 ? N - col0 : 64);
+  uint32_t pk[32];
+#pragma unroll
+  for (int p = 0; p < 32; ++p) {
+    const int j = 2 * p;
+    const __nv_bfloat162 h = __floats2bfloat162_rn(
+        __uint_as_float(j < 32 ? ra[j] : rb[j - 32]),
+        __uint_as_float(j + 1 < 32 ? ra[j + 1] : rb[j + 1 - 32]));
+    pk[p] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  if (vec8 && valid == 64) {
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      *reinterpret_cast<uint4*>(dst_row + col0 + 8 * g) =
+          make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (j < valid)
+        dst_row[col0 + j] = __ushort_as_bfloat16((unsigned short)(j & 1 ? pk[j >> 1] >> 16
+                                                                       : pk[j >> 1] & 0xFFFFu));
+  }
+  auto val = [&](int j) {
+    return __uint_as_float(j & 1 ? pk[j >> 1] & 0xFFFF0000u : pk[j >> 1] << 16);
+  };
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 64; ++j)
+    if (j < valid) m4[j & 3] = fmaxf(m4[j & 3], val(j));
+  const float m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+  const float ml = m * kLog2e;
+#pragma unroll
+  for (int j = 0; j < 64; ++j)
+    if (j < valid) s4[j & 3] += sm100::ex2_approx(fmaf(val(j), kLog2e, -ml));
+  *out = make_float2(m, (s4[0] + s4[1]) + (s4[2] + s4[3]));
+}
+
 // One 32-column chunk of one warp's 32 tile rows: this lane handles the
 // column pair (col, col+1) of rows rsel, rsel+2, ..., st points at that pair
 // in row rsel of the staged F32 accumulators (row pitch P). The epilogue is a
@@ -629,13 +677,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (args.splits > 1)
               direct_store64<float>(args.ws + (int64_t)split * M * N + row * N, nullptr,
                                     (int64_t)n0 + c0, N, ra, rb, ws_vec8);
-            else
+            else if (rowstats && std::is_same<TC, __nv_bfloat16>::value)
+              direct_store64_stats(reinterpret_cast<__nv_bfloat16*>(args.C) + row * args.e.ldc,
+                                   (int64_t)n0 + c0, N, ra, rb, c_vec8,
+                                   static_cast<float2*>(args.e.aux_out) + ((n0 + c0) >> 6) * M + row);
+            else {
               direct_store64<TC>(static_cast<TC*>(args.C) + row * args.e.ldc,
                                  has_bias ? args.e.bias : nullptr, (int64_t)n0 + c0, N, ra, rb,
                                  c_vec8);
-            if (rowstats)
-              row_stats64<TC>(ra, rb, (int64_t)n0 + c0, N,
-                              static_cast<float2*>(args.e.aux_out) + ((n0 + c0) >> 6) * M + row);
+              if (rowstats)
+                row_stats64<TC>(ra, rb, (int64_t)n0 + c0, N,
+                                static_cast<float2*>(args.e.aux_out) + ((n0 + c0) >> 6) * M + row);
+            }
           }
         }
       } else {

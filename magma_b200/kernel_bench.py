@@ -73,6 +73,8 @@ def bench_gemm(only: str | None, reps: int) -> list[dict]:
         c = torch.empty((m, n), device="cuda", dtype=od)
         kw = {}
         if epi == lib.EPI_ROWSTATS:
+            # the trainer's layout: real vocabulary columns of the padded logits
+            c = torch.empty((m, V), device="cuda", dtype=od)[:, :n]
             kw["aux_out"] = torch.empty(((n + 63) // 64) * m * 2, device="cuda")
         if epi in (lib.EPI_BIAS, lib.EPI_BIAS_GELU, lib.EPI_BIAS_RESIDUAL):
             kw["bias"] = torch.randn(n, device="cuda")
@@ -153,10 +155,9 @@ def bench_ce(reps: int) -> list[dict]:
     w = (0.02 * torch.randn((V, D), device="cuda")).to(torch.bfloat16)
     ops.gemm(x, w[:50257], trans_b=True, out=logits[:, :50257], epilogue=lib.EPI_ROWSTATS,
              aux_out=stats)
-    st = torch.cuda.current_stream().cuda_stream
     ms = _time(lambda: lib.call("magma_cross_entropy_fwd_bwd_rowstats", logits.data_ptr(),
                                 stats.data_ptr(), tg.data_ptr(), losses.data_ptr(), T, 50257, V,
-                                1.0 / T, lib.BF16, st), reps)
+                                1.0 / T, lib.BF16, torch.cuda.current_stream().cuda_stream), reps)
     out.append({"kernel": "cross_entropy_rowstats", "us": round(ms * 1e3, 2),
                 "GBs": round((T * V * 4 + nch * T * 8) / ms / 1e6, 1)})
     return out

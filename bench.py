@@ -354,8 +354,8 @@ def main() -> None:
         tr.capture()
 
     def step():
-        tr.run_fwd_bwd()
-        tr.optimizer_step(grad_scale=sync(tr.grads))
+        # gradient all-reduce per backward segment, overlapped with the rest
+        tr.optimizer_step(grad_scale=tr.run_fwd_bwd(sync=sync))
 
     for _ in range(args.warmup):
         step()

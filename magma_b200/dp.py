@@ -47,14 +47,52 @@ class GradSync:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.bucket_bytes = bucket_bytes
+        self._stream = None
+        self._works = []
+
+    def _buckets(self, grads: torch.Tensor):
+        flat = grads.view(-1)
+        per = max(1, self.bucket_bytes // flat.element_size())
+        for start in range(0, flat.numel(), per):
+            yield flat[start:start + per]
 
     def __call__(self, grads: torch.Tensor) -> float:
         if self.world == 1:
             return 1.0
-        flat = grads.view(-1)
-        per = max(1, self.bucket_bytes // flat.element_size())
-        for start in range(0, flat.numel(), per):
-            dist.all_reduce(flat[start:start + per], op=dist.ReduceOp.SUM, group=self.group)
+        for b in self._buckets(grads):
+            dist.all_reduce(b, op=dist.ReduceOp.SUM, group=self.group)
+        return 1.0 / self.world
+
+    def launch(self, grads: torch.Tensor) -> None:
+        """Starts the sum all-reduce of one finished gradient range. On CUDA it
+        runs on a communication stream that first waits for the work queued so
+        far on the current stream, so the next backward segment overlaps it;
+        finish() joins. Every rank must launch the same ranges in the same
+        order. (CPU tensors: done synchronously.)"""
+        if self.world == 1:
+            return
+        if not grads.is_cuda:
+            for b in self._buckets(grads):
+                dist.all_reduce(b, op=dist.ReduceOp.SUM, group=self.group)
+            return
+        if self._stream is None:
+            self._stream = torch.cuda.Stream(grads.device)
+        self._stream.wait_stream(torch.cuda.current_stream(grads.device))
+        with torch.cuda.stream(self._stream):
+            for b in self._buckets(grads):
+                self._works.append(
+                    dist.all_reduce(b, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+
+    def finish(self) -> float:
+        """Makes the current stream wait for every launched all-reduce and
+        returns the 1/world scale for Adam."""
+        if self.world == 1:
+            return 1.0
+        for w in self._works:
+            w.wait()
+        self._works = []
+        if self._stream is not None:
+            torch.cuda.current_stream(self._stream.device).wait_stream(self._stream)
         return 1.0 / self.world
 
 

@@ -257,8 +257,28 @@ class GPTTrainer:
                  self.ws.numel(), self._s())
 
     # ------------------------------------------------------------ fwd + bwd
+    # layers per backward segment: the gradient sync of a finished segment
+    # overlaps the backward of the next one
+    SYNC_GROUP = 3
+
     def step_fwd_bwd(self) -> None:
         """Forward + backward on the resident batch; writes self.grads and self.loss."""
+        for _ in self._fwd_bwd_parts():
+            pass
+
+    def _grad_range(self, lo_layer: int, hi_layer: int) -> tuple[int, int]:
+        """Arena range of the parameters of layers lo_layer .. hi_layer."""
+        lo = self.table[f"h{lo_layer}.ln1_w"][0]
+        nxt = (f"h{hi_layer + 1}.ln1_w" if hi_layer + 1 < self.cfg.layers else "lnf_w")
+        return lo, self.table[nxt][0]
+
+    def _num_parts(self) -> int:
+        return (self.cfg.layers + self.SYNC_GROUP - 1) // self.SYNC_GROUP
+
+    def _fwd_bwd_parts(self):
+        """Forward + backward as a generator: after every SYNC_GROUP layers of
+        the backward it yields the gradient-arena ranges that are final (the
+        last yield, after the embeddings, also covers wte, wpe and lnf)."""
         cfg, T, D, L = self.cfg, self.T, self.cfg.dim, self.cfg.layers
         s = self._s()
         P, G, W = self.params, self.grads, self.weight
@@ -316,6 +336,7 @@ class GPTTrainer:
         self._ln_bwd(self.d_ln, self.x[L], self.view(P, "lnf_w"), self.lnf_stats[0],
                      self.lnf_stats[1], self.view(G, "lnf_w"), self.view(G, "lnf_b"),
                      self.view(G, f"h{L - 1}.fcproj_b"), accumulate=0)
+        seg_top = L - 1
         for l in reversed(range(L)):
             n = lambda k: f"h{l}.{k}"  # noqa: E731
             st = self.stats[l]
@@ -355,12 +376,19 @@ class GPTTrainer:
                          self.view(G, n("ln1_w")), self.view(G, n("ln1_b")),
                          self.view(G, f"h{l - 1}.fcproj_b") if l > 0 else None,
                          bf16_copy=l > 0)
+            # layers l .. seg_top are final (layer l-1's fcproj bias gradient,
+            # written just above, belongs to the next segment)
+            if (seg_top - l + 1 == self.SYNC_GROUP) and l > 0:
+                yield [self._grad_range(l, seg_top)]
+                seg_top = l - 1
         # embeddings: dwte += scatter(dresid); dwpe = sum over batch
         self.view(G, "wpe").zero_()
         if not cfg.tied:
             self.view(G, "wte").zero_()
         lib.call("magma_embedding_bwd", _p(self.tokens), _p(self.dresid), _p(self.view(G, "wte")),
                  _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp, s)
+        yield [self._grad_range(0, seg_top), (0, self.table["h0.ln1_w"][0]),
+               (self.table["lnf_w"][0], self.P)]
 
     def _dresid_operand(self) -> torch.Tensor:
         """The residual gradient as a GEMM operand: the BF16 copy the last
@@ -377,22 +405,37 @@ class GPTTrainer:
 
     # ------------------------------------------------------------- graphs
     def capture(self) -> None:
-        """Records step_fwd_bwd as one CUDA graph (after one eager warm-up)."""
+        """Records forward+backward as CUDA graphs, one per backward segment
+        (after one eager warm-up), so that a data-parallel gradient sync can
+        start between them."""
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
             self.step_fwd_bwd()
         torch.cuda.current_stream(self.dev).wait_stream(s)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.step_fwd_bwd()
-        self.graph = g
+        parts = self._fwd_bwd_parts()
+        graphs = []
+        for _ in range(self._num_parts()):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                ranges = next(parts)
+            graphs.append((g, ranges))
+        for _ in parts:  # nothing is left to run after the last yield
+            raise RuntimeError("backward produced more segments than expected")
+        self.graph = graphs
 
-    def run_fwd_bwd(self) -> None:
-        if self.graph is not None:
-            self.graph.replay()
-        else:
-            self.step_fwd_bwd()
+    def run_fwd_bwd(self, sync=None) -> float:
+        """Forward + backward; with `sync` (a dp.GradSync) the sum all-reduce of
+        each finished backward segment's gradients is started while the next
+        segment runs. Returns the gradient scale for Adam (1/world with sync)."""
+        parts = ([r for _, r in self.graph] if self.graph is not None else self._fwd_bwd_parts())
+        for i, ranges in enumerate(parts):
+            if self.graph is not None:
+                self.graph[i][0].replay()
+            if sync is not None:
+                for lo, hi in ranges:
+                    sync.launch(self.grads[lo:hi])
+        return sync.finish() if sync is not None else 1.0
 
     # --------------------------------------------------------- public step
     def set_batch(self, tokens: torch.Tensor, targets: torch.Tensor) -> None:
@@ -402,9 +445,10 @@ class GPTTrainer:
     def train_step(self, tokens: torch.Tensor, targets: torch.Tensor, allreduce=None) -> float:
         """Host tokens/targets [B, S] in, host loss out: H2D, fwd+bwd, DP sync, Adam, D2H."""
         self.set_batch(tokens, targets)
-        self.run_fwd_bwd()
-        scale = 1.0
-        if allreduce is not None:
+        if allreduce is None or hasattr(allreduce, "launch"):
+            scale = self.run_fwd_bwd(sync=allreduce)
+        else:
+            self.run_fwd_bwd()
             scale = allreduce(self.grads)
         self.optimizer_step(grad_scale=scale)
         return float(self.loss.item())

@@ -52,6 +52,13 @@ def _rank_main(rank, port, bucket_bytes, out_q):
         loss, grads = oracle.gpt_fwd_bwd(cfg, params, shard[:, :-1], shard[:, 1:])
         g = torch.from_numpy(grads.copy())
         scale = dp.GradSync(bucket_bytes=bucket_bytes)(g)
+        # the segmented form (launch per finished range, then finish) sums the same
+        g2 = torch.from_numpy(grads.copy())
+        sync = dp.GradSync(bucket_bytes=bucket_bytes)
+        k = g2.numel() // 3
+        sync.launch(g2[k:])
+        sync.launch(g2[:k])
+        assert sync.finish() == scale and torch.equal(g2, g)
         out_q.put((rank, loss, grads, (g * scale).numpy(), scale))
         dist.barrier()
         dist.destroy_process_group()

@@ -253,36 +253,50 @@ def test_gemm_bf16_split_k(cuda, m, n, k, ta, tb):
     close(yb.float().cpu(), (ref + bias).cpu(), 2e-2)
 
 
-def test_gemm_bf16_epilogues(cuda, oracle):
+# (384, 384): aligned rows; (381, 381): rows not 8-byte aligned (scalar
+# column pairs); (389, 392): padded rows with a ragged last group of columns.
+@pytest.mark.parametrize("n,ld", [(384, 384), (381, 381), (389, 392)])
+def test_gemm_bf16_epilogues(cuda, oracle, n, ld):
     from magma_b200 import ops, lib
 
     g = torch.Generator(device="cuda").manual_seed(5)
-    m, n, k = 512, 384, 256
+    m, k = 512, 256
     a = torch.randn((m, k), device="cuda", generator=g).to(torch.bfloat16)
     w = torch.randn((n, k), device="cuda", generator=g).to(torch.bfloat16)
     bias = torch.randn(n, device="cuda", generator=g)
     acc = a.float() @ w.float().T
     pre = acc + bias
-    y = ops.gemm(a, w, trans_b=True, out_dtype=torch.float32, epilogue=lib.EPI_BIAS, bias=bias)
+
+    def buf(dtype, fill=None):
+        full = (torch.randn((m, ld), device="cuda", generator=g) if fill is None
+                else torch.full((m, ld), fill, device="cuda"))
+        return full.to(dtype)[:, :n]
+
+    y = ops.gemm(a, w, trans_b=True, out=buf(torch.float32, 0.0), epilogue=lib.EPI_BIAS, bias=bias)
     close(y.cpu(), pre.cpu(), 1e-4)
-    aux = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
-    yg = ops.gemm(a, w, trans_b=True, epilogue=lib.EPI_BIAS_GELU, bias=bias, aux_out=aux)
+    aux = buf(torch.bfloat16, 0.0)
+    yg = ops.gemm(a, w, trans_b=True, out=buf(torch.bfloat16, 0.0), epilogue=lib.EPI_BIAS_GELU,
+                  bias=bias, aux_out=aux)
     close(aux.float().cpu(), pre.cpu(), 2e-2)
     close(yg.float().cpu(), oracle.gelu_fwd(pre.cpu().numpy()), 2e-2)
-    resid = torch.randn((m, n), device="cuda", generator=g)
-    yr = ops.gemm(a, w, trans_b=True, out_dtype=torch.float32, epilogue=lib.EPI_BIAS_RESIDUAL,
-                  bias=bias, aux_in=resid)
+    resid = buf(torch.float32)
+    yr = ops.gemm(a, w, trans_b=True, out=buf(torch.float32, 0.0),
+                  epilogue=lib.EPI_BIAS_RESIDUAL, bias=bias, aux_in=resid)
     close(yr.cpu(), (resid + pre).cpu(), 1e-4)
-    dg = ops.gemm(a, w, trans_b=True, epilogue=lib.EPI_DGELU, aux_in=aux)
+    dg = ops.gemm(a, w, trans_b=True, out=buf(torch.bfloat16, 0.0), epilogue=lib.EPI_DGELU,
+                  aux_in=aux)
     want = oracle.gelu_bwd(aux.float().cpu().numpy(), acc.cpu().numpy())
     close(dg.float().cpu(), want, 2e-2)
-    c = torch.randn((m, n), device="cuda", generator=g)
+    c = buf(torch.float32)
     c0 = c.clone()
     ops.gemm(a, w, trans_b=True, out=c, epilogue=lib.EPI_ACCUMULATE)
     close(c.cpu(), (c0 + acc).cpu(), 1e-4)
-    yr2 = ops.gemm(a, w, trans_b=True, out_dtype=torch.float32, epilogue=lib.EPI_BIAS_RELU,
-                   bias=bias, aux_out=torch.empty((m, n), device="cuda"))
+    yr2 = ops.gemm(a, w, trans_b=True, out=buf(torch.float32, 0.0), epilogue=lib.EPI_BIAS_RELU,
+                   bias=bias, aux_out=buf(torch.float32, 0.0))
     close(yr2.cpu(), torch.relu(pre).cpu(), 1e-4)
+    dr = ops.gemm(a, w, trans_b=True, out=buf(torch.float32, 0.0), epilogue=lib.EPI_DRELU,
+                  aux_in=resid)
+    close(dr.cpu(), torch.where(resid > 0, acc, torch.zeros_like(acc)).cpu(), 1e-4)
 
 
 @pytest.mark.parametrize("m,n,k,ta,tb", [(256, 128, 784, 0, 0), (784, 128, 256, 1, 0),

@@ -185,7 +185,7 @@ struct TcCfg {
   // Epilogue staging: per epilogue warp a 32 x 32 F32 chunk, row pitch 34
   // floats (8-byte aligned rows; conflict-free 8-byte stores by row and
   // 8-byte loads by column pair).
-  static constexpr int kStagePitch = 34;
+  static constexpr int kStagePitch = 36;  // floats: 16-byte rows, conflict-free float4 access
   static constexpr int kStageWarpFloats = 32 * kStagePitch;
   static constexpr int kStagingBytes = kEpiWarps * kStageWarpFloats * 4;
   static constexpr int kSmemLimit = 232448;  // sm_100 dynamic shared memory per block
@@ -209,6 +209,7 @@ struct TcArgs {
   int* err;
   int vec_ok;   // C/aux pointers 8-B aligned and ldc even: column-pair vector accesses
   int vec8_ok;  // C 16-B aligned and ldc % 8 == 0: 8-column vector stores
+  int epi_vec8; // vec8_ok with 16-B aligned aux and bias: 8-column staged epilogue
   // Split-K: work unit u covers output tile (u % tiles) over k-blocks
   // [s*kb_per_split, (s+1)*kb_per_split) with s = u / tiles. With splits > 1
   // the raw F32 accumulator goes to ws + s*M*N (leading dimension N) and a
@@ -463,6 +464,76 @@ __device__ __forceinline__ void epi_rows(const TcArgs& a, const float* __restric
   }
 }
 
+// Staged epilogue, 8 columns per lane: for one 32-column chunk staged as
+// [32 rows][P] floats, lane (r8 = lane / 4, g = lane % 4) handles columns
+// [col, col + 8) of rows r8, r8 + 8, r8 + 16, r8 + 24: 16-byte shared reads,
+// 16-byte auxiliary loads (all issued first) and 16-byte stores, a warp
+// instruction covering 8 rows x 64-128 contiguous bytes. Same arithmetic and
+// order as epi_value.
+template <typename TC, int EPI, int P>
+__device__ __forceinline__ void epi_rows8(const TcArgs& a, const float* __restrict__ st,
+                                          int64_t row0, int rows_here, int r8, int64_t col,
+                                          const float (&b)[8]) {
+  constexpr bool kAux = EPI == MAGMA_EPI_BIAS_RESIDUAL || EPI == MAGMA_EPI_DGELU ||
+                        EPI == MAGMA_EPI_DRELU || EPI == MAGMA_EPI_ACCUMULATE;
+  // auxiliary operand element type: the F32 residual stream, else C's type
+  using AuxT = typename std::conditional<EPI == MAGMA_EPI_BIAS_RESIDUAL, float, TC>::type;
+  constexpr int kWords = kAux ? (int)sizeof(AuxT) / 2 : 1;  // 16-B words per 8 elements
+  const int64_t ldc = a.e.ldc;
+  TC* C = static_cast<TC*>(a.C);
+  const bool hb = a.e.bias != nullptr;
+  // raw 16-byte words of the four rows' auxiliary operand, all loads in flight
+  uint4 raw[4][kWords];
+  const AuxT* src = EPI == MAGMA_EPI_ACCUMULATE ? reinterpret_cast<const AuxT*>(C)
+                                                : static_cast<const AuxT*>(a.e.aux_in);
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + r8;
+    if (r >= rows_here) break;
+    if constexpr (kAux) {
+      if ((it & 1) == 0) {  // two rows' loads in flight at a time
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (r + 8 * k < rows_here) {
+            const uint4* q = reinterpret_cast<const uint4*>(src + (row0 + r + 8 * k) * ldc + col);
+#pragma unroll
+            for (int w = 0; w < kWords; ++w) raw[it + k][w] = q[w];
+          }
+        }
+      }
+    }
+    const float4 lo = *reinterpret_cast<const float4*>(st + r * P);
+    const float4 hi = *reinterpret_cast<const float4*>(st + r * P + 4);
+    const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    const int64_t off = (row0 + r) * ldc + col;
+    float x[8];
+    if constexpr (kAux) load8(reinterpret_cast<const AuxT*>(raw[it]), x);
+    float o[8];
+    if constexpr (EPI == MAGMA_EPI_BIAS_RESIDUAL) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(x[i], hb ? __fadd_rn(v[i], b[i]) : v[i]);
+    } else if constexpr (EPI == MAGMA_EPI_BIAS_GELU || EPI == MAGMA_EPI_BIAS_RELU) {
+      float pre[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pre[i] = hb ? __fadd_rn(v[i], b[i]) : v[i];
+      store8(static_cast<TC*>(a.e.aux_out) + off, pre);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        o[i] = EPI == MAGMA_EPI_BIAS_GELU ? gelu_t<TC>(pre[i]) : fmaxf(pre[i], 0.f);
+    } else if constexpr (EPI == MAGMA_EPI_DGELU) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[i], gelu_grad_t<TC>(x[i]));
+    } else if constexpr (EPI == MAGMA_EPI_DRELU) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = x[i] > 0.f ? v[i] : 0.f;
+    } else {  // ACCUMULATE
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __fadd_rn(x[i], v[i]);
+    }
+    store8(C + off, o);
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, typename TC, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -634,6 +705,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     float* stage = reinterpret_cast<float*>(base_ptr + Cfg::kStageOffset) +
                    (warp - 2) * Cfg::kStageWarpFloats;
     const bool vec2 = args.vec_ok != 0;
+    const bool epi_vec8 = args.epi_vec8 != 0;
     const bool ws_vec8 = (N % 8) == 0;
     const bool c_vec8 = args.vec8_ok != 0;
     const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
@@ -642,6 +714,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const bool has_bias = args.e.bias != nullptr &&
                           (args.e.epi == MAGMA_EPI_BIAS || args.e.epi == MAGMA_EPI_BIAS_GELU ||
                            args.e.epi == MAGMA_EPI_BIAS_RESIDUAL || args.e.epi == MAGMA_EPI_BIAS_RELU);
+    // auxiliary operand the staged epilogue reads, for the L2 prefetch
+    const char* aux_pf = nullptr;
+    int64_t aux_esz = sizeof(TC);
+    if (args.splits == 1) {
+      if (args.e.epi == MAGMA_EPI_BIAS_RESIDUAL) {
+        aux_pf = static_cast<const char*>(args.e.aux_in);
+        aux_esz = 4;
+      } else if (args.e.epi == MAGMA_EPI_DGELU || args.e.epi == MAGMA_EPI_DRELU) {
+        aux_pf = static_cast<const char*>(args.e.aux_in);
+      } else if (args.e.epi == MAGMA_EPI_ACCUMULATE) {
+        aux_pf = static_cast<const char*>(args.C);
+      }
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int unit = ustart; unit < num_units; unit += ustride) {
@@ -650,6 +735,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int tn = args.n_fast ? tile % tiles_n : tile / tiles_m;
       const int m0 = tm * kTM + (int)rank * kBM;
       const int n0 = tn * BN + half * kCols;
+      if (aux_pf != nullptr) {
+        // While the accumulator is still being computed, pull this warp's
+        // block of the auxiliary operand (its 32 rows x kCols columns) into L2,
+        // one row per lane, so the epilogue's loads of it hit L2.
+        const int64_t row = (int64_t)m0 + q * 32 + lane;
+        if (row < M && n0 < N) {
+          const char* p0 = aux_pf + (row * args.e.ldc + n0) * aux_esz;
+          const char* p1 = p0 + min((int64_t)kCols, (int64_t)N - n0) * aux_esz;
+          for (const char* p = reinterpret_cast<const char*>(reinterpret_cast<uintptr_t>(p0) & ~(uintptr_t)127);
+               p < p1; p += 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+        }
+      }
       if (!sm100::mbar_wait(tfull_bar(acc), acc_phase, args.err)) break;
       sm100::tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) +
@@ -703,10 +801,39 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (c0 + 32 >= kCols) release();
           float* srow = stage + lane * P;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            *reinterpret_cast<float2*>(srow + 2 * j) =
-                make_float2(__uint_as_float(ra[2 * j]), __uint_as_float(ra[2 * j + 1]));
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(srow + 4 * j) =
+                make_float4(__uint_as_float(ra[4 * j]), __uint_as_float(ra[4 * j + 1]),
+                            __uint_as_float(ra[4 * j + 2]), __uint_as_float(ra[4 * j + 3]));
           __syncwarp();
+          if (std::is_same<TC, __nv_bfloat16>::value && epi_vec8) {
+            const int r8 = lane >> 2, g8 = lane & 3;
+            const int64_t col8 = (int64_t)n0 + c0 + 8 * g8;
+            if (col8 < N && rows_here > 0) {
+              const float* st8 = stage + r8 * P + 8 * g8;
+              if (col8 + 8 <= N) {
+                float b8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if (has_bias) load8(args.e.bias + col8, b8);
+                switch (args.e.epi) {
+                  case MAGMA_EPI_BIAS_GELU: epi_rows8<TC, MAGMA_EPI_BIAS_GELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                  case MAGMA_EPI_BIAS_RESIDUAL: epi_rows8<TC, MAGMA_EPI_BIAS_RESIDUAL, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                  case MAGMA_EPI_DGELU: epi_rows8<TC, MAGMA_EPI_DGELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                  case MAGMA_EPI_ACCUMULATE: epi_rows8<TC, MAGMA_EPI_ACCUMULATE, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                  case MAGMA_EPI_BIAS_RELU: epi_rows8<TC, MAGMA_EPI_BIAS_RELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                  default: epi_rows8<TC, MAGMA_EPI_DRELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                }
+              } else {  // ragged last columns, element by element
+                TC* C = static_cast<TC*>(args.C);
+                for (int r = r8; r < rows_here; r += 8)
+                  for (int i = 0; col8 + i < N; ++i) {
+                    const int64_t off = (row0 + r) * args.e.ldc + col8 + i;
+                    C[off] = from_f32<TC>(epi_value<TC>(args.e, C, off, col8 + i, st8[(r - r8) * P + i]));
+                  }
+              }
+            }
+            __syncwarp();
+            continue;
+          }
           const int64_t col = (int64_t)n0 + c0 + 2 * cp;
           if (col < N && rows_here > 0) {
             const bool pair = col + 1 < N;
@@ -802,7 +929,7 @@ EpiCost epi_cost(int epi, bool c32) {
     case MAGMA_EPI_BIAS_GELU:
     case MAGMA_EPI_BIAS_RELU: return {2.0 * c, 2.33};
     case MAGMA_EPI_DGELU:
-    case MAGMA_EPI_DRELU: return {2.0 * c, 3.60};
+    case MAGMA_EPI_DRELU: return {2.0 * c, 2.33};
     case MAGMA_EPI_ACCUMULATE: return {2.0 * c, 2.33};
     default: return {c, c32 ? 2.53 : 1.95};   // direct row stores
   }
@@ -1098,7 +1225,8 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
     // share an A block run together and it is read from HBM once.
     const double a_bytes = 2.0 * (double)m * (double)k, b_bytes = 2.0 * (double)n * (double)k;
     const int n_fast = (a_bytes > 64e6 && a_bytes >= b_bytes && n > (plan.pair ? 256 : 128)) ? 1 : 0;
-    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, vec8_ok, plan.splits,
+    const int epi_vec8 = vec8_ok && aligned16(aux_in) && aligned16(aux_out) && aligned16(bias);
+    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, vec8_ok, epi_vec8, plan.splits,
                 plan.kb_per_split, static_cast<float*>(workspace), n_fast};
     return c32 ? dispatch_plan<float>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
                : dispatch_plan<__nv_bfloat16>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b,

@@ -182,11 +182,12 @@ struct TcCfg {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  // Epilogue staging: per epilogue warp a 32 x 32 F32 chunk, row pitch 34
-  // floats (8-byte aligned rows; conflict-free 8-byte stores by row and
-  // 8-byte loads by column pair).
-  static constexpr int kStagePitch = 36;  // floats: 16-byte rows, conflict-free float4 access
-  static constexpr int kStageWarpFloats = 32 * kStagePitch;
+  // Epilogue staging, 8 KB per epilogue warp: either a 32 x 32 F32 chunk of
+  // accumulators with row pitch 36 floats (16-byte rows, conflict-free float4
+  // access), or the swizzled TMA-store buffers of the direct epilogue (four
+  // 32 x 32 BF16 boxes or two 32 x 32 F32 boxes).
+  static constexpr int kStagePitch = 36;
+  static constexpr int kStageWarpFloats = 2048;
   static constexpr int kStagingBytes = kEpiWarps * kStageWarpFloats * 4;
   static constexpr int kSmemLimit = 232448;  // sm_100 dynamic shared memory per block
   static constexpr int kReserve = kStagingBytes + 1024 + 256;  // staging, alignment, barriers
@@ -210,6 +211,7 @@ struct TcArgs {
   int vec_ok;   // C/aux pointers 8-B aligned and ldc even: column-pair vector accesses
   int vec8_ok;  // C 16-B aligned and ldc % 8 == 0: 8-column vector stores
   int epi_vec8; // vec8_ok with 16-B aligned aux and bias: 8-column staged epilogue
+  int tma_out;  // direct epilogue stores through the tensor map tmC (C, or the split partials)
   // Split-K: work unit u covers output tile (u % tiles) over k-blocks
   // [s*kb_per_split, (s+1)*kb_per_split) with s = u / tiles. With splits > 1
   // the raw F32 accumulator goes to ws + s*M*N (leading dimension N) and a
@@ -395,6 +397,97 @@ __device__ __forceinline__ void direct_store64_stats(__nv_bfloat16* dst_row, int
   *out = make_float2(m, (s4[0] + s4[1]) + (s4[2] + s4[3]));
 }
 
+// Direct epilogue through TMA stores. A warp's 64-column block of its 32 tile
+// rows is written row = lane into swizzled shared-memory boxes of 32 rows x 32
+// columns, which lane 0 then stores with TMA: every global write is a whole
+// 64- or 128-byte row segment and the stores leave the warp's issue slots. The
+// warp's 8 KB hold two BF16 blocks (a block is rewritten once the store of the
+// block before the previous one has read it) or one F32 block.
+//
+// BF16: pk holds the 64 values as packed pairs; boxes have 64-byte rows with
+// the 64-byte swizzle (16-byte unit u of row r at unit u ^ ((r >> 1) & 3)).
+__device__ __forceinline__ void tma_block64_bf16(uint8_t* wbuf, int it, const uint32_t (&pk)[32],
+                                                 const CUtensorMap* map, int x, int y, int64_t N,
+                                                 int lane) {
+  constexpr int kBox = 32 * 64;
+  uint8_t* blk = wbuf + (it & 1) * 2 * kBox;
+  if (lane == 0) sm100::bulk_wait_group_read<1>();
+  __syncwarp();
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint8_t* row = blk + h * kBox + lane * 64;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      *reinterpret_cast<uint4*>(row + ((u ^ sw) << 4)) =
+          make_uint4(pk[16 * h + 4 * u], pk[16 * h + 4 * u + 1], pk[16 * h + 4 * u + 2],
+                     pk[16 * h + 4 * u + 3]);
+  }
+  sm100::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (x + 32 * h < N) sm100::tma_store_2d(map, sm100::smem_u32(blk + h * kBox), x + 32 * h, y);
+    sm100::bulk_commit_group();
+  }
+}
+
+// F32 (outputs and split-K partials): boxes have 128-byte rows with the
+// 128-byte swizzle (16-byte unit u of row r at unit u ^ (r & 7)); z >= 0
+// selects the 3-D partial map (x, y, split).
+__device__ __forceinline__ void tma_block64_f32(uint8_t* wbuf, const uint32_t (&ra)[32],
+                                                const uint32_t (&rb)[32], const CUtensorMap* map,
+                                                int x, int y, int z, int64_t N, int lane) {
+  constexpr int kBox = 32 * 128;
+  if (lane == 0) sm100::bulk_wait_group_read<0>();
+  __syncwarp();
+  const int sw = lane & 7;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t(&r)[32] = h ? rb : ra;
+    uint8_t* row = wbuf + h * kBox + lane * 128;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      *reinterpret_cast<uint4*>(row + ((u ^ sw) << 4)) =
+          make_uint4(r[4 * u], r[4 * u + 1], r[4 * u + 2], r[4 * u + 3]);
+  }
+  sm100::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (x + 32 * h >= N) continue;
+      const uint32_t src = sm100::smem_u32(wbuf + h * kBox);
+      if (z >= 0) sm100::tma_store_3d(map, src, x + 32 * h, y, z);
+      else sm100::tma_store_2d(map, src, x + 32 * h, y);
+    }
+    sm100::bulk_commit_group();
+  }
+}
+
+// Softmax partials of one row over 64 columns from BF16 pairs packed as in
+// tma_block64_bf16 (same arithmetic as direct_store64_stats).
+__device__ __forceinline__ void stats64_packed(const uint32_t (&pk)[32], int64_t col0, int64_t N,
+                                               float2* out) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int valid = (int)(N - col0 < 64 ? N - col0 : 64);
+  auto val = [&](int j) {
+    return __uint_as_float(j & 1 ? pk[j >> 1] & 0xFFFF0000u : pk[j >> 1] << 16);
+  };
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 64; ++j)
+    if (j < valid) m4[j & 3] = fmaxf(m4[j & 3], val(j));
+  const float m = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+  const float ml = m * kLog2e;
+#pragma unroll
+  for (int j = 0; j < 64; ++j)
+    if (j < valid) s4[j & 3] += sm100::ex2_approx(fmaf(val(j), kLog2e, -ml));
+  *out = make_float2(m, (s4[0] + s4[1]) + (s4[2] + s4[3]));
+}
+
 // One 32-column chunk of one warp's 32 tile rows: this lane handles the
 // column pair (col, col+1) of rows rsel, rsel+2, ..., st points at that pair
 // in row rsel of the staged F32 accumulators (row pitch P). The epilogue is a
@@ -537,7 +630,7 @@ __device__ __forceinline__ void epi_rows8(const TcArgs& a, const float* __restri
 template <int BN, bool A_MN, bool B_MN, typename TC, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               TcArgs args) {
+               const __grid_constant__ CUtensorMap tmC, TcArgs args) {
   using Cfg = TcCfg<BN, PAIR>;
   constexpr int kTM = PAIR ? 2 * kBM : kBM;  // output rows per tile
   constexpr int S = Cfg::kStages;
@@ -711,6 +804,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
                         args.e.epi == MAGMA_EPI_BIAS || args.e.epi == MAGMA_EPI_ROWSTATS;
     const bool rowstats = args.splits == 1 && args.e.epi == MAGMA_EPI_ROWSTATS;
+    const bool tma_direct = direct && args.tma_out != 0;
+    uint8_t* wbuf = reinterpret_cast<uint8_t*>(stage);
+    int blk_it = 0;  // 64-column blocks this warp has stored through TMA
     const bool has_bias = args.e.bias != nullptr &&
                           (args.e.epi == MAGMA_EPI_BIAS || args.e.epi == MAGMA_EPI_BIAS_GELU ||
                            args.e.epi == MAGMA_EPI_BIAS_RESIDUAL || args.e.epi == MAGMA_EPI_BIAS_RELU);
@@ -735,6 +831,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int tn = args.n_fast ? tile % tiles_n : tile / tiles_m;
       const int m0 = tm * kTM + (int)rank * kBM;
       const int n0 = tn * BN + half * kCols;
+      // bias of this warp's columns for the TMA-store epilogue: lane l holds
+      // column n0 + 32 j + l, loaded before the accumulator wait
+      float bl[kCols / 32];
+#pragma unroll
+      for (int j = 0; j < kCols / 32; ++j) {
+        const int64_t col = (int64_t)n0 + 32 * j + lane;
+        bl[j] = (tma_direct && has_bias && args.splits == 1 && col < N) ? args.e.bias[col] : 0.f;
+      }
       if (aux_pf != nullptr) {
         // While the accumulator is still being computed, pull this warp's
         // block of the auxiliary operand (its 32 rows x kCols columns) into L2,
@@ -762,7 +866,50 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           else sm100::mbar_arrive(tempty_bar(acc));
         }
       };
-      if (direct) {
+      if (tma_direct) {
+#pragma unroll
+        for (int c0 = 0; c0 < kCols; c0 += 64) {
+          uint32_t ra[32], rb[32];
+          sm100::tmem_ld32(taddr + c0, ra);
+          sm100::tmem_ld32(taddr + c0 + 32, rb);
+          sm100::tmem_wait_ld();
+          if (c0 + 64 >= kCols) release();
+          if (n0 + c0 >= N || row0 >= M) continue;
+          if (has_bias && args.splits == 1) {  // split partials: bias added by the reduce
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              ra[i] = __float_as_uint(__fadd_rn(__uint_as_float(ra[i]),
+                                                __shfl_sync(0xffffffffu, bl[c0 / 32], i)));
+              rb[i] = __float_as_uint(__fadd_rn(__uint_as_float(rb[i]),
+                                                __shfl_sync(0xffffffffu, bl[c0 / 32 + 1], i)));
+            }
+          }
+          if (args.splits > 1) {
+            tma_block64_f32(wbuf, ra, rb, &tmC, n0 + c0, (int)row0, split, N, lane);
+          } else if constexpr (std::is_same<TC, float>::value) {
+            tma_block64_f32(wbuf, ra, rb, &tmC, n0 + c0, (int)row0, -1, N, lane);
+            if (rowstats && row0 + lane < M)
+              row_stats64<TC>(ra, rb, (int64_t)n0 + c0, N,
+                              static_cast<float2*>(args.e.aux_out) + ((n0 + c0) >> 6) * M + row0 + lane);
+          } else {
+            uint32_t pk[32];
+#pragma unroll
+            for (int p = 0; p < 16; ++p) {
+              const __nv_bfloat162 lo = __floats2bfloat162_rn(__uint_as_float(ra[2 * p]),
+                                                              __uint_as_float(ra[2 * p + 1]));
+              const __nv_bfloat162 hi = __floats2bfloat162_rn(__uint_as_float(rb[2 * p]),
+                                                              __uint_as_float(rb[2 * p + 1]));
+              pk[p] = *reinterpret_cast<const uint32_t*>(&lo);
+              pk[16 + p] = *reinterpret_cast<const uint32_t*>(&hi);
+            }
+            tma_block64_bf16(wbuf, blk_it, pk, &tmC, n0 + c0, (int)row0, N, lane);
+            if (rowstats && row0 + lane < M)
+              stats64_packed(pk, (int64_t)n0 + c0, N,
+                             static_cast<float2*>(args.e.aux_out) + ((n0 + c0) >> 6) * M + row0 + lane);
+          }
+          ++blk_it;
+        }
+      } else if (direct) {
 #pragma unroll 1
         for (int c0 = 0; c0 < kCols; c0 += 64) {
           uint32_t ra[32], rb[32];
@@ -865,6 +1012,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // the TMA stores must finish before the shared memory they read goes away
+    if (tma_direct && lane == 0) sm100::bulk_wait_group_all();
+    __syncwarp();
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -952,7 +1102,7 @@ TcPlan choose_plan(int64_t M, int64_t N, int64_t K, int epi, bool c32) {
   const double kb_us[4] = {0.300, 0.515, 0.311, 0.335};    // tensor time per k-block
   const double kb_bytes[4] = {32768, 49152, 24576, 32768};  // SMEM fill per k-block per CTA
   const double l2_bytes_per_us[4] = {96.0e3, 94.7e3, 75.5e3, 87.9e3};  // per SM
-  const double pair_setup_us = 1.8, split_setup_us = 0.26, reduce_bytes_per_us = 2.87e6;
+  const double pair_setup_us = 1.8, split_setup_us = 0.26, reduce_bytes_per_us = 6.0e6;
   const EpiCost ec = epi_cost(epi, c32);
   const EpiCost ep = epi_cost(MAGMA_EPI_NONE, true);  // F32 partial stores
   const int allowed = gemm_option_mask();
@@ -1062,6 +1212,36 @@ magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int
     st = encode_tensor_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, b, N, K, ldb * 2, 64, 64,
                               CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
+  // Store map of the direct epilogue: the F32 split-K partials [splits][M][N]
+  // as a 3-D tensor, or C itself (32 x 32 boxes, 64-byte swizzle for BF16
+  // rows of 64 bytes, 128-byte swizzle for F32 rows of 128 bytes).
+  CUtensorMap tc;
+  memset(&tc, 0, sizeof(tc));
+  TcArgs a2 = args;
+  a2.tma_out = 0;
+  const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
+                      args.e.epi == MAGMA_EPI_BIAS || args.e.epi == MAGMA_EPI_ROWSTATS;
+  if (direct && args.splits > 1) {
+    if (N % 4 == 0 && aligned16(args.ws)) {
+      const uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)args.splits};
+      const uint64_t strides[2] = {(uint64_t)N * 4, (uint64_t)(M * N * 4)};
+      const uint32_t box[3] = {32, 32, 1};
+      if (magma_status_t s3 = encode_tensor_map_3d(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, args.ws,
+                                                   dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+        return s3;
+      a2.tma_out = 1;
+    }
+  } else if (direct) {
+    const int64_t row_bytes = args.e.ldc * (int64_t)sizeof(TC);
+    if (row_bytes % 16 == 0 && aligned16(args.C)) {
+      const bool bf = std::is_same<TC, __nv_bfloat16>::value;
+      if (magma_status_t s3 = encode_tensor_map_2d(
+              &tc, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, args.C,
+              N, M, row_bytes, 32, 32, bf ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+        return s3;
+      a2.tma_out = 1;
+    }
+  }
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, TC, PAIR>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -1089,13 +1269,13 @@ magma_status_t launch_tc(const void* a, const void* b, int64_t M, int64_t N, int
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (magma_status_t st = cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, args),
+    if (magma_status_t st = cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, a2),
                                         "gemm_tcgen05_pair launch"))
       return st;
   } else {
     int grid = num_sms();
     if (units < grid) grid = (int)units;
-    kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, args);
+    kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, a2);
   }
   if (magma_status_t st = check_launch("gemm_tcgen05")) return st;
   if (args.splits > 1) {
@@ -1226,7 +1406,7 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
     const double a_bytes = 2.0 * (double)m * (double)k, b_bytes = 2.0 * (double)n * (double)k;
     const int n_fast = (a_bytes > 64e6 && a_bytes >= b_bytes && n > (plan.pair ? 256 : 128)) ? 1 : 0;
     const int epi_vec8 = vec8_ok && aligned16(aux_in) && aligned16(aux_out) && aligned16(bias);
-    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, vec8_ok, epi_vec8, plan.splits,
+    TcArgs args{m, n, k, c, e, device_error_word(), vec_ok, vec8_ok, epi_vec8, 0, plan.splits,
                 plan.kb_per_split, static_cast<float*>(workspace), n_fast};
     return c32 ? dispatch_plan<float>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b, args, s)
                : dispatch_plan<__nv_bfloat16>(plan, a, b, m, n, k, lda, ldb, trans_a, trans_b,

@@ -212,6 +212,11 @@ def classify(name, args, cfg, tr):
         acc = 4 if args[13] else 0
         copy = 2 if args[6] else 0
         return "layernorm", rows * dim * (dyb + 4 + 4 + acc + copy) + rows * 8
+    if name == "magma_adam_step_clipped":
+        n = args[5]
+        return "adam", n * (28 + (2 if args[4] else 0))
+    if name == "magma_grad_norm":
+        return "adam", args[1] * 4.0  # one read of the gradient arena
     if name == "magma_adam_step":
         n = args[5]
         return "adam", n * (28 + (2 if args[4] else 0))
@@ -343,7 +348,11 @@ def main() -> None:
     torch.cuda.set_device(local)
     cfg = gpt2_small()
     B, S = args.batch, cfg.seq
-    tr = GPTTrainer(cfg, B, "bf16", lr=3e-4, seed=0)
+    # the reference GPT trainer's optimiser settings (TrainConfig.shakespeare,
+    # main.swift:76-91): AdamW-style decay, global-norm clipping at 1.0 and a
+    # warmup-cosine schedule, all inside the timed step
+    tr = GPTTrainer(cfg, B, "bf16", lr=6e-4, beta1=0.9, beta2=0.99, weight_decay=0.1, seed=0,
+                    grad_clip=1.0, lr_schedule=(100, 5000, 6e-5))
     sync = dp.GradSync()
     gen = torch.Generator().manual_seed(1234 + rank)
     tok_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()

@@ -274,6 +274,41 @@ MAGMA_API magma_status_t magma_adam_step_multi(float* const* params, const float
                                      float weight_decay, int64_t step, float grad_scale,
                                      void* stream);
 
+/* Global L2 norm of a gradient arena, as optim.clipGradNorm forms it
+ * (Sources/Core/Optimizer.swift:1229-1247; applied by the GPT trainer before
+ * every Adam step, Benchmarks/GPT2Shakespeare/Sources/main.swift:857):
+ * norm[0] = sqrt(sum_i (grads[i] * grad_scale)^2), grad_scale being the 1/n of
+ * a data-parallel mean. norm is a device F32 scalar. workspace holds per-block
+ * partial sums: at least magma_grad_norm_workspace_size(n) bytes, 4-byte
+ * aligned, on the device. The sum is taken in a fixed order, so the result is
+ * the same on every run on the same GPU model. */
+MAGMA_API int64_t magma_grad_norm_workspace_size(int64_t n);
+MAGMA_API magma_status_t magma_grad_norm(const float* grads, int64_t n, float grad_scale,
+                                         float* norm, void* workspace, int64_t workspace_bytes,
+                                         void* stream);
+
+/* Adam with global-norm clipping fused in front (clipGradNorm's scaling,
+ * Optimizer.swift:1249-1267, then optim.Adam.step, :354-412): with
+ * c = max_norm / (norm + 1e-6) if that is below 1, else 1 (also 1 for a NaN
+ * norm), the gradient is g = (grad * grad_scale) * c, then the update of
+ * magma_adam_step. grad_norm is the device scalar magma_grad_norm wrote; it is
+ * read on the device, so no host synchronisation sits between the two calls. */
+MAGMA_API magma_status_t magma_adam_step_clipped(float* params, const float* grads, float* m,
+                                                 float* v, void* shadow_bf16, int64_t n,
+                                                 float lr, float beta1, float beta2, float eps,
+                                                 float weight_decay, int64_t step,
+                                                 float grad_scale, const float* grad_norm,
+                                                 float max_norm, void* stream);
+
+/* Learning rate of optim.WarmupCosineScheduler (Optimizer.swift:766-803) at
+ * scheduler step `step` (0 for the first training step; clamped to
+ * total_steps as the scheduler's step() clamps): linear warmup
+ * base_lr * (step + 1) / warmup_steps, then min_lr + (base_lr - min_lr) *
+ * (1 + cos(pi * progress)) / 2. F32 arithmetic in the reference's order; host
+ * only (no device work). Requires 0 <= warmup_steps < total_steps. */
+MAGMA_API magma_status_t magma_lr_warmup_cosine(float base_lr, float min_lr, int64_t warmup_steps,
+                                                int64_t total_steps, int64_t step, float* lr);
+
 /* ---- glue ops on the same graphs ------------------------------------------ */
 
 /* Token + position embedding gather (Sources/Core/Data.swift:856-886, GPT

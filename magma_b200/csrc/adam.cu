@@ -14,6 +14,14 @@
 //
 // HBM-bound: 16 B read of p, g, m, v and 12 B written per element (+2 B for the
 // optional BF16 shadow copy), float4-vectorised with a grid sized to the SMs.
+//
+// Global-norm clipping (optim.clipGradNorm, Optimizer.swift:1229-1267, as the
+// GPT trainer applies it before every Adam step, main.swift:857) is split in
+// two: grad_sumsq_partial + grad_norm_finish write the norm of the scaled
+// gradient to a device scalar (per-block sums in a fixed order, so the result
+// does not depend on scheduling), and the clipped Adam kernels read that
+// scalar and scale g by the clip coefficient before the update, so no host
+// synchronisation sits between the two.
 #include <cmath>
 
 #include "common.cuh"
@@ -24,11 +32,23 @@ namespace {
 struct AdamScalars {
   float b1, omb1, b2, omb2, bc1, bc2, eps, lr, lrwd, grad_scale;
   int has_wd;
+  const float* norm;  // clipped update: device scalar with the global gradient norm
+  float max_norm;
 };
 
+// Clip coefficient of clipGradNorm (Optimizer.swift:1253-1262): maxNorm /
+// (norm + 1e-6) where that is below 1, else 1 (also 1 for a NaN norm, as the
+// reference's lessThan mask is then false).
+__device__ __forceinline__ float clip_coeff(const AdamScalars& s) {
+  if (s.norm == nullptr) return 1.f;
+  const float raw = __fdiv_rn(s.max_norm, __fadd_rn(*s.norm, 1e-6f));
+  return raw < 1.f ? raw : 1.f;
+}
+
 __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
-                                          const AdamScalars& s) {
+                                          const AdamScalars& s, float coeff = 1.f) {
   g = __fmul_rn(g, s.grad_scale);
+  if (s.norm != nullptr) g = __fmul_rn(g, coeff);  // clipped gradient
   if (s.has_wd) p = __fsub_rn(p, __fmul_rn(p, s.lrwd));
   m = __fadd_rn(__fmul_rn(m, s.b1), __fmul_rn(g, s.omb1));
   v = __fadd_rn(__fmul_rn(v, s.b2), __fmul_rn(__fmul_rn(g, g), s.omb2));
@@ -41,6 +61,7 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
 __global__ void __launch_bounds__(256)
 adam_vec4(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
           float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, int64_t n, AdamScalars s) {
+  const float coeff = clip_coeff(s);
   const int64_t n4 = n >> 2;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
@@ -48,10 +69,10 @@ adam_vec4(float* __restrict__ p, const float* __restrict__ g, float* __restrict_
     float4 gv = __ldcs(reinterpret_cast<const float4*>(g) + i);
     float4 mv = reinterpret_cast<float4*>(m)[i];
     float4 vv = reinterpret_cast<float4*>(v)[i];
-    adam_elem(pv.x, gv.x, mv.x, vv.x, s);
-    adam_elem(pv.y, gv.y, mv.y, vv.y, s);
-    adam_elem(pv.z, gv.z, mv.z, vv.z, s);
-    adam_elem(pv.w, gv.w, mv.w, vv.w, s);
+    adam_elem(pv.x, gv.x, mv.x, vv.x, s, coeff);
+    adam_elem(pv.y, gv.y, mv.y, vv.y, s, coeff);
+    adam_elem(pv.z, gv.z, mv.z, vv.z, s, coeff);
+    adam_elem(pv.w, gv.w, mv.w, vv.w, s, coeff);
     reinterpret_cast<float4*>(p)[i] = pv;
     __stcs(reinterpret_cast<float4*>(m) + i, mv);
     __stcs(reinterpret_cast<float4*>(v) + i, vv);
@@ -68,7 +89,7 @@ adam_vec4(float* __restrict__ p, const float* __restrict__ g, float* __restrict_
   if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
     int64_t i = (n4 << 2) + threadIdx.x;
     float pp = p[i], mm = m[i], vv = v[i];
-    adam_elem(pp, g[i], mm, vv, s);
+    adam_elem(pp, g[i], mm, vv, s, coeff);
     p[i] = pp;
     m[i] = mm;
     v[i] = vv;
@@ -79,10 +100,11 @@ adam_vec4(float* __restrict__ p, const float* __restrict__ g, float* __restrict_
 __global__ void __launch_bounds__(256)
 adam_scalar(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
             float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, int64_t n, AdamScalars s) {
+  const float coeff = clip_coeff(s);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     float pp = p[i], mm = m[i], vv = v[i];
-    adam_elem(pp, g[i], mm, vv, s);
+    adam_elem(pp, g[i], mm, vv, s, coeff);
     p[i] = pp;
     m[i] = mm;
     v[i] = vv;
@@ -136,7 +158,90 @@ magma_status_t make_scalars(float lr, float beta1, float beta2, float eps, float
   s->lrwd = lr * wd;
   s->has_wd = wd != 0.f;
   s->grad_scale = grad_scale;
+  s->norm = nullptr;
+  s->max_norm = 0.f;
   return MAGMA_OK;
+}
+
+// ---- global gradient norm ----------------------------------------------------
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum(float x, float* red) {
+  x = warp_sum(x);  // butterfly: the same order on every run
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[w] = x;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x == 0)
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+  return t;  // valid in thread 0
+}
+
+// partial[b] = sum over this block's grid-stride elements of (g * scale)^2.
+__global__ void __launch_bounds__(kNormThreads)
+grad_sumsq_partial(const float* __restrict__ g, int64_t n, float scale, int vec,
+                   float* __restrict__ partial) {
+  __shared__ float red[kNormThreads / 32];
+  float acc = 0.f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (vec) {
+    const int64_t n4 = n >> 2;
+    for (int64_t i = i0; i < n4; i += stride) {
+      const float4 t = __ldcs(reinterpret_cast<const float4*>(g) + i);
+      const float a = __fmul_rn(t.x, scale), b = __fmul_rn(t.y, scale);
+      const float c = __fmul_rn(t.z, scale), d = __fmul_rn(t.w, scale);
+      acc = fmaf(a, a, acc);
+      acc = fmaf(b, b, acc);
+      acc = fmaf(c, c, acc);
+      acc = fmaf(d, d, acc);
+    }
+    if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+      const float a = __fmul_rn(g[(n4 << 2) + threadIdx.x], scale);
+      acc = fmaf(a, a, acc);
+    }
+  } else {
+    for (int64_t i = i0; i < n; i += stride) {
+      const float a = __fmul_rn(g[i], scale);
+      acc = fmaf(a, a, acc);
+    }
+  }
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) partial[blockIdx.x] = t;
+}
+
+// norm[0] = sqrt(sum of the partials), summed in block order.
+__global__ void __launch_bounds__(kNormThreads)
+grad_norm_finish(const float* __restrict__ partial, int nb, float* __restrict__ norm) {
+  __shared__ float red[kNormThreads / 32];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) acc += partial[i];
+  const float t = block_sum(acc, red);
+  if (threadIdx.x == 0) norm[0] = __fsqrt_rn(t);
+}
+
+int64_t norm_blocks(int64_t n) {
+  int64_t b = ceil_div((n >> 2) > 0 ? (n >> 2) : 1, kNormThreads);
+  const int64_t cap = 4LL * num_sms();
+  return b > cap ? cap : b;
+}
+
+magma_status_t launch_adam(float* params, const float* grads, float* m, float* v,
+                           void* shadow_bf16, int64_t n, const AdamScalars& s, cudaStream_t cs) {
+  int threads = 256;
+  bool vec = aligned16(params) && aligned16(grads) && aligned16(m) && aligned16(v) &&
+             (shadow_bf16 == nullptr || (reinterpret_cast<uintptr_t>(shadow_bf16) & 7u) == 0);
+  int64_t work = vec ? (n >> 2) : n;
+  int64_t blocks = ceil_div(work > 0 ? work : 1, threads);
+  int64_t cap = 8LL * num_sms();
+  if (blocks > cap) blocks = cap;
+  if (vec)
+    adam_vec4<<<(int)blocks, threads, 0, cs>>>(params, grads, m, v, (__nv_bfloat16*)shadow_bf16,
+                                               n, s);
+  else
+    adam_scalar<<<(int)blocks, threads, 0, cs>>>(params, grads, m, v,
+                                                 (__nv_bfloat16*)shadow_bf16, n, s);
+  return check_launch("adam_step");
 }
 
 }  // namespace
@@ -156,21 +261,69 @@ magma_status_t magma_adam_step(float* params, const float* grads, float* m, floa
     return st;
   if (n == 0) return MAGMA_OK;
   MAGMA_REQUIRE(params && grads && m && v, "magma_adam_step: NULL pointer");
+  return launch_adam(params, grads, m, v, shadow_bf16, n, s, (cudaStream_t)stream);
+}
+
+int64_t magma_grad_norm_workspace_size(int64_t n) {
+  return n > 0 ? 4 * norm_blocks(n) : 0;
+}
+
+magma_status_t magma_grad_norm(const float* grads, int64_t n, float grad_scale, float* norm,
+                               void* workspace, int64_t workspace_bytes, void* stream) {
+  MAGMA_REQUIRE(n >= 0, "magma_grad_norm: negative size");
+  MAGMA_REQUIRE(norm != nullptr, "magma_grad_norm: NULL norm");
   cudaStream_t cs = (cudaStream_t)stream;
-  int threads = 256;
-  bool vec = aligned16(params) && aligned16(grads) && aligned16(m) && aligned16(v) &&
-             (shadow_bf16 == nullptr || (reinterpret_cast<uintptr_t>(shadow_bf16) & 7u) == 0);
-  int64_t work = vec ? (n >> 2) : n;
-  int64_t blocks = ceil_div(work > 0 ? work : 1, threads);
-  int64_t cap = 8LL * num_sms();
-  if (blocks > cap) blocks = cap;
-  if (vec)
-    adam_vec4<<<(int)blocks, threads, 0, cs>>>(params, grads, m, v, (__nv_bfloat16*)shadow_bf16,
-                                               n, s);
-  else
-    adam_scalar<<<(int)blocks, threads, 0, cs>>>(params, grads, m, v,
-                                                 (__nv_bfloat16*)shadow_bf16, n, s);
-  return check_launch("adam_step");
+  if (n == 0) return cuda_status(cudaMemsetAsync(norm, 0, sizeof(float), cs), "grad_norm memset");
+  MAGMA_REQUIRE(grads != nullptr, "magma_grad_norm: NULL grads");
+  const int64_t nb = norm_blocks(n);
+  MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= 4 * nb,
+                "magma_grad_norm: workspace of %lld bytes needed (magma_grad_norm_workspace_size)",
+                (long long)(4 * nb));
+  MAGMA_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 3u) == 0,
+                "magma_grad_norm: workspace must be 4-byte aligned");
+  float* partial = static_cast<float*>(workspace);
+  grad_sumsq_partial<<<(int)nb, kNormThreads, 0, cs>>>(grads, n, grad_scale,
+                                                       aligned16(grads) ? 1 : 0, partial);
+  if (magma_status_t st = check_launch("grad_sumsq_partial")) return st;
+  grad_norm_finish<<<1, kNormThreads, 0, cs>>>(partial, (int)nb, norm);
+  return check_launch("grad_norm_finish");
+}
+
+magma_status_t magma_adam_step_clipped(float* params, const float* grads, float* m, float* v,
+                                       void* shadow_bf16, int64_t n, float lr, float beta1,
+                                       float beta2, float eps, float weight_decay, int64_t step,
+                                       float grad_scale, const float* grad_norm, float max_norm,
+                                       void* stream) {
+  MAGMA_REQUIRE(n >= 0, "magma_adam_step_clipped: negative size");
+  MAGMA_REQUIRE(grad_norm != nullptr, "magma_adam_step_clipped: NULL grad_norm");
+  MAGMA_REQUIRE(max_norm > 0.f, "magma_adam_step_clipped: max_norm must be positive");
+  AdamScalars s;
+  if (magma_status_t st = make_scalars(lr, beta1, beta2, eps, weight_decay, step, grad_scale, &s))
+    return st;
+  s.norm = grad_norm;
+  s.max_norm = max_norm;
+  if (n == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(params && grads && m && v, "magma_adam_step_clipped: NULL pointer");
+  return launch_adam(params, grads, m, v, shadow_bf16, n, s, (cudaStream_t)stream);
+}
+
+magma_status_t magma_lr_warmup_cosine(float base_lr, float min_lr, int64_t warmup_steps,
+                                      int64_t total_steps, int64_t step, float* lr) {
+  MAGMA_REQUIRE(lr != nullptr, "magma_lr_warmup_cosine: NULL output");
+  MAGMA_REQUIRE(warmup_steps >= 0, "magma_lr_warmup_cosine: warmup_steps must be non-negative");
+  MAGMA_REQUIRE(total_steps > warmup_steps,
+                "magma_lr_warmup_cosine: total_steps (%lld) must exceed warmup_steps (%lld)",
+                (long long)total_steps, (long long)warmup_steps);
+  MAGMA_REQUIRE(step >= 0, "magma_lr_warmup_cosine: negative step");
+  if (step > total_steps) step = total_steps;  // the scheduler stops counting there
+  if (step < warmup_steps) {
+    *lr = base_lr * (float)(step + 1) / (float)warmup_steps;
+    return MAGMA_OK;
+  }
+  const float progress = (float)(step - warmup_steps) / (float)(total_steps - warmup_steps);
+  const float pi = 3.14159265358979323846f;
+  *lr = min_lr + (base_lr - min_lr) * (1.0f + cosf(pi * progress)) / 2.0f;
+  return MAGMA_OK;
 }
 
 magma_status_t magma_adam_step_multi(float* const* params, const float* const* grads,

@@ -34,7 +34,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import lib
+from . import lib, ops
 
 PER_LAYER = ["ln1_w", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ln2_w", "ln2_b", "fc_w",
              "fc_b", "fcproj_w", "fcproj_b"]
@@ -112,10 +112,17 @@ class GPTTrainer:
     def __init__(self, cfg: GPTConfig, batch: int, precision: str = "bf16", lr: float = 3e-4,
                  beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8,
                  weight_decay: float = 0.0, seed: int = 0, device: int | None = None,
-                 init_std: float = 0.02):
+                 init_std: float = 0.02, grad_clip: float | None = None,
+                 lr_schedule: tuple[int, int, float] | None = None):
+        """grad_clip: max global gradient norm (optim.clipGradNorm before each
+        Adam step) or None; lr_schedule: (warmup_steps, total_steps, min_lr) of
+        optim.WarmupCosineScheduler with lr as its base rate, or None for a
+        constant rate."""
         assert precision in ("bf16", "f32")
+        assert grad_clip is None or grad_clip > 0
         self.cfg, self.B, self.precision = cfg, batch, precision
         self.lr, self.beta1, self.beta2, self.eps, self.wd = lr, beta1, beta2, eps, weight_decay
+        self.grad_clip, self.lr_schedule = grad_clip, lr_schedule
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
         lib.call("magma_init", self.dev.index)
         self.table = cfg.offsets()
@@ -127,6 +134,10 @@ class GPTTrainer:
         self.m = torch.zeros(P, **f32)
         self.v = torch.zeros(P, **f32)
         self.t = 0
+        # device scalar of the last global gradient norm, and its scratch
+        self.grad_norm = torch.zeros(1, **f32)
+        self.norm_ws = torch.empty(max(lib.query("magma_grad_norm_workspace_size", P) // 4, 1),
+                                   **f32)
         self._init_params(seed, init_std)
         self.act_dtype = torch.bfloat16 if precision == "bf16" else torch.float32
         self.DT = lib.BF16 if precision == "bf16" else lib.F32
@@ -396,12 +407,31 @@ class GPTTrainer:
         return self.dresid if self.dresid_a is None else self.dresid_a
 
     # ---------------------------------------------------------------- Adam
+    def current_lr(self) -> float:
+        """The learning rate of the next Adam step: the warmup-cosine schedule
+        at scheduler step t (main.swift:830), or the constant rate."""
+        if self.lr_schedule is None:
+            return self.lr
+        warmup, total, min_lr = self.lr_schedule
+        return ops.lr_warmup_cosine(self.lr, min_lr, warmup, total, self.t)
+
     def optimizer_step(self, grad_scale: float = 1.0) -> None:
-        """optim.Adam.step over the whole arena (Optimizer.swift:354-412)."""
+        """optim.Adam.step over the whole arena (Optimizer.swift:354-412); with
+        grad_clip, clipGradNorm first (main.swift:857): the norm of the
+        (mean) gradient into a device scalar, then Adam on the clipped
+        gradient, with no host synchronisation between them."""
+        lr = self.current_lr()
         self.t += 1
-        lib.call("magma_adam_step", _p(self.params), _p(self.grads), _p(self.m), _p(self.v),
-                 _p(self.shadow), self.P, self.lr, self.beta1, self.beta2, self.eps, self.wd,
-                 self.t, grad_scale, self._s())
+        if self.grad_clip is None:
+            lib.call("magma_adam_step", _p(self.params), _p(self.grads), _p(self.m), _p(self.v),
+                     _p(self.shadow), self.P, lr, self.beta1, self.beta2, self.eps, self.wd,
+                     self.t, grad_scale, self._s())
+            return
+        lib.call("magma_grad_norm", _p(self.grads), self.P, grad_scale, _p(self.grad_norm),
+                 _p(self.norm_ws), self.norm_ws.numel() * 4, self._s())
+        lib.call("magma_adam_step_clipped", _p(self.params), _p(self.grads), _p(self.m),
+                 _p(self.v), _p(self.shadow), self.P, lr, self.beta1, self.beta2, self.eps,
+                 self.wd, self.t, grad_scale, _p(self.grad_norm), self.grad_clip, self._s())
 
     # ------------------------------------------------------------- graphs
     def capture(self) -> None:

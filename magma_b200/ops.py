@@ -218,6 +218,52 @@ def adam_step(params: torch.Tensor, grads: torch.Tensor, m: torch.Tensor, v: tor
              lr, beta1, beta2, eps, weight_decay, step, grad_scale, _stream())
 
 
+def grad_norm_workspace(n: int, device=None) -> torch.Tensor:
+    """Scratch for grad_norm over n elements (per-block partial sums)."""
+    nbytes = lib.query("magma_grad_norm_workspace_size", n)
+    return torch.empty(max(nbytes // 4, 1), dtype=torch.float32, device=device)
+
+
+def grad_norm(grads: torch.Tensor, *, grad_scale: float = 1.0, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Global L2 norm of grads * grad_scale (optim.clipGradNorm,
+    Optimizer.swift:1229-1247) as a one-element device tensor."""
+    _check_cuda(grads, out, workspace)
+    assert grads.dtype == torch.float32 and grads.is_contiguous()
+    n = grads.numel()
+    out = out if out is not None else torch.empty(1, dtype=torch.float32, device=grads.device)
+    ws = workspace if workspace is not None else grad_norm_workspace(n, grads.device)
+    lib.call("magma_grad_norm", _ptr(grads), n, grad_scale, _ptr(out), _ptr(ws),
+             ws.numel() * ws.element_size(), _stream())
+    return out
+
+
+def adam_step_clipped(params: torch.Tensor, grads: torch.Tensor, m: torch.Tensor, v: torch.Tensor,
+                      *, step: int, lr: float, grad_norm: torch.Tensor, max_norm: float,
+                      beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8,
+                      weight_decay: float = 0.0, grad_scale: float = 1.0,
+                      shadow_bf16: torch.Tensor | None = None) -> None:
+    """clipGradNorm's scaling (by the device norm, Optimizer.swift:1249-1267)
+    then optim.Adam.step, in one pass over the arena, in place."""
+    _check_cuda(params, grads, m, v, grad_norm, shadow_bf16)
+    n = params.numel()
+    assert grads.numel() == n and m.numel() == n and v.numel() == n
+    assert all(t.dtype == torch.float32 and t.is_contiguous() for t in (params, grads, m, v))
+    lib.call("magma_adam_step_clipped", _ptr(params), _ptr(grads), _ptr(m), _ptr(v),
+             _ptr(shadow_bf16), n, lr, beta1, beta2, eps, weight_decay, step, grad_scale,
+             _ptr(grad_norm), max_norm, _stream())
+
+
+def lr_warmup_cosine(base_lr: float, min_lr: float, warmup_steps: int, total_steps: int,
+                     step: int) -> float:
+    """optim.WarmupCosineScheduler.currentLR (Optimizer.swift:766-803) at
+    scheduler step `step` (0 for the first training step). Host only."""
+    out = C.c_float()
+    lib.call("magma_lr_warmup_cosine", base_lr, min_lr, warmup_steps, total_steps, step,
+             C.byref(out))
+    return out.value
+
+
 def adam_step_multi(params, grads, ms, vs, *, step: int, lr: float, beta1: float = 0.9,
                     beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.0,
                     grad_scale: float = 1.0) -> None:

@@ -310,6 +310,42 @@ void oracle_adam(float* p, const float* g, float* m, float* v, int64_t n, float 
   }
 }
 
+/* ---- global-norm clipping (Optimizer.swift:1229-1267) and the warmup-cosine
+ * schedule (Optimizer.swift:766-803) ------------------------------------------ */
+/* sqrt(sum_i (g[i]*grad_scale)^2): the products rounded to F32 as the
+ * reference's (grad * grad).sum() of the scaled gradient; the sum in double,
+ * so the oracle has no summation-order error of its own. */
+float oracle_grad_norm(const float* g, int64_t n, float grad_scale) {
+  double acc = 0.0;
+  for (int64_t i = 0; i < n; ++i) {
+    const float a = g[i] * grad_scale;
+    acc += (double)a * (double)a;
+  }
+  return (float)sqrt(acc);
+}
+
+/* clipCoeff = maxNorm / (totalNorm + 1e-6), clamped to 1 (:1253-1262), the
+ * gradient scaled by it (:1265-1267), then the oracle_adam update. */
+void oracle_adam_clipped(float* p, const float* g, float* m, float* v, int64_t n, float lr,
+                         float beta1, float beta2, float eps, float weight_decay, int64_t step,
+                         float grad_scale, float norm, float max_norm) {
+  const float raw = max_norm / (norm + 1e-6f);
+  const float coeff = raw < 1.0f ? raw : 1.0f;
+  float* gc = (float*)malloc((size_t)(n > 0 ? n : 1) * sizeof(float));
+  for (int64_t i = 0; i < n; ++i) gc[i] = (g[i] * grad_scale) * coeff;
+  oracle_adam(p, gc, m, v, n, lr, beta1, beta2, eps, weight_decay, step, 1.0f);
+  free(gc);
+}
+
+/* WarmupCosineScheduler.currentLR (:774-783) at scheduler step `step`. */
+float oracle_lr_warmup_cosine(float base_lr, float min_lr, int64_t warmup, int64_t total,
+                              int64_t step) {
+  if (step > total) step = total;
+  if (step < warmup) return base_lr * (float)(step + 1) / (float)warmup;
+  const float progress = (float)(step - warmup) / (float)(total - warmup);
+  return min_lr + (base_lr - min_lr) * (1.0f + cosf(3.14159265358979323846f * progress)) / 2.0f;
+}
+
 /* ---- GELU (StableHLOEmitter.swift:804-816) and VJP (Autodiff.swift:401-418) */
 static inline float gelu1(float x) {
   float x3 = x * (x * x);

@@ -45,6 +45,14 @@ void oracle_attention_bwd(const float* q, const float* k, const float* v, const 
 
 void oracle_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr, float beta1,
                  float beta2, float eps, float weight_decay, int64_t step, float grad_scale);
+/* Global gradient norm, clipped Adam and warmup-cosine LR (Optimizer.swift:
+ * 1229-1267, 766-803). */
+float oracle_grad_norm(const float* g, int64_t n, float grad_scale);
+void oracle_adam_clipped(float* p, const float* g, float* m, float* v, int64_t n, float lr,
+                         float beta1, float beta2, float eps, float weight_decay, int64_t step,
+                         float grad_scale, float norm, float max_norm);
+float oracle_lr_warmup_cosine(float base_lr, float min_lr, int64_t warmup, int64_t total,
+                              int64_t step);
 
 void oracle_gelu_fwd(const float* x, float* y, int64_t n);
 void oracle_gelu_bwd(const float* x, const float* dy, float* dx, int64_t n);

@@ -57,6 +57,13 @@ def lib():
                                            _i64, _i64, _i64, _i64, C.c_float, C.c_int]
         L.oracle_adam.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, C.c_float, C.c_float,
                                   C.c_float, C.c_float, C.c_float, _i64, C.c_float]
+        L.oracle_grad_norm.argtypes = [_f32p, _i64, C.c_float]
+        L.oracle_grad_norm.restype = C.c_float
+        L.oracle_adam_clipped.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, C.c_float, C.c_float,
+                                          C.c_float, C.c_float, C.c_float, _i64, C.c_float,
+                                          C.c_float, C.c_float]
+        L.oracle_lr_warmup_cosine.argtypes = [C.c_float, C.c_float, _i64, _i64, _i64]
+        L.oracle_lr_warmup_cosine.restype = C.c_float
         L.oracle_gelu_fwd.argtypes = [_f32p, _f32p, _i64]
         L.oracle_gelu_bwd.argtypes = [_f32p, _f32p, _f32p, _i64]
         L.oracle_cross_entropy.argtypes = [_f32p, _i32p, C.c_void_p, _i64, _i64]
@@ -144,6 +151,24 @@ def adam(p, g, m, v, *, lr, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, 
     """In place on p, m, v (float32 arrays)."""
     lib().oracle_adam(p, _f32(g), m, v, p.size, lr, beta1, beta2, eps, weight_decay, step,
                       grad_scale)
+
+
+def grad_norm(g, grad_scale=1.0):
+    """Global L2 norm of the scaled gradient (Optimizer.swift:1229-1247)."""
+    g = _f32(g)
+    return float(lib().oracle_grad_norm(g, g.size, grad_scale))
+
+
+def adam_clipped(p, g, m, v, *, lr, norm, max_norm, beta1=0.9, beta2=0.999, eps=1e-8,
+                 weight_decay=0.0, step=1, grad_scale=1.0):
+    """clipGradNorm's scaling by a given norm, then Adam; in place on p, m, v."""
+    lib().oracle_adam_clipped(p, _f32(g), m, v, p.size, lr, beta1, beta2, eps, weight_decay, step,
+                              grad_scale, norm, max_norm)
+
+
+def lr_warmup_cosine(base_lr, min_lr, warmup, total, step):
+    """WarmupCosineScheduler.currentLR (Optimizer.swift:774-783) at `step`."""
+    return float(lib().oracle_lr_warmup_cosine(base_lr, min_lr, warmup, total, step))
 
 
 def gelu_fwd(x):

@@ -53,6 +53,17 @@ def main() -> None:
             "source": "README.md:84-89, Examples/ValueLayers/main.swift",
             "printed_precision": 4, "loss": {"0": 5.4067, "400": 0.0005, "2000": 0.0},
         },
+        "warmup_cosine_short": {
+            "source": "Tests/CoreTests/SchedulerValidationTests.swift:47-58",
+            "base_lr": 1.0, "min_lr": 0.1, "warmup": 2, "total": 3,
+            "lr_at_step": {"0": 0.5, "2": 1.0, "4": 0.1}, "tol": 1e-6,
+        },
+        "warmup_cosine_long": {
+            "source": "Tests/CoreTests/AdvancedActivationTests.swift:218-241",
+            "base_lr": 0.1, "min_lr": 0.0, "warmup": 10, "total": 100,
+            "lr_at_step": {"0": 0.01, "10": 0.1}, "tol": 1e-6,
+            "midpoint": {"step": 55, "lr": 0.05, "tol": 0.01},
+        },
         "gelu_gradcheck": {
             "source": "Tests/CoreTests/GradientCheckingTests.swift:129-137",
             "points": [-3.0, -1.0, -0.5, 0.0, 0.3, 1.0, 2.5], "fd_eps": 1e-3, "tol": 1e-3,

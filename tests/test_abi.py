@@ -75,3 +75,23 @@ def test_device_count_without_gpu_is_zero_or_more():
     lib.call("magma_device_count", C.byref(n))
     assert n.value >= 0
 
+
+
+def test_lr_warmup_cosine_matches_oracle_bitwise(oracle):
+    """The schedule is host arithmetic: it runs without a GPU and must equal the
+    oracle's F32 restatement bit for bit, clamping at total_steps."""
+    from magma_b200 import ops
+
+    for base, lo, warm, total in [(6e-4, 6e-5, 100, 5000), (1.0, 0.1, 2, 3), (0.1, 0.0, 10, 100),
+                                  (1e-3, 1e-4, 0, 50)]:
+        for step in list(range(0, 12)) + [warm - 1, warm, warm + 1, total // 2, total - 1, total,
+                                          total + 7]:
+            if step < 0:
+                continue
+            got = ops.lr_warmup_cosine(base, lo, warm, total, step)
+            want = oracle.lr_warmup_cosine(base, lo, warm, total, step)
+            assert got == want, (base, lo, warm, total, step, got, want)
+    with pytest.raises(lib.MagmaError):
+        ops.lr_warmup_cosine(0.1, 0.0, 10, 10, 0)  # totalSteps must exceed warmupSteps
+    with pytest.raises(lib.MagmaError):
+        ops.lr_warmup_cosine(0.1, 0.0, -1, 10, 0)

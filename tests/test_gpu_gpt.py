@@ -58,6 +58,34 @@ def test_gpt_f32_matches_oracle(cuda, oracle, tied):
     assert relnorm(tr.params.cpu().numpy(), params) < 1e-4
 
 
+def test_gpt_f32_clip_and_schedule_match_oracle(cuda, oracle):
+    """The trainer with the reference GPT trainer's optimiser loop (main.swift:
+    829-882): warmup-cosine learning rate, global-norm clipping, Adam."""
+    from magma_b200.gpt import GPTConfig, GPTTrainer
+
+    kw = dict(vocab=65, seq=64, layers=2, heads=2, dim=64, tied=True)
+    _, ocfg, tok, tgt = make(oracle, kw, 4, "f32")
+    tr = GPTTrainer(GPTConfig(**kw), 4, "f32", lr=1e-2, beta2=0.99, weight_decay=0.1,
+                    grad_clip=0.5, lr_schedule=(2, 6, 1e-3))
+    tr.set_batch(torch.tensor(tok), torch.tensor(tgt))
+    params = tr.params.cpu().numpy().copy()
+    m = np.zeros_like(params)
+    v = np.zeros_like(params)
+    for step in range(1, 6):
+        lr = oracle.lr_warmup_cosine(1e-2, 1e-3, 2, 6, step - 1)
+        assert tr.current_lr() == lr
+        tr.step_fwd_bwd()
+        loss, grads = oracle.gpt_fwd_bwd(ocfg, params, tok, tgt)
+        assert abs(tr.loss.item() - loss) < 1e-3, (step, tr.loss.item(), loss)
+        norm = oracle.grad_norm(grads)
+        tr.optimizer_step()
+        assert abs(tr.grad_norm.item() - norm) < 1e-3 * norm
+        assert norm > 0.5  # the clip is active on these steps
+        oracle.adam_clipped(params, grads, m, v, lr=lr, norm=norm, max_norm=0.5, beta2=0.99,
+                            weight_decay=0.1, step=step)
+    assert relnorm(tr.params.cpu().numpy(), params) < 1e-4
+
+
 def test_gpt_bf16_close_to_oracle(cuda, oracle):
     kw = dict(vocab=300, seq=128, layers=2, heads=2, dim=128, tied=True)
     tr, ocfg, tok, tgt = make(oracle, kw, 2, "bf16")

@@ -186,6 +186,56 @@ def test_adam_shadow_and_multi(cuda, oracle):
     assert torch.equal(shadow, flat.to(torch.bfloat16))
 
 
+@pytest.mark.parametrize("n,offset", [(1, 0), (3, 0), (1000, 1), ((1 << 20) + 3, 0),
+                                      ((1 << 22) + 1, 1)])
+def test_grad_norm_matches_oracle(cuda, oracle, n, offset):
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(n)
+    g = (rng.standard_normal(n + offset) * 3).astype(np.float32)
+    tg = t(g)[offset:]  # offset 1: a view that is not 16-byte aligned
+    got = ops.grad_norm(tg, grad_scale=0.5)
+    want = oracle.grad_norm(g[offset:], grad_scale=0.5)
+    assert abs(got.item() - want) <= 1e-5 * want, (got.item(), want)
+    again = ops.grad_norm(tg, grad_scale=0.5)
+    assert torch.equal(got, again)  # fixed summation order
+
+
+def test_grad_norm_empty_is_zero(cuda):
+    from magma_b200 import ops
+
+    out = torch.full((1,), 7.0, device="cuda")
+    ops.grad_norm(torch.empty(0, device="cuda"), out=out,
+                  workspace=torch.empty(1, device="cuda"))
+    assert out.item() == 0.0
+
+
+@pytest.mark.parametrize("max_norm", [0.5, 1e6])
+def test_adam_clipped_matches_oracle_bitwise(cuda, oracle, max_norm):
+    from magma_b200 import ops
+
+    n = 100_003
+    rng = np.random.default_rng(5)
+    p = rng.standard_normal(n).astype(np.float32)
+    m = np.zeros(n, np.float32)
+    v = np.zeros(n, np.float32)
+    tp, tm, tv = t(p), t(m), t(v)
+    shadow = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    for step in range(1, 4):
+        g = rng.standard_normal(n).astype(np.float32)
+        norm = ops.grad_norm(t(g), grad_scale=0.5)
+        ops.adam_step_clipped(tp, t(g), tm, tv, step=step, lr=1e-3, grad_norm=norm,
+                              max_norm=max_norm, weight_decay=0.1, grad_scale=0.5,
+                              shadow_bf16=shadow)
+        # the oracle update given the same norm value: identical F32 op sequence
+        oracle.adam_clipped(p, g, m, v, lr=1e-3, norm=norm.item(), max_norm=max_norm,
+                            weight_decay=0.1, step=step, grad_scale=0.5)
+    assert np.array_equal(tp.cpu().numpy(), p)
+    assert np.array_equal(tm.cpu().numpy(), m)
+    assert np.array_equal(tv.cpu().numpy(), v)
+    assert torch.equal(shadow, tp.to(torch.bfloat16))
+
+
 def test_adam_closed_form(cuda):
     from magma_b200 import ops
 

@@ -237,3 +237,42 @@ def test_mlp_gradients_finite_differences(oracle):
         num = (oracle.mlp_fwd_bwd(pp, x, y, inp, hid, out)[0]
                - oracle.mlp_fwd_bwd(pm, x, y, inp, hid, out)[0]) / (2 * h)
         assert abs(num - g[i]) < 2e-3, (i, num, g[i])
+
+
+# ------------------------------------------------- clipping and LR schedule
+@pytest.mark.parametrize("key", ["warmup_cosine_short", "warmup_cosine_long"])
+def test_lr_warmup_cosine_known_answers(oracle, key):
+    g = GOLD[key]
+    for step, want in g["lr_at_step"].items():
+        got = oracle.lr_warmup_cosine(g["base_lr"], g["min_lr"], g["warmup"], g["total"], int(step))
+        assert abs(got - want) < g["tol"], (key, step, got, want)
+    if "midpoint" in g:
+        mp = g["midpoint"]
+        got = oracle.lr_warmup_cosine(g["base_lr"], g["min_lr"], g["warmup"], g["total"], mp["step"])
+        assert abs(got - mp["lr"]) < mp["tol"]
+
+
+def test_grad_norm_and_clip_closed_form(oracle):
+    # clipGradNorm (Optimizer.swift:1229-1267) on g = [3, 4]: norm 5, and with
+    # maxNorm 1 the clipped gradient is g / (5 + 1e-6); a norm below maxNorm
+    # leaves g as it is.
+    g = np.array([3.0, 4.0], np.float32)
+    assert oracle.grad_norm(g) == 5.0
+    assert oracle.grad_norm(g, grad_scale=0.5) == 2.5
+    rng = np.random.default_rng(3)
+    big = rng.standard_normal(100_003).astype(np.float32)
+    want = math.sqrt(float(np.sum(np.float64(big * np.float32(0.25)) ** 2)))
+    assert abs(oracle.grad_norm(big, grad_scale=0.25) - want) < 1e-6 * want
+    # the first Adam step moves p by lr*sign(g) whatever the clip coefficient,
+    # so check m instead: m = g_clipped * (1 - b1), (1 - b1) formed in F32
+    p = np.zeros(2, np.float32)
+    m = np.zeros(2, np.float32)
+    v = np.zeros(2, np.float32)
+    oracle.adam_clipped(p, g, m, v, lr=0.1, norm=5.0, max_norm=1.0)
+    c = np.float32(1.0) / (np.float32(5.0) + np.float32(1e-6))
+    omb1 = np.float32(1.0) - np.float32(0.9)
+    assert np.array_equal(m, (g * c) * omb1)
+    m2 = np.zeros(2, np.float32)
+    oracle.adam_clipped(np.zeros(2, np.float32), g, m2, np.zeros(2, np.float32), lr=0.1, norm=5.0,
+                        max_norm=10.0)
+    assert np.array_equal(m2, g * omb1)

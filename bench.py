@@ -215,6 +215,8 @@ def classify(name, args, cfg, tr):
     if name == "magma_adam_step_clipped":
         n = args[5]
         return "adam", n * (28 + (2 if args[4] else 0))
+    if name == "magma_embedding_bwd_deterministic":
+        return "other", 0.0
     if name == "magma_grad_norm":
         return "adam", args[1] * 4.0  # one read of the gradient arena
     if name == "magma_adam_step":

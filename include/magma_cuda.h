@@ -327,6 +327,24 @@ MAGMA_API magma_status_t magma_embedding_bwd(const int32_t* tokens, const float*
                                    int64_t batch, int64_t seq, int64_t dim, int64_t vocab,
                                    void* stream);
 
+/* The same VJP with a fixed summation order: each token row of dwte gets the
+ * rows that hold that token added one at a time in increasing row order, so
+ * the result is identical on every run (the one-hot matmul of
+ * Data.swift:890-907 reduces in an order the compiler picks; this order is the
+ * plain sequential one). The rows are put in (token, row) order (1024-row
+ * chunks sorted in shared memory, then ranked across chunks), and one warp per
+ * token adds the token's rows. workspace:
+ * magma_embedding_bwd_workspace_size(batch, seq) bytes of device memory (12
+ * bytes per row, rows rounded up to a multiple of 1024), 16-byte aligned.
+ * vocab must be below 4194303. */
+MAGMA_API int64_t magma_embedding_bwd_workspace_size(int64_t batch, int64_t seq);
+MAGMA_API magma_status_t magma_embedding_bwd_deterministic(const int32_t* tokens,
+                                                           const float* dout, float* dwte,
+                                                           float* dwpe, int64_t batch,
+                                                           int64_t seq, int64_t dim, int64_t vocab,
+                                                           void* workspace,
+                                                           int64_t workspace_bytes, void* stream);
+
 /* Softmax cross-entropy with class-index targets, forward and backward in one
  * pass (main.swift:412-433, Loss.swift:627-699): for each row r of logits
  * [rows, classes] (leading dimension ld), losses[r] = logsumexp(row) -

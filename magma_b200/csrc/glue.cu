@@ -58,6 +58,145 @@ __global__ void embedding_bwd_tok_kernel(const int32_t* __restrict__ tokens,
   }
 }
 
+// Deterministic scatter-add: the rows are put in (token, row) order, then one
+// warp per token adds that token's rows to dwte[token] in increasing row
+// order, so every token row gets its rows added one at a time in row order,
+// on every run, as a sequential loop would.
+//  1. emb_sort_chunks: one CTA per chunk of kEmbChunk rows sorts the keys
+//     token * kEmbChunk + local row in shared memory (bitonic network).
+//  2. emb_merge_rank: an element's place in the global order is its index in
+//     its chunk plus, for every other chunk, the number of that chunk's keys
+//     that come before it (token below, or equal token in an earlier chunk):
+//     binary searches over the chunks, staged in shared memory.
+//  3. emb_run_sum: one warp per run of equal tokens in the global order.
+constexpr int kEmbChunk = 1024;
+constexpr int kEmbRowBits = 10;  // log2(kEmbChunk)
+constexpr uint32_t kEmbNoKey = 0xFFFFFFFFu;
+constexpr int kEmbMaxVec = 8;    // column groups per lane held in registers
+constexpr int kEmbSmemChunks = 32;  // chunks staged in shared memory by emb_merge_rank
+
+__global__ void __launch_bounds__(kEmbChunk / 2)
+emb_sort_chunks(const int32_t* __restrict__ tokens, int64_t rows, int64_t vocab,
+                uint32_t* __restrict__ keys_out, uint32_t* __restrict__ tok_sorted, int* err) {
+  __shared__ uint32_t k[kEmbChunk];
+  const int64_t r0 = (int64_t)blockIdx.x * kEmbChunk;
+  for (int i = threadIdx.x; i < kEmbChunk; i += blockDim.x) {
+    uint32_t key = kEmbNoKey;
+    if (r0 + i < rows) {
+      const int32_t t = tokens[r0 + i];
+      if (t < 0 || t >= vocab) set_device_error(err, kDevErrBadIndex);
+      else key = ((uint32_t)t << kEmbRowBits) | (uint32_t)i;
+    }
+    k[i] = key;
+    tok_sorted[r0 + i] = kEmbNoKey;  // places no valid row takes stay empty
+  }
+  __syncthreads();
+  for (int size = 2; size <= kEmbChunk; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const int i = threadIdx.x;  // one compare-exchange per thread
+      const int lo = 2 * stride * (i / stride) + (i % stride);
+      const int hi = lo + stride;
+      const bool up = (lo & size) == 0;
+      const uint32_t a = k[lo], b = k[hi];
+      if ((a > b) == up) {
+        k[lo] = b;
+        k[hi] = a;
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < kEmbChunk; i += blockDim.x) keys_out[r0 + i] = k[i];
+}
+
+// Number of keys of a sorted chunk below x.
+__device__ __forceinline__ int emb_count_below(const uint32_t* a, uint32_t x) {
+  int lo = 0, hi = kEmbChunk;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a[mid] < x) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(256)
+emb_merge_rank(const uint32_t* __restrict__ keys, int nchunks, uint32_t* __restrict__ tok_sorted,
+               uint32_t* __restrict__ row_sorted) {
+  extern __shared__ uint32_t sk[];
+  const bool staged = nchunks <= kEmbSmemChunks;
+  if (staged) {
+    for (int i = threadIdx.x; i < nchunks * kEmbChunk; i += blockDim.x) sk[i] = keys[i];
+    __syncthreads();
+  }
+  const uint32_t* src = staged ? sk : keys;
+  const int64_t total = (int64_t)nchunks * kEmbChunk;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t key = keys[e];
+    if (key == kEmbNoKey) continue;
+    const uint32_t t = key >> kEmbRowBits;
+    const int c = (int)(e / kEmbChunk), i = (int)(e % kEmbChunk);
+    int64_t pos = i;
+    for (int cc = 0; cc < nchunks; ++cc)
+      if (cc != c)
+        pos += emb_count_below(src + (int64_t)cc * kEmbChunk,
+                               (cc < c ? t + 1 : t) << kEmbRowBits);
+    tok_sorted[pos] = t;
+    row_sorted[pos] = (uint32_t)(c * kEmbChunk) + (key & (kEmbChunk - 1));
+  }
+}
+
+// One warp per run start of the globally ordered tokens; columns in groups of
+// 32 * 4 * kEmbMaxVec (float4 path) or 32 * kEmbMaxVec.
+__global__ void __launch_bounds__(256)
+emb_run_sum(const uint32_t* __restrict__ tok_sorted, const uint32_t* __restrict__ row_sorted,
+            int64_t n, const float* __restrict__ dout, float* __restrict__ dwte, int dim,
+            int vec) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  for (int64_t p = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); p < n;
+       p += (int64_t)gridDim.x * warps) {
+    const uint32_t t = tok_sorted[p];
+    if (t == kEmbNoKey) continue;
+    if (p > 0 && tok_sorted[p - 1] == t) continue;  // not the start of a run
+    float* dst = dwte + (int64_t)t * dim;
+    const int group = (vec ? 4 : 1) * 32 * kEmbMaxVec;
+    for (int c0 = 0; c0 < dim; c0 += group) {
+      float4 acc[kEmbMaxVec];
+#pragma unroll
+      for (int u = 0; u < kEmbMaxVec; ++u) {
+        const int col = vec ? c0 + 4 * (lane + 32 * u) : c0 + lane + 32 * u;
+        acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (vec && col < dim) acc[u] = *reinterpret_cast<const float4*>(dst + col);
+        else if (!vec && col < dim) acc[u].x = dst[col];
+      }
+      for (int64_t j = p; j < n && tok_sorted[j] == t; ++j) {
+        const float* src = dout + (int64_t)row_sorted[j] * dim;
+#pragma unroll
+        for (int u = 0; u < kEmbMaxVec; ++u) {
+          const int col = vec ? c0 + 4 * (lane + 32 * u) : c0 + lane + 32 * u;
+          if (col >= dim) continue;
+          if (vec) {
+            const float4 d = *reinterpret_cast<const float4*>(src + col);
+            acc[u].x = __fadd_rn(acc[u].x, d.x);
+            acc[u].y = __fadd_rn(acc[u].y, d.y);
+            acc[u].z = __fadd_rn(acc[u].z, d.z);
+            acc[u].w = __fadd_rn(acc[u].w, d.w);
+          } else {
+            acc[u].x = __fadd_rn(acc[u].x, src[col]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kEmbMaxVec; ++u) {
+        const int col = vec ? c0 + 4 * (lane + 32 * u) : c0 + lane + 32 * u;
+        if (vec && col < dim) *reinterpret_cast<float4*>(dst + col) = acc[u];
+        else if (!vec && col < dim) dst[col] = acc[u].x;
+      }
+    }
+  }
+}
+
 // dwpe[s, i] += sum_b dout[b*seq + s, i], summed in b order (deterministic).
 __global__ void embedding_bwd_pos_kernel(const float* __restrict__ dout, float* __restrict__ dwpe,
                                          int64_t batch, int64_t seq, int dim) {
@@ -506,6 +645,66 @@ magma_status_t magma_embedding_bwd(const int32_t* tokens, const float* dout, flo
   embedding_bwd_tok_kernel<<<grid_for(rows, 8), 256, 0, s>>>(tokens, dout, dwte, rows, (int)dim,
                                                              vocab, err);
   if (magma_status_t st = check_launch("embedding_bwd_tok")) return st;
+  if (dwpe != nullptr) {
+    embedding_bwd_pos_kernel<<<grid_for(seq * dim, 256), 256, 0, s>>>(dout, dwpe, batch, seq,
+                                                                       (int)dim);
+    if (magma_status_t st = check_launch("embedding_bwd_pos")) return st;
+  }
+  return MAGMA_OK;
+}
+
+int64_t magma_embedding_bwd_workspace_size(int64_t batch, int64_t seq) {
+  const int64_t rows = batch * seq;
+  return rows > 0 ? 12 * ceil_div(rows, kEmbChunk) * kEmbChunk : 0;  // keys, tokens, rows
+}
+
+magma_status_t magma_embedding_bwd_deterministic(const int32_t* tokens, const float* dout,
+                                                 float* dwte, float* dwpe, int64_t batch,
+                                                 int64_t seq, int64_t dim, int64_t vocab,
+                                                 void* workspace, int64_t workspace_bytes,
+                                                 void* stream) {
+  MAGMA_REQUIRE(batch >= 0 && seq > 0 && dim > 0 && vocab > 0 && dim <= INT32_MAX,
+                "magma_embedding_bwd_deterministic: bad shape");
+  MAGMA_REQUIRE(vocab < (int64_t)(kEmbNoKey >> kEmbRowBits),
+                "magma_embedding_bwd_deterministic: vocab %lld above %u", (long long)vocab,
+                kEmbNoKey >> kEmbRowBits);
+  const int64_t rows = batch * seq;
+  if (rows == 0) return MAGMA_OK;
+  MAGMA_REQUIRE(tokens && dout && dwte, "magma_embedding_bwd_deterministic: NULL pointer");
+  const int64_t need = magma_embedding_bwd_workspace_size(batch, seq);
+  MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= need && aligned16(workspace),
+                "magma_embedding_bwd_deterministic: a 16-byte aligned workspace of %lld bytes "
+                "is needed (magma_embedding_bwd_workspace_size)", (long long)need);
+  const int64_t nchunks = ceil_div(rows, kEmbChunk);
+  MAGMA_REQUIRE(nchunks <= INT32_MAX / kEmbChunk, "magma_embedding_bwd_deterministic: too many rows");
+  const int64_t padded = nchunks * kEmbChunk;
+  cudaStream_t s = (cudaStream_t)stream;
+  uint32_t* keys = static_cast<uint32_t*>(workspace);
+  uint32_t* tok_sorted = keys + padded;
+  uint32_t* row_sorted = tok_sorted + padded;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (magma_status_t st = cuda_status(
+            cudaFuncSetAttribute(emb_merge_rank, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kEmbSmemChunks * kEmbChunk * 4),
+            "cudaFuncSetAttribute(emb_merge_rank)"))
+      return st;
+    attr_set[dev] = true;
+  }
+  emb_sort_chunks<<<(unsigned)nchunks, kEmbChunk / 2, 0, s>>>(tokens, rows, vocab, keys,
+                                                               tok_sorted, device_error_word());
+  if (magma_status_t st = check_launch("embedding_bwd_sort")) return st;
+  const size_t smem = nchunks <= kEmbSmemChunks ? (size_t)padded * 4 : 0;
+  int64_t mb = ceil_div(padded, 256);
+  if (mb > 2 * num_sms()) mb = 2 * num_sms();
+  emb_merge_rank<<<(unsigned)mb, 256, smem, s>>>(keys, (int)nchunks, tok_sorted, row_sorted);
+  if (magma_status_t st = check_launch("embedding_bwd_rank")) return st;
+  const int vec = (dim % 4) == 0 && aligned16(dout) && aligned16(dwte);
+  emb_run_sum<<<grid_for(rows, 8), 256, 0, s>>>(tok_sorted, row_sorted, padded, dout, dwte,
+                                                (int)dim, vec);
+  if (magma_status_t st = check_launch("embedding_bwd_runs")) return st;
   if (dwpe != nullptr) {
     embedding_bwd_pos_kernel<<<grid_for(seq * dim, 256), 256, 0, s>>>(dout, dwpe, batch, seq,
                                                                        (int)dim);

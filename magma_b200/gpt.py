@@ -32,6 +32,7 @@ import ctypes as C
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import lib, ops
@@ -134,6 +135,10 @@ class GPTTrainer:
         self.m = torch.zeros(P, **f32)
         self.v = torch.zeros(P, **f32)
         self.t = 0
+        # sort keys of the deterministic embedding backward
+        self.emb_ws = torch.empty(
+            max(lib.query("magma_embedding_bwd_workspace_size", batch, cfg.seq) // 4, 1),
+            dtype=torch.int32, device=self.dev)
         # device scalar of the last global gradient norm, and its scratch
         self.grad_norm = torch.zeros(1, **f32)
         self.norm_ws = torch.empty(max(lib.query("magma_grad_norm_workspace_size", P) // 4, 1),
@@ -396,8 +401,9 @@ class GPTTrainer:
         self.view(G, "wpe").zero_()
         if not cfg.tied:
             self.view(G, "wte").zero_()
-        lib.call("magma_embedding_bwd", _p(self.tokens), _p(self.dresid), _p(self.view(G, "wte")),
-                 _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp, s)
+        lib.call("magma_embedding_bwd_deterministic", _p(self.tokens), _p(self.dresid),
+                 _p(self.view(G, "wte")), _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp,
+                 _p(self.emb_ws), self.emb_ws.numel() * 4, s)
         yield [self._grad_range(0, seg_top), (0, self.table["h0.ln1_w"][0]),
                (self.table["lnf_w"][0], self.P)]
 
@@ -432,6 +438,73 @@ class GPTTrainer:
         lib.call("magma_adam_step_clipped", _p(self.params), _p(self.grads), _p(self.m),
                  _p(self.v), _p(self.shadow), self.P, lr, self.beta1, self.beta2, self.eps,
                  self.wd, self.t, grad_scale, _p(self.grad_norm), self.grad_clip, self._s())
+
+    # --------------------------------------------------------- checkpoints
+    def _model_tensors(self) -> list[tuple[str, tuple[int, ...], int]]:
+        """(name, shape as stored, arena offset) of every parameter: the
+        embedding and lm-head tables without their vocabulary padding rows."""
+        out = []
+        for name, shp in self.cfg.shapes():
+            if name in ("wte", "lm_head"):
+                shp = (self.cfg.vocab,) + tuple(shp[1:])
+            out.append((name, tuple(shp), self.table[name][0]))
+        return out
+
+    def save_checkpoint(self, path) -> None:
+        """Parameters to `path` in the reference's BinaryCheckpoint format
+        (Module.swift:4838-4890); Adam's m, v and step count to `path`.adam in
+        the same format."""
+        from . import checkpoint as ck
+
+        torch.cuda.current_stream(self.dev).synchronize()
+        host = {k: a.cpu().numpy() for k, a in (("p", self.params), ("m", self.m), ("v", self.v))}
+        ents = {k: [] for k in host}
+        for name, shp, off in self._model_tensors():
+            n = math.prod(shp)
+            for k in host:
+                suffix = "" if k == "p" else f".{k}"
+                ents[k].append(ck.Entry(name + suffix, shp, host[k][off:off + n]))
+        ck.save(path, ents["p"])
+        step = ck.Entry("adam.step", (), np.array([float(self.t)], np.float32))
+        ck.save(str(path) + ".adam", ents["m"] + ents["v"], [step])
+
+    def load_checkpoint(self, path, optimizer_state: bool = True) -> None:
+        """Inverse of save_checkpoint. Everything is read and checked (count,
+        order, shapes) before the arenas change; a missing .adam file with
+        optimizer_state=True is an error."""
+        from . import checkpoint as ck
+
+        tensors = self._model_tensors()
+        expected = [(n, s) for n, s, _ in tensors]
+        _, params, bufs = ck.load(path)
+        ck.match(params, expected, "parameter")
+        if bufs:
+            raise ck.CheckpointError(f"the GPT model has no buffers; checkpoint has {len(bufs)}")
+        if optimizer_state:
+            _, mv, extra = ck.load(str(path) + ".adam")
+            ck.match(mv, [(n + ".m", s) for n, s in expected] + [(n + ".v", s) for n, s in expected],
+                     "optimizer tensor")
+            if len(extra) != 1 or extra[0].name != "adam.step" or extra[0].shape != ():
+                raise ck.CheckpointError("optimizer file lacks its adam.step entry")
+        host = {"p": self.params.cpu().numpy().copy()}
+        if optimizer_state:
+            host["m"] = np.zeros(self.P, np.float32)
+            host["v"] = np.zeros(self.P, np.float32)
+        k = len(tensors)
+        for i, (name, shp, off) in enumerate(tensors):
+            n = math.prod(shp)
+            host["p"][off:off + n] = params[i].values
+            if optimizer_state:
+                host["m"][off:off + n] = mv[i].values
+                host["v"][off:off + n] = mv[k + i].values
+        self.params.copy_(torch.from_numpy(host["p"]))
+        if optimizer_state:
+            self.m.copy_(torch.from_numpy(host["m"]))
+            self.v.copy_(torch.from_numpy(host["v"]))
+            self.t = int(extra[0].values[0])
+        if self.shadow is not None:
+            self._sync_shadow()
+        torch.cuda.current_stream(self.dev).synchronize()
 
     # ------------------------------------------------------------- graphs
     def capture(self) -> None:

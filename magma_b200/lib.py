@@ -113,6 +113,9 @@ SIGNATURES = {
     "magma_lr_warmup_cosine": (None, [_f, _f, _i64, _i64, _i64, C.POINTER(_f)]),
     "magma_embedding_fwd": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "magma_embedding_bwd": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "magma_embedding_bwd_workspace_size": (_i64, [_i64, _i64]),
+    "magma_embedding_bwd_deterministic": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp,
+                                                 _i64, _vp]),
     "magma_cross_entropy_fwd_bwd": (None, [_vp, _vp, _vp, _i64, _i64, _i64, _f, _i32, _vp]),
     "magma_cross_entropy_fwd_bwd_rowstats": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f,
                                                     _i32, _vp]),
@@ -135,6 +138,7 @@ KERNELS_PER_CALL = {
     "magma_attention_fwd": 1, "magma_attention_bwd": 3, "magma_adam_step": 1,
     "magma_adam_step_multi": 1, "magma_embedding_fwd": 1, "magma_embedding_bwd": 2,
     "magma_grad_norm": 2, "magma_adam_step_clipped": 1, "magma_lr_warmup_cosine": 0,
+    "magma_embedding_bwd_deterministic": 4,
     "magma_cross_entropy_fwd_bwd": 1,
     "magma_cross_entropy_fwd_bwd_rowstats": 1, "magma_reduce_sum": 1, "magma_gelu_fwd": 1,
     "magma_gelu_bwd": 1, "magma_relu_fwd": 1, "magma_relu_bwd": 1, "magma_bias_grad": 2,

@@ -295,6 +295,20 @@ def embedding_bwd(tokens: torch.Tensor, dout: torch.Tensor, dwte: torch.Tensor,
              dwte.shape[1], dwte.shape[0], _stream())
 
 
+def embedding_bwd_deterministic(tokens: torch.Tensor, dout: torch.Tensor, dwte: torch.Tensor,
+                                dwpe: torch.Tensor | None,
+                                workspace: torch.Tensor | None = None) -> None:
+    """The scatter-add VJP with rows added to each token row in row order
+    (identical on every run), accumulating."""
+    B, S = tokens.shape
+    need = lib.query("magma_embedding_bwd_workspace_size", B, S)
+    ws = workspace if workspace is not None else torch.empty(
+        max(need // 4, 1), dtype=torch.int32, device=dwte.device)
+    lib.call("magma_embedding_bwd_deterministic", _ptr(tokens), _ptr(dout), _ptr(dwte),
+             _ptr(dwpe), B, S, dwte.shape[1], dwte.shape[0], _ptr(ws),
+             ws.numel() * ws.element_size(), _stream())
+
+
 def cross_entropy_fwd_bwd(logits: torch.Tensor, targets: torch.Tensor, classes: int | None = None,
                           grad_scale: float | None = None, losses: torch.Tensor | None = None):
     """Softmax CE (main.swift:412-433): per-row losses; logits become dlogits in place."""

@@ -86,6 +86,30 @@ def test_gpt_f32_clip_and_schedule_match_oracle(cuda, oracle):
     assert relnorm(tr.params.cpu().numpy(), params) < 1e-4
 
 
+def test_gpt_checkpoint_round_trip(cuda, oracle, tmp_path):
+    """save_checkpoint / load_checkpoint: a second trainer that loads the
+    files continues exactly as the first (same loss, same parameters)."""
+    from magma_b200.gpt import GPTConfig, GPTTrainer
+
+    kw = dict(vocab=300, seq=128, layers=2, heads=2, dim=128, tied=True)
+    a, _, tok, tgt = make(oracle, kw, 2, "bf16")
+    for _ in range(2):
+        a.step_fwd_bwd()
+        a.optimizer_step()
+    a.save_checkpoint(tmp_path / "gpt.bin")
+    b = GPTTrainer(GPTConfig(**kw), 2, "bf16", lr=1e-3, seed=5)
+    b.set_batch(torch.tensor(tok), torch.tensor(tgt))
+    b.load_checkpoint(tmp_path / "gpt.bin")
+    assert b.t == a.t == 2
+    for x, y in ((a.params, b.params), (a.m, b.m), (a.v, b.v), (a.shadow, b.shadow)):
+        assert torch.equal(x, y)
+    for tr in (a, b):
+        tr.step_fwd_bwd()
+        tr.optimizer_step()
+    assert a.loss.item() == b.loss.item()
+    assert torch.equal(a.params, b.params)
+
+
 def test_gpt_bf16_close_to_oracle(cuda, oracle):
     kw = dict(vocab=300, seq=128, layers=2, heads=2, dim=128, tied=True)
     tr, ocfg, tok, tgt = make(oracle, kw, 2, "bf16")

@@ -569,6 +569,39 @@ def test_embedding_fwd_bwd(cuda):
     close(dwpe.cpu(), dout.reshape(B, S, D).sum(0), 1e-5)
 
 
+@pytest.mark.parametrize("B,S,D,V,dist", [(4, 16, 32, 50, "uniform"), (8, 1024, 768, 50257, "uniform"),
+                                           (3, 7000, 36, 300, "skewed"), (2, 9000, 16, 5, "uniform"),
+                                           (1, 5, 13, 7, "one")])
+def test_embedding_bwd_deterministic_is_sequential_sum(cuda, B, S, D, V, dist):
+    """Each token row gets its rows added one at a time in row order: the same
+    F32 result as a sequential loop, bit for bit, over several 16384-row chunks,
+    heavy repeats (a 5-token vocabulary; one token everywhere), odd dims."""
+    from magma_b200 import ops
+
+    rng = np.random.default_rng(B * S + D)
+    if dist == "skewed":  # a Zipf-like mix: a few tokens in most rows
+        tok = np.minimum(rng.zipf(1.3, (B, S)) - 1, V - 1).astype(np.int32)
+    elif dist == "one":
+        tok = np.full((B, S), 3, np.int32)
+    else:
+        tok = rng.integers(0, V, (B, S)).astype(np.int32)
+    dout = rng.standard_normal((B * S, D)).astype(np.float32)
+    init = rng.standard_normal((V, D)).astype(np.float32)  # the VJP accumulates
+    want = init.copy()
+    flat = tok.reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    for r in order:  # rows grouped by token, increasing row order inside a group
+        want[flat[r]] += dout[r]
+    dwte = t(init)
+    dwpe = torch.zeros((S, D), device="cuda")
+    ops.embedding_bwd_deterministic(t(tok, torch.int32), t(dout), dwte, dwpe)
+    assert np.array_equal(dwte.cpu().numpy(), want)
+    close(dwpe.cpu(), dout.reshape(B, S, D).sum(0), 1e-5)
+    again = t(init)
+    ops.embedding_bwd_deterministic(t(tok, torch.int32), t(dout), again, None)
+    assert torch.equal(again, dwte)
+
+
 def test_bad_token_sets_device_error(cuda):
     from magma_b200 import ops, lib
 

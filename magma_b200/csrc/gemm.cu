@@ -610,12 +610,26 @@ __device__ __forceinline__ void epi_rows8(const TcArgs& a, const float* __restri
 #pragma unroll
       for (int i = 0; i < 8; ++i) pre[i] = hb ? __fadd_rn(v[i], b[i]) : v[i];
       store8(static_cast<TC*>(a.e.aux_out) + off, pre);
+      if constexpr (EPI == MAGMA_EPI_BIAS_GELU && std::is_same<TC, __nv_bfloat16>::value) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        o[i] = EPI == MAGMA_EPI_BIAS_GELU ? gelu_t<TC>(pre[i]) : fmaxf(pre[i], 0.f);
+        for (int i = 0; i < 8; i += 2) gelu_pair_fast(o[i], o[i + 1], pre[i], pre[i + 1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          o[i] = EPI == MAGMA_EPI_BIAS_GELU ? gelu_t<TC>(pre[i]) : fmaxf(pre[i], 0.f);
+      }
     } else if constexpr (EPI == MAGMA_EPI_DGELU) {
+      if constexpr (std::is_same<TC, __nv_bfloat16>::value) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[i], gelu_grad_t<TC>(x[i]));
+        for (int i = 0; i < 8; i += 2) {
+          float g0, g1;
+          gelu_grad_pair_fast(g0, g1, x[i], x[i + 1]);
+          f2_unpack(f2_mul(f2_pack(v[i], v[i + 1]), f2_pack(g0, g1)), o[i], o[i + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(v[i], gelu_grad_t<TC>(x[i]));
+      }
     } else if constexpr (EPI == MAGMA_EPI_DRELU) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = x[i] > 0.f ? v[i] : 0.f;

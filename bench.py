@@ -233,6 +233,22 @@ def classify(name, args, cfg, tr):
 
 
 # ------------------------------------------------------------------- CPU baseline
+# The reference GPT trainer's optimiser settings (TrainConfig.shakespeare,
+# main.swift:76-91), used by the GPU step and by the timed CPU steps alike.
+OPT = dict(lr=6e-4, min_lr=6e-5, warmup=100, total=5000, beta1=0.9, beta2=0.99, wd=0.1, clip=1.0)
+
+
+def oracle_step(oracle, cfg, params, m, v, tok, tgt, step: int) -> None:
+    """One training step of the oracle: forward + backward, the global gradient
+    norm, the warmup-cosine learning rate and Adam on the clipped gradient (the
+    GPU step's sequence, main.swift:829-882)."""
+    _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tgt)
+    norm = oracle.grad_norm(g)
+    lr = oracle.lr_warmup_cosine(OPT["lr"], OPT["min_lr"], OPT["warmup"], OPT["total"], step - 1)
+    oracle.adam_clipped(params, g, m, v, lr=lr, norm=norm, max_norm=OPT["clip"],
+                        beta1=OPT["beta1"], beta2=OPT["beta2"], weight_decay=OPT["wd"], step=step)
+
+
 def cpu_baseline(budget_s: float = 20.0) -> dict:
     """Oracle GPT-2-small fwd+bwd+Adam on a bounded sample, all host threads."""
     import numpy as np
@@ -253,14 +269,13 @@ def cpu_baseline(budget_s: float = 20.0) -> dict:
     tgt = rng.integers(0, 50257, (1, seq)).astype(np.int32)
     steps, t0 = 0, time.perf_counter()
     while True:
-        _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tgt)
-        oracle.adam(params, g, m, v, lr=3e-4, step=steps + 1)
+        oracle_step(oracle, cfg, params, m, v, tok, tgt, steps + 1)
         steps += 1
         el = time.perf_counter() - t0
         if el > budget_s or steps >= 3:
             break
     return {"value": steps * seq / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{steps} step(s) of GPT-2 small (124M, 12 layers) F32 fwd+bwd+Adam on 1 x "
+            "sample": f"{steps} step(s) of GPT-2 small (124M, 12 layers) F32 fwd+bwd+clip+Adam on 1 x "
                       f"{seq} tokens (positions < {seq}), oracle/ C restatement, OpenMP "
                       f"{threads} threads, {el:.1f} s"}
 
@@ -290,8 +305,7 @@ def run_reference(args) -> None:
     cfg, params, m, v = make(seq)
     tok = rng.integers(0, 50257, (1, seq)).astype(np.int32)
     t0 = time.perf_counter()
-    _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tok)
-    oracle.adam(params, g, m, v, lr=3e-4, step=1)
+    oracle_step(oracle, cfg, params, m, v, tok, tok, 1)
     first = time.perf_counter() - t0
     total = args.steps + args.warmup
     # shrink the per-step sample so the whole run stays within ~3 minutes
@@ -302,12 +316,10 @@ def run_reference(args) -> None:
     tok = rng.integers(0, 50257, (1, seq)).astype(np.int32)
     tgt = rng.integers(0, 50257, (1, seq)).astype(np.int32)
     for i in range(args.warmup):
-        _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tgt)
-        oracle.adam(params, g, m, v, lr=3e-4, step=i + 1)
+        oracle_step(oracle, cfg, params, m, v, tok, tgt, i + 1)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        _, g = oracle.gpt_fwd_bwd(cfg, params, tok, tgt)
-        oracle.adam(params, g, m, v, lr=3e-4, step=args.warmup + i + 1)
+        oracle_step(oracle, cfg, params, m, v, tok, tgt, args.warmup + i + 1)
     el = time.perf_counter() - t0
     value = args.steps * seq / el
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -315,7 +327,7 @@ def run_reference(args) -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": workload_config(world, args.batch),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"per step: GPT-2 small F32 fwd+bwd+Adam on 1 x {seq} "
+                             "sample": f"per step: GPT-2 small F32 fwd+bwd+clip+Adam on 1 x {seq} "
                                        "tokens (the oracle/ C restatement of the reference's "
                                        "op sequence; the Swift/XLA reference cannot be built "
                                        "here)"},
@@ -353,8 +365,9 @@ def main() -> None:
     # the reference GPT trainer's optimiser settings (TrainConfig.shakespeare,
     # main.swift:76-91): AdamW-style decay, global-norm clipping at 1.0 and a
     # warmup-cosine schedule, all inside the timed step
-    tr = GPTTrainer(cfg, B, "bf16", lr=6e-4, beta1=0.9, beta2=0.99, weight_decay=0.1, seed=0,
-                    grad_clip=1.0, lr_schedule=(100, 5000, 6e-5))
+    tr = GPTTrainer(cfg, B, "bf16", lr=OPT["lr"], beta1=OPT["beta1"], beta2=OPT["beta2"],
+                    weight_decay=OPT["wd"], seed=0, grad_clip=OPT["clip"],
+                    lr_schedule=(OPT["warmup"], OPT["total"], OPT["min_lr"]))
     sync = dp.GradSync()
     gen = torch.Generator().manual_seed(1234 + rank)
     tok_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()

@@ -165,9 +165,14 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (a.S + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
-  const int qt0 = 2 * (n_pairs - 1 - (int)blockIdx.x);
+  // Blocks are dispatched in linear index order; the pair index varies
+  // slowest so that every head's heaviest pair (most key tiles under causal)
+  // starts first and the lightest ones fill the tail.
+  const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+  const int heads = (int)(gridDim.y * gridDim.z);
+  const int qt0 = 2 * (n_pairs - 1 - lin / heads);
   const bool has1 = qt0 + 1 < n_qt;
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int h = (lin % heads) % (int)gridDim.y, b = (lin % heads) / (int)gridDim.y;
   // key tiles visited by query tile t
   const int nk0 = a.causal ? qt0 + 1 : n_qt;
   const int nk1 = has1 ? (a.causal ? qt0 + 2 : n_qt) : 0;
@@ -479,8 +484,13 @@ attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_t = (a.S + kTile - 1) / kTile;
-  const int kt = (int)blockIdx.x;  // tile 0 has the most query tiles under causal
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Linear dispatch order with the key tile varying slowest: key tile 0 has
+  // the most query tiles under causal, so the heaviest blocks start first and
+  // the lightest fill the tail.
+  const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+  const int heads = (int)(gridDim.y * gridDim.z);
+  const int kt = lin / heads;
+  const int h = (lin % heads) % (int)gridDim.y, b = (lin % heads) / (int)gridDim.y;
   const int k0 = kt * kTile;
   const int first_q = a.causal ? kt : 0;
   const int n_it = n_t - first_q;
@@ -926,8 +936,13 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_t = (a.S + kTile - 1) / kTile;
-  const int kt = (int)blockIdx.x;  // tile 0 has the most query tiles under causal
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Linear dispatch order with the key tile varying slowest: key tile 0 has
+  // the most query tiles under causal, so the heaviest blocks start first and
+  // the lightest fill the tail.
+  const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+  const int heads = (int)(gridDim.y * gridDim.z);
+  const int kt = lin / heads;
+  const int h = (lin % heads) % (int)gridDim.y, b = (lin % heads) / (int)gridDim.y;
   const int k0 = kt * kTile;
   const int first_q = a.causal ? kt : 0;
   const int n_it = n_t - first_q;

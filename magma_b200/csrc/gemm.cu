@@ -813,6 +813,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                    (warp - 2) * Cfg::kStageWarpFloats;
     const bool vec2 = args.vec_ok != 0;
     const bool epi_vec8 = args.epi_vec8 != 0;
+    const bool vec8_staged =
+        epi_vec8 && (std::is_same<TC, __nv_bfloat16>::value ||
+                     args.e.epi == MAGMA_EPI_BIAS_RESIDUAL || args.e.epi == MAGMA_EPI_ACCUMULATE);
+    // the tile's bias columns of this warp, staged after the 32 x 36 chunk stage
+    float* bias_s = stage + 32 * Cfg::kStagePitch;
     const bool ws_vec8 = (N % 8) == 0;
     const bool c_vec8 = args.vec8_ok != 0;
     const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
@@ -852,6 +857,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int j = 0; j < kCols / 32; ++j) {
         const int64_t col = (int64_t)n0 + 32 * j + lane;
         bl[j] = (tma_direct && has_bias && args.splits == 1 && col < N) ? args.e.bias[col] : 0.f;
+      }
+      if (vec8_staged && has_bias && !direct) {
+        // this warp's kCols bias values, read once per tile while the
+        // accumulator is still being computed (columns past N read as 0)
+        for (int c = 4 * lane; c < kCols; c += 128) {
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if ((int64_t)n0 + c + 4 <= N) {
+            v = *reinterpret_cast<const float4*>(args.e.bias + n0 + c);
+          } else {
+            if ((int64_t)n0 + c < N) v.x = args.e.bias[n0 + c];
+            if ((int64_t)n0 + c + 1 < N) v.y = args.e.bias[n0 + c + 1];
+            if ((int64_t)n0 + c + 2 < N) v.z = args.e.bias[n0 + c + 2];
+          }
+          *reinterpret_cast<float4*>(bias_s + c) = v;
+        }
+        __syncwarp();
       }
       if (aux_pf != nullptr) {
         // While the accumulator is still being computed, pull this warp's
@@ -967,15 +988,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 make_float4(__uint_as_float(ra[4 * j]), __uint_as_float(ra[4 * j + 1]),
                             __uint_as_float(ra[4 * j + 2]), __uint_as_float(ra[4 * j + 3]));
           __syncwarp();
-          if (std::is_same<TC, __nv_bfloat16>::value && epi_vec8) {
+          if (vec8_staged) {
             const int r8 = lane >> 2, g8 = lane & 3;
             const int64_t col8 = (int64_t)n0 + c0 + 8 * g8;
             if (col8 < N && rows_here > 0) {
               const float* st8 = stage + r8 * P + 8 * g8;
               if (col8 + 8 <= N) {
                 float b8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                if (has_bias) load8(args.e.bias + col8, b8);
-                switch (args.e.epi) {
+                if (has_bias) {  // staged in shared memory at the start of the tile
+                  const float4 lo = *reinterpret_cast<const float4*>(bias_s + c0 + 8 * g8);
+                  const float4 hi = *reinterpret_cast<const float4*>(bias_s + c0 + 8 * g8 + 4);
+                  b8[0] = lo.x; b8[1] = lo.y; b8[2] = lo.z; b8[3] = lo.w;
+                  b8[4] = hi.x; b8[5] = hi.y; b8[6] = hi.z; b8[7] = hi.w;
+                }
+                if constexpr (std::is_same<TC, float>::value) {
+                  // F32 outputs take this path only for the transcendental-free epilogues
+                  if (args.e.epi == MAGMA_EPI_BIAS_RESIDUAL)
+                    epi_rows8<TC, MAGMA_EPI_BIAS_RESIDUAL, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8);
+                  else
+                    epi_rows8<TC, MAGMA_EPI_ACCUMULATE, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8);
+                } else switch (args.e.epi) {
                   case MAGMA_EPI_BIAS_GELU: epi_rows8<TC, MAGMA_EPI_BIAS_GELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
                   case MAGMA_EPI_BIAS_RESIDUAL: epi_rows8<TC, MAGMA_EPI_BIAS_RESIDUAL, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
                   case MAGMA_EPI_DGELU: epi_rows8<TC, MAGMA_EPI_DGELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;

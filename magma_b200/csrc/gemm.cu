@@ -557,6 +557,20 @@ __device__ __forceinline__ void epi_rows(const TcArgs& a, const float* __restric
   }
 }
 
+// Asynchronous 16-byte global -> shared copies (the LSU path, completion by
+// commit groups); valid = false writes 16 zero bytes without reading.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // Staged epilogue, 8 columns per lane: for one 32-column chunk staged as
 // [32 rows][P] floats, lane (r8 = lane / 4, g = lane % 4) handles columns
 // [col, col + 8) of rows r8, r8 + 8, r8 + 16, r8 + 24: 16-byte shared reads,
@@ -566,7 +580,7 @@ __device__ __forceinline__ void epi_rows(const TcArgs& a, const float* __restric
 template <typename TC, int EPI, int P>
 __device__ __forceinline__ void epi_rows8(const TcArgs& a, const float* __restrict__ st,
                                           int64_t row0, int rows_here, int r8, int64_t col,
-                                          const float (&b)[8]) {
+                                          const float (&b)[8], const uint4* pre = nullptr) {
   constexpr bool kAux = EPI == MAGMA_EPI_BIAS_RESIDUAL || EPI == MAGMA_EPI_DGELU ||
                         EPI == MAGMA_EPI_DRELU || EPI == MAGMA_EPI_ACCUMULATE;
   // auxiliary operand element type: the F32 residual stream, else C's type
@@ -583,7 +597,19 @@ __device__ __forceinline__ void epi_rows8(const TcArgs& a, const float* __restri
   for (int it = 0; it < 4; ++it) {
     const int r = it * 8 + r8;
     if (r >= rows_here) break;
-    if constexpr (kAux) {
+    if constexpr (kAux && kWords == 1) {
+      if (pre != nullptr) {  // BF16 auxiliary rows already staged in shared memory
+        raw[it][0] = pre[it];
+      } else if ((it & 1) == 0) {  // two rows' loads in flight at a time
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (r + 8 * k < rows_here) {
+            const uint4* q = reinterpret_cast<const uint4*>(src + (row0 + r + 8 * k) * ldc + col);
+            raw[it + k][0] = q[0];
+          }
+        }
+      }
+    } else if constexpr (kAux) {
       if ((it & 1) == 0) {  // two rows' loads in flight at a time
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
@@ -818,6 +844,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                      args.e.epi == MAGMA_EPI_BIAS_RESIDUAL || args.e.epi == MAGMA_EPI_ACCUMULATE);
     // the tile's bias columns of this warp, staged after the 32 x 36 chunk stage
     float* bias_s = stage + 32 * Cfg::kStagePitch;
+    // BF16 activation-VJP epilogues: the next 32-column chunk of the auxiliary
+    // operand (32 rows x 64 bytes) is copied into shared memory by cp.async
+    // while the current one is computed (the first chunk of a tile while the
+    // accumulator is)
+    const bool aux_smem = vec8_staged && std::is_same<TC, __nv_bfloat16>::value &&
+                          (args.e.epi == MAGMA_EPI_DGELU || args.e.epi == MAGMA_EPI_DRELU);
+    uint8_t* aux_s = reinterpret_cast<uint8_t*>(bias_s + 128);
+    auto issue_aux = [&](int m0_, int n0_, int c0_) {
+      const int r8 = lane >> 2, g8 = lane & 3;
+      const __nv_bfloat16* auxp = static_cast<const __nv_bfloat16*>(args.e.aux_in);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = r8 + 8 * k;
+        const int64_t row = (int64_t)m0_ + q * 32 + r;
+        const int64_t col = (int64_t)n0_ + c0_ + 8 * g8;
+        const bool valid = row < M && col + 8 <= N;
+        cp_async16(sm100::smem_u32(aux_s + r * 64 + g8 * 16),
+                   valid ? static_cast<const void*>(auxp + row * args.e.ldc + col)
+                         : static_cast<const void*>(auxp),
+                   valid);
+      }
+      cp_async_commit();
+    };
     const bool ws_vec8 = (N % 8) == 0;
     const bool c_vec8 = args.vec8_ok != 0;
     const bool direct = args.splits > 1 || args.e.epi == MAGMA_EPI_NONE ||
@@ -858,6 +907,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int64_t col = (int64_t)n0 + 32 * j + lane;
         bl[j] = (tma_direct && has_bias && args.splits == 1 && col < N) ? args.e.bias[col] : 0.f;
       }
+      if (aux_smem) issue_aux(m0, n0, 0);  // the tile's first chunk
       if (vec8_staged && has_bias && !direct) {
         // this warp's kCols bias values, read once per tile while the
         // accumulator is still being computed (columns past N read as 0)
@@ -990,6 +1040,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           __syncwarp();
           if (vec8_staged) {
             const int r8 = lane >> 2, g8 = lane & 3;
+            uint4 pre[4];
+            if (aux_smem) {  // the whole warp: this chunk's auxiliary rows, then the next copy
+              cp_async_wait_all();
+              __syncwarp();
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                pre[k] = *reinterpret_cast<const uint4*>(aux_s + (r8 + 8 * k) * 64 + g8 * 16);
+              __syncwarp();
+              if (c0 + 32 < kCols) issue_aux(m0, n0, c0 + 32);
+            }
             const int64_t col8 = (int64_t)n0 + c0 + 8 * g8;
             if (col8 < N && rows_here > 0) {
               const float* st8 = stage + r8 * P + 8 * g8;
@@ -1010,10 +1070,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 } else switch (args.e.epi) {
                   case MAGMA_EPI_BIAS_GELU: epi_rows8<TC, MAGMA_EPI_BIAS_GELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
                   case MAGMA_EPI_BIAS_RESIDUAL: epi_rows8<TC, MAGMA_EPI_BIAS_RESIDUAL, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
-                  case MAGMA_EPI_DGELU: epi_rows8<TC, MAGMA_EPI_DGELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                  case MAGMA_EPI_DGELU: epi_rows8<TC, MAGMA_EPI_DGELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8, aux_smem ? pre : nullptr); break;
                   case MAGMA_EPI_ACCUMULATE: epi_rows8<TC, MAGMA_EPI_ACCUMULATE, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
                   case MAGMA_EPI_BIAS_RELU: epi_rows8<TC, MAGMA_EPI_BIAS_RELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
-                  default: epi_rows8<TC, MAGMA_EPI_DRELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8); break;
+                  default: epi_rows8<TC, MAGMA_EPI_DRELU, P>(args, st8 - r8 * P, row0, rows_here, r8, col8, b8, aux_smem ? pre : nullptr); break;
                 }
               } else {  // ragged last columns, element by element
                 TC* C = static_cast<TC*>(args.C);
@@ -1060,6 +1120,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     // the TMA stores must finish before the shared memory they read goes away
     if (tma_direct && lane == 0) sm100::bulk_wait_group_all();
+    if (aux_smem) cp_async_wait_all();  // no copy into shared memory outlives the CTA
     __syncwarp();
   }
   sm100::tc_fence_before();

@@ -8,23 +8,31 @@
 // majorness here (no transpose kernels), and the bias add / activation /
 // residual add / activation VJP that follow the dot are fused into the store.
 //
-// BF16 path: a persistent, warp-specialised tcgen05 kernel.
-//   warp 0      TMA producer: 128x64 A and BNx64 B tiles, 128-byte swizzle,
-//               into a STAGES-deep shared-memory ring (full/empty mbarriers);
+// BF16 path: a persistent, warp-specialised tcgen05 kernel (320 threads).
+//   warp 0      TMA producer: A and B tiles of 64 K-elements, 128-byte swizzle,
+//               into an up-to-8-stage shared-memory ring (full/empty mbarriers);
 //   warp 1      TMEM allocator and MMA issuer: one thread issues
-//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) into one
-//               of two TMEM accumulators (2 x BN columns) and commits;
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = row), fused
-//               epilogue math, 16-byte global stores; the accumulator is handed
-//               back to the MMA warp so the next tile's MMAs overlap this store.
+//               tcgen05.mma.kind::f16 (K = 16) into one of two TMEM
+//               accumulators and commits, so the next tile's MMAs overlap the
+//               epilogue of this one;
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (thread = row), fused
+//               epilogue math; plain, bias and row-statistics outputs and
+//               split-K partials leave through swizzled 32x32 shared-memory
+//               boxes and TMA stores; the auxiliary epilogues (GELU, residual,
+//               activation VJPs) go through a padded staging area with
+//               16-byte row-segment accesses.
+// Tile options, chosen per shape by a cost model fitted to measured times: one
+// CTA with a 128x128 or 128x256 tile, or a CTA pair (cta_group::2, M = 256,
+// each CTA loading half of A and half of B) with 256x128 or 256x256, plus
+// K-split work units summed in a fixed order by a reduce kernel.
 // Operands may be K-major or MN-major (instruction-descriptor bits 15/16),
 // which covers x.W^T (forward), dY.W (input gradient) and X^T.dY (weight
 // gradient) without copies.
 //
 // F32 path: a register-blocked FFMA kernel (128x128 tile, 8x8 per thread).
-// It is the fp32-accurate contraction for the fp32 configurations (the tensor
-// cores' TF32 would miss a 1e-4 relative tolerance) and the path for shapes
-// TMA cannot describe.
+// It is the F32-accurate contraction for the F32 configurations (a single
+// TF32 product rounds its operands to 10 mantissa bits, which misses a 1e-4
+// relative tolerance) and the path for shapes TMA cannot describe.
 #include <cuda.h>
 
 #include <cstdio>

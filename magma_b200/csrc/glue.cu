@@ -197,9 +197,10 @@ emb_run_sum(const uint32_t* __restrict__ tok_sorted, const uint32_t* __restrict_
   }
 }
 
-// dwpe[s, i] += sum_b dout[b*seq + s, i], summed in b order (deterministic).
+// dwpe[s, i] (+)= sum_b dout[b*seq + s, i], summed in b order (deterministic);
+// accumulate = 0 writes the sum.
 __global__ void embedding_bwd_pos_kernel(const float* __restrict__ dout, float* __restrict__ dwpe,
-                                         int64_t batch, int64_t seq, int dim) {
+                                         int64_t batch, int64_t seq, int dim, int accumulate) {
   int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t total = seq * dim;
   for (; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
@@ -207,7 +208,7 @@ __global__ void embedding_bwd_pos_kernel(const float* __restrict__ dout, float* 
     int i = (int)(idx % dim);
     float acc = 0.f;
     for (int64_t b = 0; b < batch; ++b) acc += dout[(b * seq + s) * dim + i];
-    dwpe[idx] += acc;
+    dwpe[idx] = accumulate ? dwpe[idx] + acc : acc;
   }
 }
 
@@ -487,6 +488,32 @@ reduce_sum_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t 
   }
 }
 
+// Mean-squared error of the value-layer example (Examples/ValueLayers/main.swift:
+// r = pred - target; loss = sum(r * r) / divisor) and its VJP: the divide's
+// pullback gives v = 1 / divisor, the sum's broadcasts it, and the product
+// r * r returns v * r to each factor, added: dpred = v * r + v * r. One block;
+// every thread sums a fixed stride of elements, then a fixed tree.
+__global__ void __launch_bounds__(1024)
+mse_kernel(const float* __restrict__ pred, const float* __restrict__ target,
+           float* __restrict__ dpred, float* __restrict__ loss, int64_t n, float divisor) {
+  __shared__ float red[32];
+  const float v = 1.0f / divisor;
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float r = pred[i] - target[i];
+    s += r * r;
+    if (dpred) dpred[i] = __fadd_rn(__fmul_rn(v, r), __fmul_rn(v, r));
+  }
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) loss[0] = t / divisor;
+  }
+}
+
 // ---- element-wise activations ------------------------------------------------
 enum class Act { GeluFwd, GeluBwd, ReluFwd, ReluBwd };
 
@@ -647,7 +674,7 @@ magma_status_t magma_embedding_bwd(const int32_t* tokens, const float* dout, flo
   if (magma_status_t st = check_launch("embedding_bwd_tok")) return st;
   if (dwpe != nullptr) {
     embedding_bwd_pos_kernel<<<grid_for(seq * dim, 256), 256, 0, s>>>(dout, dwpe, batch, seq,
-                                                                       (int)dim);
+                                                                       (int)dim, 1);
     if (magma_status_t st = check_launch("embedding_bwd_pos")) return st;
   }
   return MAGMA_OK;
@@ -661,8 +688,8 @@ int64_t magma_embedding_bwd_workspace_size(int64_t batch, int64_t seq) {
 magma_status_t magma_embedding_bwd_deterministic(const int32_t* tokens, const float* dout,
                                                  float* dwte, float* dwpe, int64_t batch,
                                                  int64_t seq, int64_t dim, int64_t vocab,
-                                                 void* workspace, int64_t workspace_bytes,
-                                                 void* stream) {
+                                                 int32_t accumulate_dwpe, void* workspace,
+                                                 int64_t workspace_bytes, void* stream) {
   MAGMA_REQUIRE(batch >= 0 && seq > 0 && dim > 0 && vocab > 0 && dim <= INT32_MAX,
                 "magma_embedding_bwd_deterministic: bad shape");
   MAGMA_REQUIRE(vocab < (int64_t)(kEmbNoKey >> kEmbRowBits),
@@ -707,7 +734,7 @@ magma_status_t magma_embedding_bwd_deterministic(const int32_t* tokens, const fl
   if (magma_status_t st = check_launch("embedding_bwd_runs")) return st;
   if (dwpe != nullptr) {
     embedding_bwd_pos_kernel<<<grid_for(seq * dim, 256), 256, 0, s>>>(dout, dwpe, batch, seq,
-                                                                       (int)dim);
+                                                                       (int)dim, accumulate_dwpe);
     if (magma_status_t st = check_launch("embedding_bwd_pos")) return st;
   }
   return MAGMA_OK;
@@ -785,6 +812,15 @@ magma_status_t magma_reduce_sum(const float* x, float* out, int64_t n, float sca
   MAGMA_REQUIRE(out != nullptr && (n == 0 || x != nullptr), "magma_reduce_sum: NULL pointer");
   reduce_sum_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, out, n, scale);
   return check_launch("reduce_sum");
+}
+
+magma_status_t magma_mse_fwd_bwd(const float* pred, const float* target, float* dpred,
+                                float* loss, int64_t n, float divisor, void* stream) {
+  MAGMA_REQUIRE(n >= 0 && divisor > 0.f, "magma_mse_fwd_bwd: bad arguments n=%lld divisor=%g",
+                (long long)n, (double)divisor);
+  MAGMA_REQUIRE(loss != nullptr && (n == 0 || (pred && target)), "magma_mse_fwd_bwd: NULL pointer");
+  mse_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(pred, target, dpred, loss, n, divisor);
+  return check_launch("mse");
 }
 
 magma_status_t magma_gelu_fwd(const void* x, void* y, int64_t n, magma_dtype_t dtype,

@@ -82,6 +82,56 @@ class GPTConfig:
         table["__total__"] = (off, ())
         return table
 
+    def reference_parameters(self) -> list[tuple[str, tuple[int, ...], int]]:
+        """The reference GPT2 model's parameters() in its order
+        (Benchmarks/GPT2Shakespeare/Sources/main.swift:255-256, 184-185,
+        127-130, 314-317): wte, wpe; per block ln1 (weight, bias), wQ, wK, wV,
+        wO (weight [out, in], bias each), ln2, cFc, cProj; lnF; lmHead (weight
+        only). Each entry is (the name nn layers give it, shape, offset in the
+        parameter arena): wQ/wK/wV are row blocks of the fused [3D, D]
+        projection and its bias, the embedding tables their first `vocab`
+        rows, and a tied lmHead the token embedding itself."""
+        D, t = self.dim, self.offsets()
+        out = [("weight", (self.vocab, D), t["wte"][0]), ("weight", (self.seq, D), t["wpe"][0])]
+        for l in range(self.layers):
+            o = lambda n: t[f"h{l}.{n}"][0]  # noqa: E731
+            out += [("weight", (D,), o("ln1_w")), ("bias", (D,), o("ln1_b"))]
+            for j in range(3):  # wQ, wK, wV
+                out += [("weight", (D, D), o("qkv_w") + j * D * D),
+                        ("bias", (D,), o("qkv_b") + j * D)]
+            out += [("weight", (D, D), o("proj_w")), ("bias", (D,), o("proj_b")),
+                    ("weight", (D,), o("ln2_w")), ("bias", (D,), o("ln2_b")),
+                    ("weight", (4 * D, D), o("fc_w")), ("bias", (4 * D,), o("fc_b")),
+                    ("weight", (D, 4 * D), o("fcproj_w")), ("bias", (D,), o("fcproj_b"))]
+        out += [("weight", (D,), t["lnf_w"][0]), ("bias", (D,), t["lnf_b"][0]),
+                ("weight", (self.vocab, D), t["wte" if self.tied else "lm_head"][0])]
+        return out
+
+    def to_reference_entries(self, arena: np.ndarray, suffix: str = ""):
+        """Checkpoint entries of an F32 arena in the reference's parameter order."""
+        from . import checkpoint as ck
+
+        return [ck.Entry(name + suffix, shp, arena[off:off + math.prod(shp)])
+                for name, shp, off in self.reference_parameters()]
+
+    def from_reference_entries(self, entries, arena: np.ndarray, kind: str = "parameter") -> None:
+        """Writes checkpoint entries in the reference's order into an F32 arena
+        (count and shapes checked by position, as BinaryCheckpoint.load does);
+        for a tied model the lmHead entry must equal the token embedding."""
+        from . import checkpoint as ck
+
+        ref = self.reference_parameters()
+        ck.match(entries, [(n, s) for n, s, _ in ref], kind)
+        for i, (e, (_, shp, off)) in enumerate(zip(entries, ref)):
+            n = math.prod(shp)
+            if self.tied and i == len(ref) - 1:
+                if not np.array_equal(arena[off:off + n], e.values):
+                    raise ck.CheckpointError(
+                        f"{kind} {i} (lmHead) differs from the token embedding: the checkpoint "
+                        "holds an untied model; load it with tied=False")
+                continue
+            arena[off:off + n] = e.values
+
     def num_params(self) -> int:
         """Parameters excluding the vocabulary padding rows."""
         n = sum(math.prod(s) for _, s in self.shapes())
@@ -397,12 +447,13 @@ class GPTTrainer:
             if (seg_top - l + 1 == self.SYNC_GROUP) and l > 0:
                 yield [self._grad_range(l, seg_top)]
                 seg_top = l - 1
-        # embeddings: dwte += scatter(dresid); dwpe = sum over batch
-        self.view(G, "wpe").zero_()
+        # embeddings: dwte += scatter(dresid) (tied: onto the lm-head
+        # gradient; untied: onto zeros); dwpe = sum over the batch, written
         if not cfg.tied:
-            self.view(G, "wte").zero_()
+            wte_g = self.view(G, "wte")
+            lib.call("magma_memset", _p(wte_g), 0, wte_g.numel() * 4, s)
         lib.call("magma_embedding_bwd_deterministic", _p(self.tokens), _p(self.dresid),
-                 _p(self.view(G, "wte")), _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp,
+                 _p(self.view(G, "wte")), _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp, 0,
                  _p(self.emb_ws), self.emb_ws.numel() * 4, s)
         yield [self._grad_range(0, seg_top), (0, self.table["h0.ln1_w"][0]),
                (self.table["lnf_w"][0], self.P)]
@@ -440,33 +491,24 @@ class GPTTrainer:
                  self.wd, self.t, grad_scale, _p(self.grad_norm), self.grad_clip, self._s())
 
     # --------------------------------------------------------- checkpoints
-    def _model_tensors(self) -> list[tuple[str, tuple[int, ...], int]]:
-        """(name, shape as stored, arena offset) of every parameter: the
-        embedding and lm-head tables without their vocabulary padding rows."""
-        out = []
-        for name, shp in self.cfg.shapes():
-            if name in ("wte", "lm_head"):
-                shp = (self.cfg.vocab,) + tuple(shp[1:])
-            out.append((name, tuple(shp), self.table[name][0]))
-        return out
-
     def save_checkpoint(self, path) -> None:
         """Parameters to `path` in the reference's BinaryCheckpoint format
-        (Module.swift:4838-4890); Adam's m, v and step count to `path`.adam in
-        the same format."""
+        (Module.swift:4838-4890), in the reference GPT2's parameters() order
+        with its shapes (GPTConfig.reference_parameters: separate wQ/wK/wV,
+        lmHead written even when tied), so the file loads wherever that model's
+        parameter list does. Adam's m and v (same order) and the step count go
+        to `path`.adam in the same format; the step is stored as two F32
+        values, its low and high 16 bits, each exact in F32."""
         from . import checkpoint as ck
 
+        if not 0 <= self.t < 1 << 32:
+            raise ck.CheckpointError(f"step count {self.t} does not fit 32 bits")
         torch.cuda.current_stream(self.dev).synchronize()
         host = {k: a.cpu().numpy() for k, a in (("p", self.params), ("m", self.m), ("v", self.v))}
-        ents = {k: [] for k in host}
-        for name, shp, off in self._model_tensors():
-            n = math.prod(shp)
-            for k in host:
-                suffix = "" if k == "p" else f".{k}"
-                ents[k].append(ck.Entry(name + suffix, shp, host[k][off:off + n]))
-        ck.save(path, ents["p"])
-        step = ck.Entry("adam.step", (), np.array([float(self.t)], np.float32))
-        ck.save(str(path) + ".adam", ents["m"] + ents["v"], [step])
+        ck.save(path, self.cfg.to_reference_entries(host["p"]))
+        step = ck.Entry("adam.step", (2,), np.array([self.t & 0xFFFF, self.t >> 16], np.float32))
+        ck.save(str(path) + ".adam", self.cfg.to_reference_entries(host["m"], ".m")
+                + self.cfg.to_reference_entries(host["v"], ".v"), [step])
 
     def load_checkpoint(self, path, optimizer_state: bool = True) -> None:
         """Inverse of save_checkpoint. Everything is read and checked (count,
@@ -474,34 +516,30 @@ class GPTTrainer:
         optimizer_state=True is an error."""
         from . import checkpoint as ck
 
-        tensors = self._model_tensors()
-        expected = [(n, s) for n, s, _ in tensors]
         _, params, bufs = ck.load(path)
-        ck.match(params, expected, "parameter")
         if bufs:
             raise ck.CheckpointError(f"the GPT model has no buffers; checkpoint has {len(bufs)}")
+        host = {"p": self.params.cpu().numpy().copy()}
+        self.cfg.from_reference_entries(params, host["p"])
         if optimizer_state:
             _, mv, extra = ck.load(str(path) + ".adam")
-            ck.match(mv, [(n + ".m", s) for n, s in expected] + [(n + ".v", s) for n, s in expected],
-                     "optimizer tensor")
-            if len(extra) != 1 or extra[0].name != "adam.step" or extra[0].shape != ():
+            k = len(params)
+            if len(mv) != 2 * k:
+                raise ck.CheckpointError(f"optimizer file has {len(mv)} tensors, expected {2 * k}")
+            if len(extra) != 1 or extra[0].name != "adam.step" or extra[0].shape != (2,):
                 raise ck.CheckpointError("optimizer file lacks its adam.step entry")
-        host = {"p": self.params.cpu().numpy().copy()}
-        if optimizer_state:
+            lo, hi = (float(x) for x in extra[0].values)
+            if not (lo.is_integer() and hi.is_integer() and 0 <= lo < 65536 and 0 <= hi < 65536):
+                raise ck.CheckpointError(f"corrupt adam.step entry ({lo}, {hi})")
             host["m"] = np.zeros(self.P, np.float32)
             host["v"] = np.zeros(self.P, np.float32)
-        k = len(tensors)
-        for i, (name, shp, off) in enumerate(tensors):
-            n = math.prod(shp)
-            host["p"][off:off + n] = params[i].values
-            if optimizer_state:
-                host["m"][off:off + n] = mv[i].values
-                host["v"][off:off + n] = mv[k + i].values
+            self.cfg.from_reference_entries(mv[:k], host["m"], "optimizer tensor")
+            self.cfg.from_reference_entries(mv[k:], host["v"], "optimizer tensor")
         self.params.copy_(torch.from_numpy(host["p"]))
         if optimizer_state:
             self.m.copy_(torch.from_numpy(host["m"]))
             self.v.copy_(torch.from_numpy(host["v"]))
-            self.t = int(extra[0].values[0])
+            self.t = int(lo) + (int(hi) << 16)
         if self.shadow is not None:
             self._sync_shadow()
         torch.cuda.current_stream(self.dev).synchronize()

@@ -297,15 +297,17 @@ def embedding_bwd(tokens: torch.Tensor, dout: torch.Tensor, dwte: torch.Tensor,
 
 def embedding_bwd_deterministic(tokens: torch.Tensor, dout: torch.Tensor, dwte: torch.Tensor,
                                 dwpe: torch.Tensor | None,
-                                workspace: torch.Tensor | None = None) -> None:
+                                workspace: torch.Tensor | None = None,
+                                accumulate_dwpe: bool = True) -> None:
     """The scatter-add VJP with rows added to each token row in row order
-    (identical on every run), accumulating."""
+    (identical on every run), accumulating into dwte; dwpe is added to, or
+    written with accumulate_dwpe=False."""
     B, S = tokens.shape
     need = lib.query("magma_embedding_bwd_workspace_size", B, S)
     ws = workspace if workspace is not None else torch.empty(
         max(need // 4, 1), dtype=torch.int32, device=dwte.device)
     lib.call("magma_embedding_bwd_deterministic", _ptr(tokens), _ptr(dout), _ptr(dwte),
-             _ptr(dwpe), B, S, dwte.shape[1], dwte.shape[0], _ptr(ws),
+             _ptr(dwpe), B, S, dwte.shape[1], dwte.shape[0], int(accumulate_dwpe), _ptr(ws),
              ws.numel() * ws.element_size(), _stream())
 
 

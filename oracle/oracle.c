@@ -171,6 +171,183 @@ void oracle_layernorm_bwd(const float* dy, const float* x, const float* gamma, f
   free(pg);
 }
 
+/* nn.LayerNorm's backward (Module.swift:2774-2784): the module takes the
+ * variance through Tensor.variance(dims:unbiased:false), whose custom VJP
+ * (vjpVariance, Autodiff.swift:576-592) returns v * centered * (2/N) without
+ * a path through the mean, while the GPT block's layerNorm (main.swift:
+ * 364-375, oracle_layernorm_bwd above) forms it as mean(centered*centered).
+ * The two agree up to rounding (sum(centered) = 0). Chain per row:
+ *   normalized = centered / std  vjpDivide: dcent = v/std, dstd = sum(-v*result/std)
+ *   std = sqrt(var + eps)        vjpSqrt: v*0.5/result
+ *   var = x.variance(...)        vjpVariance: dvar * centered * (2/N)
+ *   centered = x - mean          vjpSubtract: dx += dcent, dmean = -sum(dcent)
+ *   mean = x.mean(...)           vjpMeanDims: dmean / N broadcast. */
+void oracle_layernorm_module_bwd(const float* dy, const float* x, const float* gamma, float* dx,
+                                 float* dgamma, float* dbeta, int64_t rows, int64_t dim,
+                                 float eps) {
+  const float two_n = 2.0f / (float)dim;
+  float* row_mean = (float*)xmalloc((size_t)rows * sizeof(float));
+  float* row_std = (float*)xmalloc((size_t)rows * sizeof(float));
+#pragma omp parallel
+  {
+    float* centered = (float*)xmalloc((size_t)dim * sizeof(float));
+    float* dcent = (float*)xmalloc((size_t)dim * sizeof(float));
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      const float* xr = x + r * dim;
+      const float* dyr = dy + r * dim;
+      float s = 0.f;
+      for (int64_t i = 0; i < dim; ++i) s += xr[i];
+      const float mean = s / (float)dim;
+      float ss = 0.f;
+      for (int64_t i = 0; i < dim; ++i) {
+        centered[i] = xr[i] - mean;
+        ss += centered[i] * centered[i];
+      }
+      const float stdv = sqrtf(ss / (float)dim + eps);
+      row_mean[r] = mean;
+      row_std[r] = stdv;
+      float dstd = 0.f;
+      for (int64_t i = 0; i < dim; ++i) {
+        const float normalized = centered[i] / stdv;
+        const float dnorm = dyr[i] * gamma[i];
+        dcent[i] = dnorm / stdv;
+        dstd += (-dnorm) * normalized / stdv;
+      }
+      const float dvar = dstd * 0.5f / stdv;
+      float dmean = 0.f;
+      for (int64_t i = 0; i < dim; ++i) dmean += -dcent[i];
+      const float dmb = dmean / (float)dim;
+      for (int64_t i = 0; i < dim; ++i) dx[r * dim + i] = dcent[i] + dmb + dvar * centered[i] * two_n;
+    }
+    free(centered);
+    free(dcent);
+  }
+  if (dgamma || dbeta) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < dim; ++i) {
+      float sg = 0.f, sb = 0.f;
+      for (int64_t r = 0; r < rows; ++r) {
+        sg += dy[r * dim + i] * ((x[r * dim + i] - row_mean[r]) / row_std[r]);
+        sb += dy[r * dim + i];
+      }
+      if (dgamma) dgamma[i] = sg;
+      if (dbeta) dbeta[i] = sb;
+    }
+  }
+  free(row_mean);
+  free(row_std);
+}
+
+/* ---- reduction, softmax and masking primitives (2-D, row-major [rows, cols])
+ * The pieces the LayerNorm and attention chains are made of, exported so that
+ * the reference's own gradient checks of these primitives
+ * (Tests/CoreTests/CrossModuleDifferentiabilityTests.swift) can be run on the
+ * oracle. axis 0 reduces over rows (one result per column), axis 1 over
+ * columns (one per row); axis 2 reduces over both (one result). */
+static void reduce_geometry(int64_t rows, int64_t cols, int axis, int64_t* outer, int64_t* count,
+                            int64_t* stride_out, int64_t* stride_in) {
+  if (axis == 1) { *outer = rows; *count = cols; *stride_out = cols; *stride_in = 1; }
+  else if (axis == 0) { *outer = cols; *count = rows; *stride_out = 1; *stride_in = cols; }
+  else { *outer = 1; *count = rows * cols; *stride_out = 0; *stride_in = 1; }
+}
+
+/* Tensor.variance(dims:unbiased:) (Tensor.swift:2014-2043): meanVal = mean;
+ * centered = x - meanVal; mean(centered*centered); times count/(count-1)
+ * when unbiased and count > 1. out has one entry per reduced group. */
+void oracle_variance_fwd(const float* x, float* out, int64_t rows, int64_t cols, int axis,
+                         int unbiased) {
+  int64_t outer, count, so, si;
+  reduce_geometry(rows, cols, axis, &outer, &count, &so, &si);
+  for (int64_t o = 0; o < outer; ++o) {
+    const float* base = x + o * so;
+    float s = 0.f;
+    for (int64_t i = 0; i < count; ++i) s += base[i * si];
+    const float mean = s / (float)count;
+    float ss = 0.f;
+    for (int64_t i = 0; i < count; ++i) {
+      const float c = base[i * si] - mean;
+      ss += c * c;
+    }
+    float var = ss / (float)count;
+    if (unbiased && count > 1) var = var * ((float)count / (float)(count - 1));
+    out[o] = var;
+  }
+}
+
+/* vjpVariance (Autodiff.swift:576-592): dx = v * centered * (2/d), d = N-1
+ * when unbiased and N > 1, else N; v has one entry per reduced group. */
+void oracle_variance_vjp(const float* x, const float* v, float* dx, int64_t rows, int64_t cols,
+                         int axis, int unbiased) {
+  int64_t outer, count, so, si;
+  reduce_geometry(rows, cols, axis, &outer, &count, &so, &si);
+  const int64_t den = unbiased && count > 1 ? count - 1 : count;
+  const float scale = 2.0f / (float)den;
+  for (int64_t o = 0; o < outer; ++o) {
+    const float* base = x + o * so;
+    float s = 0.f;
+    for (int64_t i = 0; i < count; ++i) s += base[i * si];
+    const float mean = s / (float)count;
+    for (int64_t i = 0; i < count; ++i) {
+      const float c = base[i * si] - mean;
+      dx[o * so + i * si] = v[o] * c * scale;
+    }
+  }
+}
+
+/* Softmax composite (StableHLOEmitter.swift:795-803: max, subtract, exp, sum,
+ * divide) along axis 0 or 1 of a [rows, cols] tensor. */
+void oracle_softmax_fwd(const float* x, float* s, int64_t rows, int64_t cols, int axis) {
+  int64_t outer, count, so, si;
+  reduce_geometry(rows, cols, axis, &outer, &count, &so, &si);
+  for (int64_t o = 0; o < outer; ++o) {
+    const float* xb = x + o * so;
+    float* sb = s + o * so;
+    float mx = -INFINITY;
+    for (int64_t i = 0; i < count; ++i) mx = xb[i * si] > mx ? xb[i * si] : mx;
+    float sum = 0.f;
+    for (int64_t i = 0; i < count; ++i) {
+      sb[i * si] = expf(xb[i * si] - mx);
+      sum += sb[i * si];
+    }
+    for (int64_t i = 0; i < count; ++i) sb[i * si] = sb[i * si] / sum;
+  }
+}
+
+/* vjpSoftmax (Autodiff.swift:379-386) along axis 0 or 1, given the softmax
+ * output s and the cotangent v; the per-row form is what the attention
+ * backward applies to its probabilities. */
+void oracle_softmax_vjp(const float* s, const float* v, float* dx, int64_t rows, int64_t cols,
+                        int axis) {
+  int64_t outer, count, so, si;
+  reduce_geometry(rows, cols, axis, &outer, &count, &so, &si);
+  for (int64_t o = 0; o < outer; ++o) {
+    float sumvs = 0.f;
+    for (int64_t i = 0; i < count; ++i) sumvs += v[o * so + i * si] * s[o * so + i * si];
+    for (int64_t i = 0; i < count; ++i) {
+      const int64_t e = o * so + i * si;
+      dx[e] = s[e] * (v[e] - sumvs);
+    }
+  }
+}
+
+/* maskedFill (Tensor.swift:1251-1262): out = mask != 0 ? value : x, and its
+ * VJP (vjpMaskedFill, Autodiff.swift:601-613): dx = v * (1 - selected),
+ * dvalue = v * selected (value of the same shape). The attention chains use
+ * it as the causal mask (value -1e9; its cotangent is discarded). */
+void oracle_masked_fill_fwd(const float* x, const float* mask, const float* value, float* out,
+                            int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = mask[i] != 0.0f ? value[i] : x[i];
+}
+void oracle_masked_fill_vjp(const float* mask, const float* v, float* dx, float* dvalue,
+                            int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    const float selected = mask[i] != 0.0f ? 1.0f : 0.0f;
+    if (dx) dx[i] = v[i] * (1.0f - selected);
+    if (dvalue) dvalue[i] = v[i] * selected;
+  }
+}
+
 /* ---- attention ------------------------------------------------------------
  * main.swift:467-481 / Module.swift:2408-2441: scores = (q . k^T) * scale;
  * masked = scores + mask (0 or -1e9, main.swift:793-801); softmax composite
@@ -226,9 +403,19 @@ void oracle_attention_fwd(const float* q, const float* k, const float* v, float*
   }
 }
 
+/* vjpSoftmax (Autodiff.swift:379-386) on one row of n entries:
+ * dx = s * (v - sum(v * s)), the sum over the row in increasing order. */
+static void softmax_vjp_row(const float* s, const float* v, float* dx, int64_t n) {
+  float sumvs = 0.f;
+  for (int64_t j = 0; j < n; ++j) sumvs += v[j] * s[j];
+  for (int64_t j = 0; j < n; ++j) dx[j] = s[j] * (v[j] - sumvs);
+}
+
 /* VJP chain: vjpBatchedMatmul (Autodiff.swift:309-317): dP = dO.V^T, dV = P^T.dO;
  * vjpSoftmax (:379-386): dS = P*(dP - sum(dP*P)); mask add passes dS; scale
- * multiply (:76-82): dQK = dS*scale; dQ = dQK.K, dK = dQK^T.Q. */
+ * multiply (:76-82): dQK = dS*scale; dQ = dQK.K, dK = dQK^T.Q. Every output
+ * element is a sum over its contraction index in increasing order; the loops
+ * that accumulate whole rows keep that order per element. */
 void oracle_attention_bwd(const float* q, const float* k, const float* v, const float* d_o,
                           float* dq, float* dk, float* dv, int64_t batch, int64_t heads,
                           int64_t seq, int64_t hd, float scale, int causal) {
@@ -253,32 +440,91 @@ void oracle_attention_bwd(const float* q, const float* k, const float* v, const 
           for (int64_t d = 0; d < hd; ++d) s += doh[i * hd + d] * vh[j * hd + d];
           dp[i * seq + j] = s;
         }
-      for (int64_t j = 0; j < seq; ++j)
-        for (int64_t d = 0; d < hd; ++d) {
-          float s = 0.f;
-          for (int64_t i = 0; i < seq; ++i) s += p[i * seq + j] * doh[i * hd + d];
-          dvh[j * hd + d] = s;
-        }
+      /* dV[j, :] = sum_i P[i, j] dO[i, :] */
+      memset(dvh, 0, (size_t)seq * hd * sizeof(float));
+      for (int64_t i = 0; i < seq; ++i)
+        for (int64_t j = 0; j < seq; ++j) axpy_row(dvh + j * hd, doh + i * hd, p[i * seq + j], hd);
       for (int64_t i = 0; i < seq; ++i) {
-        float sumvs = 0.f;
-        for (int64_t j = 0; j < seq; ++j) sumvs += dp[i * seq + j] * p[i * seq + j];
+        softmax_vjp_row(p + i * seq, dp + i * seq, dp + i * seq, seq);
+        for (int64_t j = 0; j < seq; ++j) dp[i * seq + j] = dp[i * seq + j] * scale;
+      }
+      /* dQ[i, :] = sum_j dQK[i, j] K[j, :];  dK[j, :] = sum_i dQK[i, j] Q[i, :] */
+      memset(dqh, 0, (size_t)seq * hd * sizeof(float));
+      memset(dkh, 0, (size_t)seq * hd * sizeof(float));
+      for (int64_t i = 0; i < seq; ++i)
+        for (int64_t j = 0; j < seq; ++j) axpy_row(dqh + i * hd, kh + j * hd, dp[i * seq + j], hd);
+      for (int64_t i = 0; i < seq; ++i)
+        for (int64_t j = 0; j < seq; ++j) axpy_row(dkh + j * hd, qh + i * hd, dp[i * seq + j], hd);
+    }
+    free(p);
+    free(dp);
+  }
+}
+
+/* BF16 round-to-nearest-even of an F32 value (LazyTensor.swift:1511-1516),
+ * returned as F32. NaN stays NaN. */
+static inline float bf16_round(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return x;
+  u = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  float r;
+  memcpy(&r, &u, 4);
+  return r;
+}
+
+/* The attention VJP chain as a BF16 program runs it: the probabilities and the
+ * softmax cotangent are materialised as BF16 tensors before the contractions
+ * that consume them (a BF16 graph of the reference stores every intermediate
+ * in BF16, rounding to nearest even, LazyTensor.swift:1511-1516), and the
+ * row term of the softmax VJP is formed from the stored (BF16) output:
+ * sum_j dP_ij P_ij = sum_d dO_id O_id. Everything else as
+ * oracle_attention_bwd, in F32: dP = dO.V^T; dS = P*(dP - delta);
+ * dV = bf16(P)^T.dO; dQ = (bf16(dS).K)*scale; dK = (bf16(dS)^T.Q)*scale.
+ * Inputs are the BF16 values as F32; o is the forward output as stored. */
+void oracle_attention_bwd_bf16(const float* q, const float* k, const float* v, const float* o,
+                               const float* d_o, float* dq, float* dk, float* dv, int64_t batch,
+                               int64_t heads, int64_t seq, int64_t hd, float scale, int causal) {
+  const int64_t bh = batch * heads;
+#pragma omp parallel
+  {
+    float* p = (float*)xmalloc((size_t)seq * seq * sizeof(float));
+    float* dp = (float*)xmalloc((size_t)seq * seq * sizeof(float));
+#pragma omp for schedule(dynamic)
+    for (int64_t h = 0; h < bh; ++h) {
+      const float* qh = q + h * seq * hd;
+      const float* kh = k + h * seq * hd;
+      const float* vh = v + h * seq * hd;
+      const float* oh = o + h * seq * hd;
+      const float* doh = d_o + h * seq * hd;
+      float* dqh = dq + h * seq * hd;
+      float* dkh = dk + h * seq * hd;
+      float* dvh = dv + h * seq * hd;
+      attention_probs_head(qh, kh, p, NULL, seq, hd, scale, causal);
+      for (int64_t i = 0; i < seq; ++i) {
+        float delta = 0.f;
+        for (int64_t d = 0; d < hd; ++d) delta += doh[i * hd + d] * oh[i * hd + d];
         for (int64_t j = 0; j < seq; ++j) {
-          float ds = p[i * seq + j] * (dp[i * seq + j] - sumvs);
-          dp[i * seq + j] = ds * scale;
+          float s = 0.f;
+          for (int64_t d = 0; d < hd; ++d) s += doh[i * hd + d] * vh[j * hd + d];
+          const float pij = p[i * seq + j];
+          dp[i * seq + j] = bf16_round(pij * (s - delta));
+          p[i * seq + j] = bf16_round(pij);
         }
       }
+      memset(dvh, 0, (size_t)seq * hd * sizeof(float));
+      memset(dqh, 0, (size_t)seq * hd * sizeof(float));
+      memset(dkh, 0, (size_t)seq * hd * sizeof(float));
       for (int64_t i = 0; i < seq; ++i)
-        for (int64_t d = 0; d < hd; ++d) {
-          float s = 0.f;
-          for (int64_t j = 0; j < seq; ++j) s += dp[i * seq + j] * kh[j * hd + d];
-          dqh[i * hd + d] = s;
+        for (int64_t j = 0; j < seq; ++j) {
+          axpy_row(dvh + j * hd, doh + i * hd, p[i * seq + j], hd);
+          axpy_row(dqh + i * hd, kh + j * hd, dp[i * seq + j], hd);
+          axpy_row(dkh + j * hd, qh + i * hd, dp[i * seq + j], hd);
         }
-      for (int64_t j = 0; j < seq; ++j)
-        for (int64_t d = 0; d < hd; ++d) {
-          float s = 0.f;
-          for (int64_t i = 0; i < seq; ++i) s += dp[i * seq + j] * qh[i * hd + d];
-          dkh[j * hd + d] = s;
-        }
+      for (int64_t e = 0; e < seq * hd; ++e) {
+        dqh[e] = dqh[e] * scale;
+        dkh[e] = dkh[e] * scale;
+      }
     }
     free(p);
     free(dp);

@@ -34,6 +34,25 @@ void oracle_layernorm_fwd(const float* x, const float* gamma, const float* beta,
 void oracle_layernorm_bwd(const float* dy, const float* x, const float* gamma, float* dx,
                           float* dgamma, float* dbeta, int64_t rows, int64_t dim, float eps);
 
+/* nn.LayerNorm's backward chain (variance through vjpVariance). */
+void oracle_layernorm_module_bwd(const float* dy, const float* x, const float* gamma, float* dx,
+                                 float* dgamma, float* dbeta, int64_t rows, int64_t dim,
+                                 float eps);
+
+/* Primitives of those chains on [rows, cols]; axis 0: over rows, 1: over
+ * columns, 2: over both. */
+void oracle_variance_fwd(const float* x, float* out, int64_t rows, int64_t cols, int axis,
+                         int unbiased);
+void oracle_variance_vjp(const float* x, const float* v, float* dx, int64_t rows, int64_t cols,
+                         int axis, int unbiased);
+void oracle_softmax_fwd(const float* x, float* s, int64_t rows, int64_t cols, int axis);
+void oracle_softmax_vjp(const float* s, const float* v, float* dx, int64_t rows, int64_t cols,
+                        int axis);
+void oracle_masked_fill_fwd(const float* x, const float* mask, const float* value, float* out,
+                            int64_t n);
+void oracle_masked_fill_vjp(const float* mask, const float* v, float* dx, float* dvalue,
+                            int64_t n);
+
 /* Q,K,V,O contiguous [batch, heads, seq, hd]. probs (optional) receives the
  * softmax [batch, heads, seq, seq]; lse (optional) the row log-sum-exp. */
 void oracle_attention_fwd(const float* q, const float* k, const float* v, float* o, float* probs,
@@ -42,6 +61,13 @@ void oracle_attention_fwd(const float* q, const float* k, const float* v, float*
 void oracle_attention_bwd(const float* q, const float* k, const float* v, const float* d_o,
                           float* dq, float* dk, float* dv, int64_t batch, int64_t heads,
                           int64_t seq, int64_t hd, float scale, int causal);
+
+/* The same chain with the probabilities and the softmax cotangent rounded to
+ * BF16 before their contractions and the row term taken from the stored
+ * output o (all inputs BF16 values carried as F32). */
+void oracle_attention_bwd_bf16(const float* q, const float* k, const float* v, const float* o,
+                               const float* d_o, float* dq, float* dk, float* dv, int64_t batch,
+                               int64_t heads, int64_t seq, int64_t hd, float scale, int causal);
 
 void oracle_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr, float beta1,
                  float beta2, float eps, float weight_decay, int64_t step, float grad_scale);

@@ -51,10 +51,21 @@ def lib():
                                            _i64, _i64, C.c_float]
         L.oracle_layernorm_bwd.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64,
                                            C.c_float]
+        L.oracle_layernorm_module_bwd.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                                  _i64, _i64, C.c_float]
+        L.oracle_variance_fwd.argtypes = [_f32p, _f32p, _i64, _i64, C.c_int, C.c_int]
+        L.oracle_variance_vjp.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, C.c_int, C.c_int]
+        L.oracle_softmax_fwd.argtypes = [_f32p, _f32p, _i64, _i64, C.c_int]
+        L.oracle_softmax_vjp.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, C.c_int]
+        L.oracle_masked_fill_fwd.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64]
+        L.oracle_masked_fill_vjp.argtypes = [_f32p, _f32p, C.c_void_p, C.c_void_p, _i64]
         L.oracle_attention_fwd.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
                                            _i64, _i64, _i64, _i64, C.c_float, C.c_int]
         L.oracle_attention_bwd.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
                                            _i64, _i64, _i64, _i64, C.c_float, C.c_int]
+        L.oracle_attention_bwd_bf16.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                                _f32p, _f32p, _i64, _i64, _i64, _i64, C.c_float,
+                                                C.c_int]
         L.oracle_adam.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, C.c_float, C.c_float,
                                   C.c_float, C.c_float, C.c_float, _i64, C.c_float]
         L.oracle_grad_norm.argtypes = [_f32p, _i64, C.c_float]
@@ -127,6 +138,68 @@ def layernorm_bwd(dy, x, gamma, eps=1e-5):
     return dx, dg, db
 
 
+def layernorm_module_bwd(dy, x, gamma, eps=1e-5):
+    """nn.LayerNorm's backward chain (variance through vjpVariance)."""
+    x, dy = _f32(x), _f32(dy)
+    rows, dim = x.reshape(-1, x.shape[-1]).shape
+    dx = np.empty_like(x)
+    dg = np.empty(dim, np.float32)
+    db = np.empty(dim, np.float32)
+    lib().oracle_layernorm_module_bwd(dy, x, _f32(gamma), dx, dg, db, rows, dim, eps)
+    return dx, dg, db
+
+
+def _groups(shape, axis):
+    rows, cols = shape
+    return {0: cols, 1: rows, 2: 1}[axis]
+
+
+def variance_fwd(x, axis, unbiased):
+    """Tensor.variance over axis 0, 1 or both (2) of a 2-D array."""
+    x = _f32(x)
+    out = np.empty(_groups(x.shape, axis), np.float32)
+    lib().oracle_variance_fwd(x, out, x.shape[0], x.shape[1], axis, int(unbiased))
+    return out
+
+
+def variance_vjp(x, v, axis, unbiased):
+    x = _f32(x)
+    dx = np.empty_like(x)
+    lib().oracle_variance_vjp(x, _f32(np.reshape(v, -1)), dx, x.shape[0], x.shape[1], axis,
+                              int(unbiased))
+    return dx
+
+
+def softmax_fwd(x, axis):
+    x = _f32(x)
+    s = np.empty_like(x)
+    lib().oracle_softmax_fwd(x, s, x.shape[0], x.shape[1], axis)
+    return s
+
+
+def softmax_vjp(s, v, axis):
+    s = _f32(s)
+    dx = np.empty_like(s)
+    lib().oracle_softmax_vjp(s, _f32(v), dx, s.shape[0], s.shape[1], axis)
+    return dx
+
+
+def masked_fill_fwd(x, mask, value):
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().oracle_masked_fill_fwd(x, _f32(mask), _f32(value), out, x.size)
+    return out
+
+
+def masked_fill_vjp(mask, v):
+    """(d self, d value) of maskedFill for a cotangent v."""
+    v = _f32(v)
+    dx = np.empty_like(v)
+    dval = np.empty_like(v)
+    lib().oracle_masked_fill_vjp(_f32(mask), v, dx.ctypes.data, dval.ctypes.data, v.size)
+    return dx, dval
+
+
 def attention_fwd(q, k, v, scale, causal=True, want_probs=False):
     q, k, v = _f32(q), _f32(k), _f32(v)
     b, h, s, d = q.shape
@@ -143,6 +216,16 @@ def attention_bwd(q, k, v, d_o, scale, causal=True):
     b, h, s, d = q.shape
     dq, dk, dv = np.empty_like(q), np.empty_like(q), np.empty_like(q)
     lib().oracle_attention_bwd(q, k, v, d_o, dq, dk, dv, b, h, s, d, scale, int(causal))
+    return dq, dk, dv
+
+
+def attention_bwd_bf16(q, k, v, o, d_o, scale, causal=True):
+    """The attention VJP with BF16 probabilities and softmax cotangent and the
+    row term from the stored output o (inputs: BF16 values as float32)."""
+    q, k, v, o, d_o = (_f32(a) for a in (q, k, v, o, d_o))
+    b, h, s, d = q.shape
+    dq, dk, dv = np.empty_like(q), np.empty_like(q), np.empty_like(q)
+    lib().oracle_attention_bwd_bf16(q, k, v, o, d_o, dq, dk, dv, b, h, s, d, scale, int(causal))
     return dq, dk, dv
 
 

@@ -100,3 +100,53 @@ def test_token_dataset_rejects_small_or_missing_files(tmp_path):
         MemoryMappedTokenDataset(tmp_path / "small.bin", 8)
     with pytest.raises(TokenDatasetError, match="not found"):
         MemoryMappedTokenDataset(tmp_path / "missing.bin", 8)
+
+
+def test_gpt_checkpoint_order_is_the_reference_parameter_list():
+    """GPT2.parameters() (Benchmarks/GPT2Shakespeare/Sources/main.swift:255-256,
+    184-185, 127-130, 314-317): wte, wpe, 16 tensors per block (ln1, wQ, wK, wV,
+    wO, ln2, cFc, cProj; weight then bias), lnF, lmHead (no bias)."""
+    from magma_b200.gpt import gpt2_small
+
+    cfg = gpt2_small()
+    ref = cfg.reference_parameters()
+    D, V = 768, 50257
+    per_block = [(D,), (D,), (D, D), (D,), (D, D), (D,), (D, D), (D,), (D, D), (D,), (D,), (D,),
+                 (4 * D, D), (4 * D,), (D, 4 * D), (D,)]
+    want = [(V, D), (1024, D)] + per_block * 12 + [(D,), (D,), (V, D)]
+    assert len(ref) == 2 + 16 * 12 + 3 == 197
+    assert [s for _, s, _ in ref] == want
+    assert [n for n, _, _ in ref][:6] == ["weight", "weight", "weight", "bias", "weight", "bias"]
+    # parameters of the reference model: 163M with its separate lm-head
+    assert sum(int(np.prod(s)) for _, s, _ in ref) == 124_439_808 + V * D
+
+
+@pytest.mark.parametrize("tied", [True, False])
+def test_gpt_checkpoint_entries_round_trip(tmp_path, tied):
+    from magma_b200.gpt import GPTConfig
+
+    cfg = GPTConfig(vocab=70, seq=16, layers=2, heads=2, dim=32, tied=tied)
+    total = cfg.offsets()["__total__"][0]
+    rng = np.random.default_rng(1)
+    arena = np.zeros(total, np.float32)  # alignment gaps and vocabulary padding stay zero
+    for _, shp, off in cfg.reference_parameters():
+        n = int(np.prod(shp))
+        arena[off:off + n] = rng.standard_normal(n)
+    ents = cfg.to_reference_entries(arena)
+    ck.save(tmp_path / "g.bin", ents)
+    _, back, _ = ck.load(tmp_path / "g.bin")
+    # wQ of layer 0 is the first D rows of the fused projection
+    q_off = cfg.offsets()["h0.qkv_w"][0]
+    assert np.array_equal(back[4].values, arena[q_off:q_off + 32 * 32])
+    k_off = q_off + 32 * 32
+    assert np.array_equal(back[6].values, arena[k_off:k_off + 32 * 32])
+    got = np.zeros_like(arena)
+    cfg.from_reference_entries(back, got)
+    assert np.array_equal(got, arena)
+    with pytest.raises(ck.CheckpointError, match="count"):
+        cfg.from_reference_entries(back[:-1], got)
+    if tied:
+        bad = list(back)
+        bad[-1] = ck.Entry("weight", bad[-1].shape, bad[-1].values + 1)
+        with pytest.raises(ck.CheckpointError, match="untied"):
+            cfg.from_reference_entries(bad, got)

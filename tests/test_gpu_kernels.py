@@ -600,6 +600,11 @@ def test_embedding_bwd_deterministic_is_sequential_sum(cuda, B, S, D, V, dist):
     again = t(init)
     ops.embedding_bwd_deterministic(t(tok, torch.int32), t(dout), again, None)
     assert torch.equal(again, dwte)
+    # written rather than added: stale contents of dwpe do not matter
+    written = torch.full((S, D), 7.0, device="cuda")
+    ops.embedding_bwd_deterministic(t(tok, torch.int32), t(dout), t(init), written,
+                                    accumulate_dwpe=False)
+    assert torch.equal(written, dwpe)
 
 
 def test_bad_token_sets_device_error(cuda):

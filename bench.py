@@ -91,7 +91,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "100"], stdout=open(self.path, "w"),
+                 "-i", str(self.gpu), "-lms", "50"], stdout=open(self.path, "w"),
                 stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
@@ -232,6 +232,36 @@ def classify(name, args, cfg, tr):
     return "other", 0.0
 
 
+# ------------------------------------------------------------- configuration lines
+def config_lines(peaks: dict) -> dict:
+    """The standalone benchmark configurations on this GPU, each against its
+    roofline: LayerNorm fwd+bwd F32 [8192, 768] (HBM), causal attention
+    fwd+bwd [8, 12, 1024, 64] in BF16 (tensor pipe) and F32, and the
+    784-128-10 MLP train step (launch-bound: microseconds per step)."""
+    from magma_b200 import kernel_bench as kb
+
+    out = {}
+    ln = kb.bench_layernorm_f32(50)
+    ln.update(bound="hbm", peak=peaks["hbm_gbs"], unit="GB/s",
+              frac=round(ln["GBs"] / peaks["hbm_gbs"], 4))
+    out["layernorm_f32"] = ln
+    for name, dt, reps in (("attention_bf16", "bf16", 20), ("attention_f32", "f32", 3)):
+        import torch
+
+        at = kb.bench_attention_config(reps, torch.bfloat16 if dt == "bf16" else torch.float32)
+        at.update(bound="tensor", peak=peaks["bf16_tflops"], unit="TFLOP/s",
+                  frac=round(at["tflops"] / peaks["bf16_tflops"], 4),
+                  peak_source="measured bf16_tflops (burst; kernels timed alone)")
+        out[name] = at
+    try:
+        from magma_b200 import mlp
+
+        out["mlp_f32"] = mlp.bench_step()
+    except ImportError:
+        pass
+    return out
+
+
 # ------------------------------------------------------------------- CPU baseline
 # The reference GPT trainer's optimiser settings (TrainConfig.shakespeare,
 # main.swift:76-91), used by the GPU step and by the timed CPU steps alike.
@@ -325,7 +355,16 @@ def run_reference(args) -> None:
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": workload_config(world, args.batch),
+            "data": "synthetic",
+            "config": {"workload": f"GPT-2 small (124M: 12 layers, 12 heads, d_model 768, vocab "
+                                   f"50257, tied lm-head) F32 train step on 1 x {seq} tokens "
+                                   f"(positions < {seq}), F32 master weights + Adam with clipping "
+                                   "and the warmup-cosine schedule",
+                       "model": "gpt2-small-124M", "global_batch": 1, "seq_len": seq,
+                       "batch_per_gpu": 1, "parallelism": "none (host cores)",
+                       "note": "a bounded per-step sample of the GPU arm's 8 x 1024-token step: "
+                               "tokens/s is per token at seq <= 64, where attention costs less "
+                               "per token than at seq 1024"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": f"per step: GPT-2 small F32 fwd+bwd+clip+Adam on 1 x {seq} "
                                        "tokens (the oracle/ C restatement of the reference's "
@@ -340,12 +379,14 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--impl", choices=["magma", "reference"], default="magma")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the standalone LayerNorm / attention / MLP configuration lines")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -368,7 +409,8 @@ def main() -> None:
     tr = GPTTrainer(cfg, B, "bf16", lr=OPT["lr"], beta1=OPT["beta1"], beta2=OPT["beta2"],
                     weight_decay=OPT["wd"], seed=0, grad_clip=OPT["clip"],
                     lr_schedule=(OPT["warmup"], OPT["total"], OPT["min_lr"]))
-    sync = dp.GradSync()
+    # the gradient all-reduce goes through the library's C-ABI collectives
+    sync = dp.GradSync(comm=dp.Comm.from_process_group() if world > 1 else None)
     gen = torch.Generator().manual_seed(1234 + rank)
     tok_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()
     tgt_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()
@@ -459,9 +501,16 @@ def main() -> None:
     others = {k: entry(k, b) for k, b in (("attention_fwd", "tensor"), ("attention_bwd", "tensor"),
                                            ("layernorm", "hbm"), ("adam", "hbm"),
                                            ("cross_entropy", "hbm"))}
+    # FLOPs of one step: every GEMM and attention call of the instrumented step
+    step_flops = sum(kinds[k]["work"] for k in ("gemm", "attention_fwd", "attention_bwd")
+                     if k in kinds)
+    configs = None
+    if world == 1 and not args.no_configs:
+        configs = config_lines(peaks)
     if rank != 0:
         if world > 1:
             dist.barrier()
+            sync.close()
             dist.destroy_process_group()
         return
     cpu = None
@@ -480,11 +529,14 @@ def main() -> None:
         "cpu_baseline": cpu,
         "gpu_launches": int(launches * args.steps),
         "clocks": clocks, "loss": round(loss_now, 4),
-        "mfu": round(6.54e12 / (ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+        "mfu": round(step_flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+        "flops_per_step": step_flops,
+        "configs": configs,
     }
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        sync.close()
         dist.destroy_process_group()
 
 

@@ -328,7 +328,9 @@ MAGMA_API magma_status_t magma_embedding_bwd(const int32_t* tokens, const float*
                                    void* stream);
 
 /* The same VJP with a fixed summation order: each token row of dwte gets the
- * rows that hold that token added one at a time in increasing row order, so
+ * rows that hold that token added one at a time in increasing row order
+ * (dwte accumulates; dwpe, if not NULL, is added to when accumulate_dwpe != 0
+ * and written otherwise), so
  * the result is identical on every run (the one-hot matmul of
  * Data.swift:890-907 reduces in an order the compiler picks; this order is the
  * plain sequential one). The rows are put in (token, row) order (1024-row
@@ -342,6 +344,7 @@ MAGMA_API magma_status_t magma_embedding_bwd_deterministic(const int32_t* tokens
                                                            const float* dout, float* dwte,
                                                            float* dwpe, int64_t batch,
                                                            int64_t seq, int64_t dim, int64_t vocab,
+                                                           int32_t accumulate_dwpe,
                                                            void* workspace,
                                                            int64_t workspace_bytes, void* stream);
 
@@ -367,6 +370,14 @@ MAGMA_API magma_status_t magma_cross_entropy_fwd_bwd_rowstats(void* logits, cons
 /* Deterministic sum of n F32 values into out[0] (e.g. the mean loss with
  * scale = 1/n). */
 MAGMA_API magma_status_t magma_reduce_sum(const float* x, float* out, int64_t n, float scale, void* stream);
+
+/* Mean-squared error as the reference's value-layer example writes it
+ * (Examples/ValueLayers/main.swift: r = pred - target; loss = sum(r*r) / n)
+ * and its VJP (Autodiff.swift: divide, sum and multiply pullbacks):
+ * loss[0] = sum_i (pred_i - target_i)^2 / divisor and, if dpred is not NULL,
+ * dpred_i = v*r_i + v*r_i with v = 1/divisor. F32, n elements. */
+MAGMA_API magma_status_t magma_mse_fwd_bwd(const float* pred, const float* target, float* dpred,
+                                           float* loss, int64_t n, float divisor, void* stream);
 
 /* GELU (tanh form, StableHLOEmitter.swift:804-816) and its VJP
  * (Autodiff.swift:401-418), element-wise; dtype F32 or BF16. */
@@ -394,6 +405,71 @@ MAGMA_API magma_status_t magma_convert(const void* src, void* dst, int64_t n,
 /* y = y * alpha (F32), e.g. the 1/n of allReduceMean (MLIRBuilder.swift:923-929)
  * applied after a sum all-reduce. */
 MAGMA_API magma_status_t magma_scale(float* y, int64_t n, float alpha, void* stream);
+
+/* ---- collectives (data-parallel exchange) -----------------------------------
+ * The reference's replicated step crosses its C shim at PJRT_ExecuteMultiDevice
+ * (Sources/CXLARuntime/PJRTSimpleWrapper.c:1412), with the gradient mean traced
+ * as crossReplicaMean (Sources/Core/Distributed.swift:59-64) and lowered to
+ * all_reduce(add) then a multiply by 1/n (MLIRBuilder.swift:923-929). These
+ * entry points are that exchange over NCCL: one communicator per GPU, the
+ * collective enqueued on the caller's stream. NCCL is opened at run time
+ * (libnccl.so.2); without it every call returns MAGMA_UNAVAILABLE.
+ * Communicators are non-blocking: initialisation and each enqueue wait at most
+ * a bounded time for the other ranks (timeout_ms, or 120 s), then abort the
+ * communicator and return MAGMA_DEADLINE_EXCEEDED. */
+#define MAGMA_COMM_ID_BYTES 128
+#define MAGMA_REDUCE_SUM 0
+#define MAGMA_REDUCE_MAX 1
+#define MAGMA_REDUCE_MIN 2
+#define MAGMA_REDUCE_AVG 3
+
+/* A new communicator id (rank 0 makes it; the caller hands the bytes to the
+ * other ranks over its own channel). id: at least MAGMA_COMM_ID_BYTES bytes. */
+MAGMA_API magma_status_t magma_comm_unique_id(uint8_t* id, size_t bytes);
+/* Joins rank `rank` of `nranks` on the current device (one process or thread
+ * per GPU). timeout_ms <= 0 means 120 s. */
+MAGMA_API magma_status_t magma_comm_init_rank(void** comm, int32_t nranks, int32_t rank,
+                                              const uint8_t* id, int64_t timeout_ms);
+/* One communicator per listed device, all in this process (devices may be
+ * NULL for 0..ndev-1); comms receives ndev handles. */
+MAGMA_API magma_status_t magma_comm_init_all(int32_t ndev, const int32_t* devices, void** comms);
+MAGMA_API magma_status_t magma_comm_destroy(void* comm);
+/* Ends a communicator without waiting for its peers (after a failure). */
+MAGMA_API magma_status_t magma_comm_abort(void* comm);
+MAGMA_API magma_status_t magma_comm_size(void* comm, int32_t* nranks);
+MAGMA_API magma_status_t magma_comm_rank(void* comm, int32_t* rank);
+/* MAGMA_OK while the communicator is healthy; an error status (with the NCCL
+ * reason in the last-error message) once it has failed, e.g. after a peer
+ * died. Host-side; does not wait. */
+MAGMA_API magma_status_t magma_comm_check(void* comm);
+/* recv = reduce over ranks of send, count elements (in place when send ==
+ * recv). op: MAGMA_REDUCE_*. dtype F32, BF16, S32 or S64. */
+MAGMA_API magma_status_t magma_allreduce(const void* send, void* recv, int64_t count,
+                                         magma_dtype_t dtype, int32_t op, void* comm,
+                                         void* stream);
+/* recv (recv_count elements) = this rank's block of the reduction of send
+ * (nranks * recv_count elements, rank r owning [r*recv_count, (r+1)*recv_count)). */
+MAGMA_API magma_status_t magma_reduce_scatter(const void* send, void* recv, int64_t recv_count,
+                                              magma_dtype_t dtype, int32_t op, void* comm,
+                                              void* stream);
+/* recv (nranks * send_count elements) = every rank's send, in rank order. */
+MAGMA_API magma_status_t magma_all_gather(const void* send, void* recv, int64_t send_count,
+                                          magma_dtype_t dtype, void* comm, void* stream);
+/* Brackets several collectives (e.g. one per device of magma_comm_init_all
+ * from one thread) so that they are issued together. */
+MAGMA_API magma_status_t magma_group_start(void);
+MAGMA_API magma_status_t magma_group_end(void);
+
+/* ---- events (ordering between streams, device timing) ---------------------- */
+MAGMA_API magma_status_t magma_event_create(void** event, int32_t enable_timing);
+MAGMA_API magma_status_t magma_event_destroy(void* event);
+MAGMA_API magma_status_t magma_event_record(void* event, void* stream);
+/* Work queued on `stream` after this call waits for the event. */
+MAGMA_API magma_status_t magma_stream_wait_event(void* stream, void* event);
+MAGMA_API magma_status_t magma_event_synchronize(void* event);
+/* *done = 1 once the work before the event has finished, else 0. */
+MAGMA_API magma_status_t magma_event_query(void* event, int32_t* done);
+MAGMA_API magma_status_t magma_event_elapsed_ms(void* start, void* end, float* ms);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -1,11 +1,14 @@
 """Per-kernel micro-benchmarks at the GPT-2-small training-step shapes.
 
-    python -m magma_b200.kernel_bench [all|gemm|attention|layernorm|adam|ce] [name] [--reps N]
+    python -m magma_b200.kernel_bench [all|gemm|attention|layernorm|adam|ce|configs] [name] [--reps N]
 
 Times each library call standalone with CUDA events after warm-up and prints
 one JSON object per kernel: duration and achieved TFLOP/s (contractions) or
 GB/s (memory-bound kernels, algorithmic bytes). ``name`` restricts the GEMM
-set to one shape (e.g. ``fc_fwd``) — handy under a profiler.
+set to one shape (e.g. ``fc_fwd``) — handy under a profiler. ``configs`` times
+the standalone benchmark configurations: LayerNorm F32 at [8192, 768] and
+causal attention at [8, 12, 1024, 64] in BF16 and F32, each cycling through
+buffer sets larger than L2.
 """
 from __future__ import annotations
 
@@ -163,6 +166,102 @@ def bench_ce(reps: int) -> list[dict]:
     return out
 
 
+def _time_rotating(fns, reps: int) -> float:
+    """Mean device time of one call when `reps` calls cycle through `fns` (one
+    closure per buffer set, the sets together larger than the 126 MB L2, so
+    every call reads its inputs from HBM)."""
+    return _time(_cycler(fns), reps)
+
+
+def _cycler(fns):
+    state = {"i": 0}
+
+    def run():
+        fns[state["i"] % len(fns)]()
+        state["i"] += 1
+    return run
+
+
+def bench_layernorm_f32(reps: int, rows: int = 8192, dim: int = 768, sets: int = 6) -> dict:
+    """LayerNorm forward + backward, F32 in and out, [rows, dim]: x ~ N(0,1),
+    gamma ~ N(1, 0.02), beta ~ N(0, 0.02), dy ~ N(0,1). Algorithmic bytes: the
+    forward reads x and writes y, the backward reads x and dy and writes dx
+    (4 bytes each), plus the per-row statistics and the per-column vectors."""
+    bufs = []
+    for _ in range(sets):
+        x = torch.randn((rows, dim), device="cuda")
+        g = 1 + 0.02 * torch.randn(dim, device="cuda")
+        b = 0.02 * torch.randn(dim, device="cuda")
+        dy = torch.randn((rows, dim), device="cuda")
+        y = torch.empty_like(x)
+        dx = torch.empty_like(x)
+        mean = torch.empty(rows, device="cuda")
+        rstd = torch.empty(rows, device="cuda")
+        dg = torch.empty(dim, device="cuda")
+        db = torch.empty(dim, device="cuda")
+        bufs.append((x, g, b, dy, y, dx, mean, rstd, dg, db))
+    ws = ops.workspace(lib.query("magma_layernorm_bwd_workspace_size", rows, dim))
+    st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+
+    def fwd(bs):
+        x, g, b, dy, y, dx, mean, rstd, dg, db = bs
+        lib.call("magma_layernorm_fwd", x.data_ptr(), g.data_ptr(), b.data_ptr(), y.data_ptr(),
+                 mean.data_ptr(), rstd.data_ptr(), rows, dim, 1e-5, lib.F32, lib.F32, st())
+
+    def bwd(bs):
+        x, g, b, dy, y, dx, mean, rstd, dg, db = bs
+        lib.call("magma_layernorm_bwd", dy.data_ptr(), x.data_ptr(), g.data_ptr(),
+                 mean.data_ptr(), rstd.data_ptr(), dx.data_ptr(), dg.data_ptr(), db.data_ptr(),
+                 rows, dim, lib.F32, lib.F32, lib.F32, 0, 0, ws.data_ptr(), ws.numel(), st())
+
+    for bs in bufs:
+        fwd(bs)
+    f_ms = _time_rotating([lambda bs=bs: fwd(bs) for bs in bufs], reps)
+    b_ms = _time_rotating([lambda bs=bs: bwd(bs) for bs in bufs], reps)
+    fwd_bytes = rows * dim * 8 + rows * 8 + dim * 8
+    bwd_bytes = rows * dim * 12 + rows * 8 + dim * 12
+    return {"workload": f"LayerNorm fwd+bwd F32 [{rows}, {dim}]", "fwd_us": round(f_ms * 1e3, 2),
+            "bwd_us": round(b_ms * 1e3, 2), "us": round((f_ms + b_ms) * 1e3, 2),
+            "bytes": fwd_bytes + bwd_bytes,
+            "GBs": round((fwd_bytes + bwd_bytes) / (f_ms + b_ms) / 1e6, 1),
+            "l2": f"{sets} rotating buffer sets ({sets * rows * dim * 16 >> 20} MiB)"}
+
+
+def bench_attention_config(reps: int, dtype: torch.dtype, batch: int = 8, heads: int = 12,
+                           seq: int = 1024, hd: int = 64, sets: int = 4) -> dict:
+    """Causal attention forward + backward on contiguous [B, H, S, hd] tensors
+    (Q, K, V, dO ~ N(0,1), scale 1/sqrt(hd)). Work counted with the causal half:
+    forward 4*B*H*hd*S(S+1)/2 FLOPs, backward twice that."""
+    shape = (batch, heads, seq, hd)
+    bufs = []
+    for _ in range(sets):
+        q, k, v, do = (torch.randn(shape, device="cuda").to(dtype) for _ in range(4))
+        o, lse = ops.attention_fwd(q, k, v, hd ** -0.5, True)
+        dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+        bufs.append((q, k, v, do, o, lse, dq, dk, dv))
+    scale = hd ** -0.5
+
+    def fwd(bs):
+        q, k, v, do, o, lse, dq, dk, dv = bs
+        ops.attention_fwd(q, k, v, scale, True, out=o)
+
+    def bwd(bs):
+        q, k, v, do, o, lse, dq, dk, dv = bs
+        ops.attention_bwd(q, k, v, o, do, lse, scale, True, dq, dk, dv)
+
+    f_ms = _time_rotating([lambda bs=bs: fwd(bs) for bs in bufs], reps)
+    b_ms = _time_rotating([lambda bs=bs: bwd(bs) for bs in bufs], reps)
+    flops = 4.0 * batch * heads * hd * seq * (seq + 1) / 2
+    name = "bf16" if dtype == torch.bfloat16 else "f32"
+    return {"workload": f"causal attention fwd+bwd {name} [{batch}, {heads}, {seq}, {hd}]",
+            "fwd_us": round(f_ms * 1e3, 2), "bwd_us": round(b_ms * 1e3, 2),
+            "us": round((f_ms + b_ms) * 1e3, 2), "flops": 3 * flops,
+            "fwd_tflops": round(flops / f_ms / 1e9, 1),
+            "bwd_tflops": round(2 * flops / b_ms / 1e9, 1),
+            "tflops": round(3 * flops / (f_ms + b_ms) / 1e9, 1),
+            "l2": f"{sets} rotating buffer sets"}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", nargs="?", default="all")
@@ -182,6 +281,9 @@ def main(argv=None) -> None:
         res += bench_adam(a.reps)
     if a.what in ("all", "ce"):
         res += bench_ce(a.reps)
+    if a.what in ("all", "configs"):
+        res += [bench_layernorm_f32(a.reps), bench_attention_config(a.reps, torch.bfloat16),
+                bench_attention_config(max(2, a.reps // 10), torch.float32)]
     for r in res:
         print(json.dumps(r), flush=True)
 

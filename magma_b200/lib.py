@@ -40,6 +40,13 @@ S64 = 4
 F32 = 10
 BF16 = 12
 
+# reductions of the collectives
+REDUCE_SUM = 0
+REDUCE_MAX = 1
+REDUCE_MIN = 2
+REDUCE_AVG = 3
+COMM_ID_BYTES = 128
+
 # GEMM epilogues
 EPI_NONE = 0
 EPI_BIAS = 1
@@ -114,12 +121,13 @@ SIGNATURES = {
     "magma_embedding_fwd": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "magma_embedding_bwd": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "magma_embedding_bwd_workspace_size": (_i64, [_i64, _i64]),
-    "magma_embedding_bwd_deterministic": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp,
-                                                 _i64, _vp]),
+    "magma_embedding_bwd_deterministic": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32,
+                                                 _vp, _i64, _vp]),
     "magma_cross_entropy_fwd_bwd": (None, [_vp, _vp, _vp, _i64, _i64, _i64, _f, _i32, _vp]),
     "magma_cross_entropy_fwd_bwd_rowstats": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f,
                                                     _i32, _vp]),
     "magma_reduce_sum": (None, [_vp, _vp, _i64, _f, _vp]),
+    "magma_mse_fwd_bwd": (None, [_vp, _vp, _vp, _vp, _i64, _f, _vp]),
     "magma_gelu_fwd": (None, [_vp, _vp, _i64, _i32, _vp]),
     "magma_gelu_bwd": (None, [_vp, _vp, _vp, _i64, _i32, _vp]),
     "magma_relu_fwd": (None, [_vp, _vp, _i64, _i32, _vp]),
@@ -127,6 +135,26 @@ SIGNATURES = {
     "magma_bias_grad_workspace_size": (_sz, [_i64, _i64]),
     "magma_bias_grad": (None, [_vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _sz, _vp]),
     "magma_convert": (None, [_vp, _vp, _i64, _i32, _i32, _vp]),
+    "magma_comm_unique_id": (None, [C.c_char_p, _sz]),
+    "magma_comm_init_rank": (None, [C.POINTER(_vp), _i32, _i32, C.c_char_p, _i64]),
+    "magma_comm_init_all": (None, [_i32, C.POINTER(_i32), C.POINTER(_vp)]),
+    "magma_comm_destroy": (None, [_vp]),
+    "magma_comm_abort": (None, [_vp]),
+    "magma_comm_size": (None, [_vp, C.POINTER(_i32)]),
+    "magma_comm_rank": (None, [_vp, C.POINTER(_i32)]),
+    "magma_comm_check": (None, [_vp]),
+    "magma_allreduce": (None, [_vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+    "magma_reduce_scatter": (None, [_vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+    "magma_all_gather": (None, [_vp, _vp, _i64, _i32, _vp, _vp]),
+    "magma_group_start": (None, []),
+    "magma_group_end": (None, []),
+    "magma_event_create": (None, [C.POINTER(_vp), _i32]),
+    "magma_event_destroy": (None, [_vp]),
+    "magma_event_record": (None, [_vp, _vp]),
+    "magma_stream_wait_event": (None, [_vp, _vp]),
+    "magma_event_synchronize": (None, [_vp]),
+    "magma_event_query": (None, [_vp, C.POINTER(_i32)]),
+    "magma_event_elapsed_ms": (None, [_vp, _vp, C.POINTER(_f)]),
     "magma_scale": (None, [_vp, _i64, _f, _vp]),
 }
 
@@ -142,7 +170,9 @@ KERNELS_PER_CALL = {
     "magma_cross_entropy_fwd_bwd": 1,
     "magma_cross_entropy_fwd_bwd_rowstats": 1, "magma_reduce_sum": 1, "magma_gelu_fwd": 1,
     "magma_gelu_bwd": 1, "magma_relu_fwd": 1, "magma_relu_bwd": 1, "magma_bias_grad": 2,
-    "magma_convert": 1, "magma_scale": 1,
+    "magma_convert": 1, "magma_scale": 1, "magma_mse_fwd_bwd": 1, "magma_memset": 0,
+    # collectives run NCCL's kernels, not this library's
+    "magma_allreduce": 0, "magma_reduce_scatter": 0, "magma_all_gather": 0,
 }
 
 _lib = None

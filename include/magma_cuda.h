@@ -287,6 +287,18 @@ MAGMA_API magma_status_t magma_grad_norm(const float* grads, int64_t n, float gr
                                          float* norm, void* workspace, int64_t workspace_bytes,
                                          void* stream);
 
+/* The pieces of magma_grad_norm for a gradient sharded over ranks: each rank
+ * writes the sum of squares of its (scaled) part to a device scalar
+ * (magma_grad_sumsq, same workspace as magma_grad_norm), the ranks gather
+ * those scalars (magma_all_gather), and magma_grad_norm_combine adds `count`
+ * of them in index order and takes the square root, so every rank computes the
+ * same norm. */
+MAGMA_API magma_status_t magma_grad_sumsq(const float* grads, int64_t n, float grad_scale,
+                                          float* sumsq, void* workspace, int64_t workspace_bytes,
+                                          void* stream);
+MAGMA_API magma_status_t magma_grad_norm_combine(const float* sumsq, int64_t count, float* norm,
+                                                 void* stream);
+
 /* Adam with global-norm clipping fused in front (clipGradNorm's scaling,
  * Optimizer.swift:1249-1267, then optim.Adam.step, :354-412): with
  * c = max_norm / (norm + 1e-6) if that is below 1, else 1 (also 1 for a NaN

@@ -210,14 +210,24 @@ grad_sumsq_partial(const float* __restrict__ g, int64_t n, float scale, int vec,
   if (threadIdx.x == 0) partial[blockIdx.x] = t;
 }
 
-// norm[0] = sqrt(sum of the partials), summed in block order.
+// norm[0] = sqrt(sum of the partials) (or the sum itself without SQRT),
+// summed in block order.
+template <bool SQRT>
 __global__ void __launch_bounds__(kNormThreads)
 grad_norm_finish(const float* __restrict__ partial, int nb, float* __restrict__ norm) {
   __shared__ float red[kNormThreads / 32];
   float acc = 0.f;
   for (int i = threadIdx.x; i < nb; i += blockDim.x) acc += partial[i];
   const float t = block_sum(acc, red);
-  if (threadIdx.x == 0) norm[0] = __fsqrt_rn(t);
+  if (threadIdx.x == 0) norm[0] = SQRT ? __fsqrt_rn(t) : t;
+}
+
+// norm[0] = sqrt(sumsq[0] + sumsq[1] + ...), added in index order by one thread.
+__global__ void grad_norm_combine(const float* __restrict__ sumsq, int64_t count,
+                                  float* __restrict__ norm) {
+  float t = 0.f;
+  for (int64_t i = 0; i < count; ++i) t += sumsq[i];
+  norm[0] = __fsqrt_rn(t);
 }
 
 int64_t norm_blocks(int64_t n) {
@@ -242,6 +252,29 @@ magma_status_t launch_adam(float* params, const float* grads, float* m, float* v
     adam_scalar<<<(int)blocks, threads, 0, cs>>>(params, grads, m, v,
                                                  (__nv_bfloat16*)shadow_bf16, n, s);
   return check_launch("adam_step");
+}
+
+template <bool SQRT>
+magma_status_t grad_norm_impl(const char* fn, const float* grads, int64_t n, float grad_scale,
+                              float* norm, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
+  MAGMA_REQUIRE(n >= 0, "%s: negative size", fn);
+  MAGMA_REQUIRE(norm != nullptr, "%s: NULL output", fn);
+  cudaStream_t cs = (cudaStream_t)stream;
+  if (n == 0) return cuda_status(cudaMemsetAsync(norm, 0, sizeof(float), cs), "grad_norm memset");
+  MAGMA_REQUIRE(grads != nullptr, "%s: NULL grads", fn);
+  const int64_t nb = norm_blocks(n);
+  MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= 4 * nb,
+                "%s: workspace of %lld bytes needed (magma_grad_norm_workspace_size)", fn,
+                (long long)(4 * nb));
+  MAGMA_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 3u) == 0,
+                "%s: workspace must be 4-byte aligned", fn);
+  float* partial = static_cast<float*>(workspace);
+  grad_sumsq_partial<<<(int)nb, kNormThreads, 0, cs>>>(grads, n, grad_scale,
+                                                       aligned16(grads) ? 1 : 0, partial);
+  if (magma_status_t st = check_launch("grad_sumsq_partial")) return st;
+  grad_norm_finish<SQRT><<<1, kNormThreads, 0, cs>>>(partial, (int)nb, norm);
+  return check_launch("grad_norm_finish");
 }
 
 }  // namespace
@@ -270,23 +303,22 @@ int64_t magma_grad_norm_workspace_size(int64_t n) {
 
 magma_status_t magma_grad_norm(const float* grads, int64_t n, float grad_scale, float* norm,
                                void* workspace, int64_t workspace_bytes, void* stream) {
-  MAGMA_REQUIRE(n >= 0, "magma_grad_norm: negative size");
-  MAGMA_REQUIRE(norm != nullptr, "magma_grad_norm: NULL norm");
-  cudaStream_t cs = (cudaStream_t)stream;
-  if (n == 0) return cuda_status(cudaMemsetAsync(norm, 0, sizeof(float), cs), "grad_norm memset");
-  MAGMA_REQUIRE(grads != nullptr, "magma_grad_norm: NULL grads");
-  const int64_t nb = norm_blocks(n);
-  MAGMA_REQUIRE(workspace != nullptr && workspace_bytes >= 4 * nb,
-                "magma_grad_norm: workspace of %lld bytes needed (magma_grad_norm_workspace_size)",
-                (long long)(4 * nb));
-  MAGMA_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 3u) == 0,
-                "magma_grad_norm: workspace must be 4-byte aligned");
-  float* partial = static_cast<float*>(workspace);
-  grad_sumsq_partial<<<(int)nb, kNormThreads, 0, cs>>>(grads, n, grad_scale,
-                                                       aligned16(grads) ? 1 : 0, partial);
-  if (magma_status_t st = check_launch("grad_sumsq_partial")) return st;
-  grad_norm_finish<<<1, kNormThreads, 0, cs>>>(partial, (int)nb, norm);
-  return check_launch("grad_norm_finish");
+  return grad_norm_impl<true>("magma_grad_norm", grads, n, grad_scale, norm, workspace,
+                              workspace_bytes, stream);
+}
+
+magma_status_t magma_grad_sumsq(const float* grads, int64_t n, float grad_scale, float* sumsq,
+                                void* workspace, int64_t workspace_bytes, void* stream) {
+  return grad_norm_impl<false>("magma_grad_sumsq", grads, n, grad_scale, sumsq, workspace,
+                               workspace_bytes, stream);
+}
+
+magma_status_t magma_grad_norm_combine(const float* sumsq, int64_t count, float* norm,
+                                       void* stream) {
+  MAGMA_REQUIRE(count >= 1 && sumsq != nullptr && norm != nullptr,
+                "magma_grad_norm_combine: bad arguments");
+  grad_norm_combine<<<1, 1, 0, (cudaStream_t)stream>>>(sumsq, count, norm);
+  return check_launch("grad_norm_combine");
 }
 
 magma_status_t magma_adam_step_clipped(float* params, const float* grads, float* m, float* v,

@@ -90,15 +90,21 @@ __device__ __forceinline__ float epi_value(const EpiArgs& e, const TC* C, int64_
 // ============================== F32 FFMA kernel ==============================
 constexpr int kSimtBM = 128, kSimtBN = 128, kSimtBK = 8;
 
+// K-split form (ws != nullptr): block z computes the K range [z*kps, (z+1)*kps)
+// and stores its raw F32 sums to plane z of ws ([splits][M][N]); the planes
+// are added in split order by splitk_reduce, which applies the epilogue.
 template <typename TA, typename TC, bool TA_T, bool TB_T>
 __global__ void __launch_bounds__(256)
 gemm_simt_kernel(const TA* __restrict__ A, const TA* __restrict__ B, TC* __restrict__ C,
-                 int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, EpiArgs e) {
+                 int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, EpiArgs e,
+                 int64_t kps, float* __restrict__ ws) {
   __shared__ float As[2][kSimtBK][kSimtBM + 4];
   __shared__ float Bs[2][kSimtBK][kSimtBN + 4];
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
   const int64_t m0 = (int64_t)blockIdx.y * kSimtBM, n0 = (int64_t)blockIdx.x * kSimtBN;
+  const int64_t kbeg = (int64_t)blockIdx.z * kps;
+  const int64_t kend = kbeg + kps < K ? kbeg + kps : K;
   float acc[8][8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -112,12 +118,12 @@ gemm_simt_kernel(const TA* __restrict__ A, const TA* __restrict__ B, TC* __restr
       int mm, kk;
       if (!TA_T) { mm = idx >> 3; kk = idx & 7; } else { kk = idx >> 7; mm = idx & 127; }
       int64_t gm = m0 + mm, gk = k0 + kk;
-      ra[i] = (gm < M && gk < K) ? to_f32(TA_T ? A[gk * lda + gm] : A[gm * lda + gk]) : 0.f;
+      ra[i] = (gm < M && gk < kend) ? to_f32(TA_T ? A[gk * lda + gm] : A[gm * lda + gk]) : 0.f;
       int nn;
       if (!TB_T) { kk = idx >> 7; nn = idx & 127; } else { nn = idx >> 3; kk = idx & 7; }
       int64_t gn = n0 + nn;
       gk = k0 + kk;
-      rb[i] = (gn < N && gk < K) ? to_f32(TB_T ? B[gn * ldb + gk] : B[gk * ldb + gn]) : 0.f;
+      rb[i] = (gn < N && gk < kend) ? to_f32(TB_T ? B[gn * ldb + gk] : B[gk * ldb + gn]) : 0.f;
     }
   };
   auto store_tiles = [&](int buf) {
@@ -132,15 +138,15 @@ gemm_simt_kernel(const TA* __restrict__ A, const TA* __restrict__ B, TC* __restr
       Bs[buf][kk][nn] = rb[i];
     }
   };
-  const int64_t ktiles = (K + kSimtBK - 1) / kSimtBK;
+  const int64_t ktiles = kend > kbeg ? (kend - kbeg + kSimtBK - 1) / kSimtBK : 0;
   if (ktiles > 0) {
-    load_tiles(0);
+    load_tiles(kbeg);
     store_tiles(0);
   }
   __syncthreads();
   for (int64_t kt = 0; kt < ktiles; ++kt) {
     const int buf = kt & 1;
-    if (kt + 1 < ktiles) load_tiles((kt + 1) * kSimtBK);
+    if (kt + 1 < ktiles) load_tiles(kbeg + (kt + 1) * kSimtBK);
 #pragma unroll
     for (int k = 0; k < kSimtBK; ++k) {
       float a[8], b[8];
@@ -168,6 +174,10 @@ gemm_simt_kernel(const TA* __restrict__ A, const TA* __restrict__ B, TC* __restr
     for (int j = 0; j < 8; ++j) {
       int64_t col = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
       if (col >= N) continue;
+      if (ws != nullptr) {
+        ws[((int64_t)blockIdx.z * M + row) * N + col] = acc[i][j];
+        continue;
+      }
       int64_t off = row * e.ldc + col;
       C[off] = from_f32<TC>(epi_value<TC>(e, C, off, col, acc[i][j]));
     }
@@ -1431,19 +1441,61 @@ magma_status_t dispatch_plan(const TcPlan& plan, const void* a, const void* b, i
                         : dispatch_major<128, TC, false>(a, b, M, N, K, lda, ldb, ta, tb, args, s);
 }
 
+// K splits of the F32 kernel: when its output tiles fill under half of the
+// SMs and K is long, the K loop is cut into up to 16 chunks of whole 64-deep
+// blocks (so that every SM-limited, latency-bound chain is shorter).
+int simt_splits(int64_t M, int64_t N, int64_t K, int64_t* kps) {
+  const int64_t tiles = ceil_div(N, kSimtBN) * ceil_div(M, kSimtBM);
+  *kps = K;
+  if (tiles * 2 > num_sms() || K < 256) return 1;
+  int64_t sp = ceil_div(num_sms(), tiles);
+  if (sp > 16) sp = 16;
+  if (sp > K / 64) sp = K / 64;
+  if (sp < 2) return 1;
+  *kps = ceil_div(ceil_div(K, sp), 64) * 64;
+  return (int)ceil_div(K, *kps);
+}
+
+size_t simt_workspace(int64_t M, int64_t N, int64_t K) {
+  int64_t kps;
+  const int sp = simt_splits(M, N, K, &kps);
+  return sp > 1 ? (size_t)sp * M * N * sizeof(float) : 0;
+}
+
 template <typename TA, typename TC>
 magma_status_t launch_simt(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K,
                            int64_t lda, int64_t ldb, int ta, int tb, const EpiArgs& e,
-                           cudaStream_t s) {
-  dim3 grid((unsigned)ceil_div(N, kSimtBN), (unsigned)ceil_div(M, kSimtBM));
+                           void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  int64_t kps = K;
+  int splits = simt_splits(M, N, K, &kps);
+  if (splits > 1 && (workspace == nullptr || !aligned16(workspace) ||
+                     workspace_bytes < (size_t)splits * M * N * sizeof(float))) {
+    splits = 1;
+    kps = K;
+  }
+  float* ws = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  dim3 grid((unsigned)ceil_div(N, kSimtBN), (unsigned)ceil_div(M, kSimtBM), (unsigned)splits);
   const TA* A = (const TA*)a;
   const TA* B = (const TA*)b;
   TC* C = (TC*)c;
-  if (!ta && !tb) gemm_simt_kernel<TA, TC, false, false><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
-  else if (!ta && tb) gemm_simt_kernel<TA, TC, false, true><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
-  else if (ta && !tb) gemm_simt_kernel<TA, TC, true, false><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
-  else gemm_simt_kernel<TA, TC, true, true><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e);
-  return check_launch("gemm_f32");
+  if (!ta && !tb) gemm_simt_kernel<TA, TC, false, false><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e, kps, ws);
+  else if (!ta && tb) gemm_simt_kernel<TA, TC, false, true><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e, kps, ws);
+  else if (ta && !tb) gemm_simt_kernel<TA, TC, true, false><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e, kps, ws);
+  else gemm_simt_kernel<TA, TC, true, true><<<grid, 256, 0, s>>>(A, B, C, M, N, K, lda, ldb, e, kps, ws);
+  if (magma_status_t st = check_launch("gemm_f32")) return st;
+  if (splits > 1) {
+    const int64_t per_row = (N & 3) == 0 ? N / 4 : N;
+    int64_t gx = ceil_div(per_row, 256);
+    if (gx > 16) gx = 16;
+    int64_t gy = (8LL * num_sms() + gx - 1) / gx;
+    if (gy > M) gy = M;
+    if (gy > 65535) gy = 65535;
+    const int vec_c = (e.ldc % 4) == 0 && aligned16(c);
+    splitk_reduce<TC><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, s>>>(ws, splits, M, N, C, e,
+                                                                       vec_c);
+    return check_launch("gemm_f32_splitk_reduce");
+  }
+  return MAGMA_OK;
 }
 
 }  // namespace
@@ -1454,7 +1506,9 @@ using namespace magma;
 extern "C" {
 
 size_t magma_gemm_workspace_size(int64_t m, int64_t n, int64_t k, magma_dtype_t ab_dtype) {
-  if (ab_dtype != MAGMA_DTYPE_BF16 || m <= 0 || n <= 0 || k <= 0) return 0;
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  if (ab_dtype == MAGMA_DTYPE_F32) return simt_workspace(m, n, k);
+  if (ab_dtype != MAGMA_DTYPE_BF16) return 0;
   // The plan depends on the epilogue and output type, which this query does
   // not take: return the largest split workspace over the epilogue classes.
   static const int kEpis[] = {MAGMA_EPI_NONE, MAGMA_EPI_BIAS_RESIDUAL, MAGMA_EPI_BIAS_GELU,
@@ -1531,12 +1585,15 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
                 "magma_gemm: ROWSTATS needs the tensor-core path (16-byte aligned operands, "
                 "lda and ldb multiples of 8)");
   if (ab_dtype == MAGMA_DTYPE_F32)
-    return c32 ? launch_simt<float, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e, s)
+    return c32 ? launch_simt<float, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e,
+                                           workspace, workspace_bytes, s)
                : launch_simt<float, __nv_bfloat16>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b,
-                                                   e, s);
-  return c32 ? launch_simt<__nv_bfloat16, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e, s)
+                                                   e, workspace, workspace_bytes, s);
+  return c32 ? launch_simt<__nv_bfloat16, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e,
+                                                 workspace, workspace_bytes, s)
              : launch_simt<__nv_bfloat16, __nv_bfloat16>(a, b, c, m, n, k, lda, ldb, trans_a,
-                                                         trans_b, e, s);
+                                                         trans_b, e, workspace, workspace_bytes,
+                                                         s);
 }
 
 }  // extern "C"

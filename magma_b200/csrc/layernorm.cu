@@ -26,6 +26,7 @@
 // workspace, then over CTAs in CTA order by a second kernel. Other shapes use
 // scalar generic kernels.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -103,14 +104,20 @@ ln_fwd_stream(const TX* __restrict__ x, const float* __restrict__ gamma,
     }
   }
   __syncwarp();
-  float g[G][4], bt[G][4];
+  // gamma / beta of this lane's columns as packed F32 pairs
+  unsigned long long g2[G][2], b2[G][2];
 #pragma unroll
   for (int c = 0; c < G; ++c) {
     const int e = 128 * c + 4 * lane;
+    float gv[4] = {0.f, 0.f, 0.f, 0.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
     if (e < dim) {
-      load4(gamma + e, g[c]);
-      load4(beta + e, bt[c]);
+      load4(gamma + e, gv);
+      load4(beta + e, bv);
     }
+    g2[c][0] = f2_pack(gv[0], gv[1]);
+    g2[c][1] = f2_pack(gv[2], gv[3]);
+    b2[c][0] = f2_pack(bv[0], bv[1]);
+    b2[c][1] = f2_pack(bv[2], bv[3]);
   }
   for (int64_t j = 0; j < n; ++j) {
     const int slot = (int)(j % kFwdRing);
@@ -120,11 +127,16 @@ ln_fwd_stream(const TX* __restrict__ x, const float* __restrict__ gamma,
       return;
     }
     const TX* src = reinterpret_cast<const TX*>(ring + slot * row_bytes);
-    float v[G][4];
+    // the row as packed pairs (columns 4l + 128c + {0,1} and {2,3}); zero
+    // past the end of a short row
+    unsigned long long v[G][2];
 #pragma unroll
     for (int c = 0; c < G; ++c) {
       const int e = 128 * c + 4 * lane;
-      if (e < dim) load4(src + e, v[c]);
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      if (e < dim) load4(src + e, t);
+      v[c][0] = f2_pack(t[0], t[1]);
+      v[c][1] = f2_pack(t[2], t[3]);
     }
     __syncwarp();
     if (lane == 0 && j + kFwdRing < n) {
@@ -133,31 +145,36 @@ ln_fwd_stream(const TX* __restrict__ x, const float* __restrict__ gamma,
       bulk_load(smem_u32(ring + slot * row_bytes), x + (row + kFwdRing * stride) * dim,
                 row_bytes, bar);
     }
-    float s = 0.f;
+    // sums on packed pairs (two running sums per lane, added at the end)
+    unsigned long long acc = f2_pack(0.f, 0.f);
 #pragma unroll
-    for (int c = 0; c < G; ++c)
-      if (128 * c + 4 * lane < dim)
+    for (int c = 0; c < G; ++c) acc = f2_add(acc, f2_add(v[c][0], v[c][1]));
+    float s0, s1;
+    f2_unpack(acc, s0, s1);
+    const float mean = __fdiv_rn(warp_sum(__fadd_rn(s0, s1)), (float)dim);
+    const unsigned long long mean2 = f2_pack(mean, mean);
+    unsigned long long sq = f2_pack(0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) s += v[c][i];
-    s = warp_sum(s);
-    const float mean = __fdiv_rn(s, (float)dim);
-    float ss = 0.f;
+    for (int c = 0; c < G; ++c) {
+      const bool live = 128 * c + 4 * lane < dim;
 #pragma unroll
-    for (int c = 0; c < G; ++c)
-      if (128 * c + 4 * lane < dim)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float d = __fsub_rn(v[c][i], mean);
-          v[c][i] = d;
-          ss += d * d;
-        }
-    ss = warp_sum(ss);
+      for (int i = 0; i < 2; ++i) {
+        const unsigned long long d = f2_sub(v[c][i], mean2);
+        v[c][i] = d;
+        if (live) sq = f2_fma(d, d, sq);
+      }
+    }
+    float q0, q1;
+    f2_unpack(sq, q0, q1);
+    const float ss = warp_sum(__fadd_rn(q0, q1));
     const float stdv = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps));
-    // (x - mean) / std per element as q = d * (1/std) with one residual
-    // correction (Markstein's method: r = RN(1/std), e = d - q*std exact by
+    // (x - mean) / std per element as q = d * RN(1/std); for an F32 output one
+    // residual correction follows (Markstein's method: e = d - q*std exact by
     // FMA, q' = q + e*r), which gives the correctly rounded quotient of the
-    // reference's divide in all but rare one-ulp cases, on the FMA pipe.
+    // reference's divide in all but rare one-ulp cases. A BF16 output keeps q:
+    // the one-ulp F32 difference is far below the BF16 rounding step.
     const float rinv = __frcp_rn(stdv);
+    const unsigned long long r2 = f2_pack(rinv, rinv), ns2 = f2_pack(-stdv, -stdv);
     TY* yr = y + row * dim;
 #pragma unroll
     for (int c = 0; c < G; ++c) {
@@ -165,10 +182,10 @@ ln_fwd_stream(const TX* __restrict__ x, const float* __restrict__ gamma,
       if (e < dim) {
         float o[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float q = __fmul_rn(v[c][i], rinv);
-          const float q2 = __fmaf_rn(__fmaf_rn(-q, stdv, v[c][i]), rinv, q);
-          o[i] = __fadd_rn(__fmul_rn(q2, g[c][i]), bt[c][i]);
+        for (int i = 0; i < 2; ++i) {
+          unsigned long long q = f2_mul(v[c][i], r2);
+          if (std::is_same<TY, float>::value) q = f2_fma(f2_fma(q, ns2, v[c][i]), r2, q);
+          f2_unpack(f2_add(f2_mul(q, g2[c][i]), b2[c][i]), o[2 * i], o[2 * i + 1]);
         }
         store4(yr + e, o);
       }

@@ -211,6 +211,53 @@ class GradSync:
             self.comm = None
 
 
+class ShardSync:
+    """The exchange of sharded data parallelism (ZeRO stage 1) over a Comm:
+    each finished gradient range is reduce-scattered in place (rank r keeps the
+    sum of block r of the range; the range's length must split evenly), on a
+    communication stream that overlaps the rest of the backward like
+    GradSync's all-reduce; after the sharded Adam step, gather_range
+    all-gathers each range of the updated parameters in place."""
+
+    def __init__(self, comm: Comm):
+        self.comm, self.world, self.rank = comm, comm.world, comm.rank
+        self._stream = None
+        self._ready = self._done = None
+        self._pending = False
+
+    def owned(self, lo: int, hi: int) -> tuple[int, int]:
+        """This rank's slice [a, b) of the arena range [lo, hi)."""
+        n = hi - lo
+        if n % (4 * self.world):
+            raise ValueError(f"range of {n} elements does not split into {self.world} slices "
+                             "of whole 16-byte groups")
+        per = n // self.world
+        return lo + self.rank * per, lo + (self.rank + 1) * per
+
+    def launch(self, grads: torch.Tensor) -> None:
+        """Reduce-scatters one finished range (a 1-D view of the arena) in place."""
+        if self._stream is None:
+            self._stream = torch.cuda.Stream(grads.device)
+            self._ready, self._done = _Event(), _Event()
+        self._ready.record(_stream(grads))
+        self._ready.wait(self._stream.cuda_stream)
+        per = grads.numel() // self.world
+        self.comm.reduce_scatter(grads, grads[self.rank * per:(self.rank + 1) * per],
+                                 stream=self._stream.cuda_stream)
+        self._pending = True
+
+    def finish(self) -> float:
+        if self._pending:
+            self._done.record(self._stream.cuda_stream)
+            self._done.wait(torch.cuda.current_stream(self._stream.device).cuda_stream)
+            self._pending = False
+        return 1.0 / self.world
+
+    def gather_range(self, arena: torch.Tensor, lo: int, hi: int, stream: int | None = None):
+        a, b = self.owned(lo, hi)
+        self.comm.all_gather(arena[a:b], arena[lo:hi], stream=stream)
+
+
 def shard_batch(global_tokens: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     """Rows [rank*b, (rank+1)*b) of a [world*b, S] batch (DistributedSampler's
     contiguous split, Data.swift:151-230)."""

@@ -339,7 +339,24 @@ class GPTTrainer:
         return lo, self.table[nxt][0]
 
     def _num_parts(self) -> int:
-        return (self.cfg.layers + self.SYNC_GROUP - 1) // self.SYNC_GROUP
+        return len(self.segment_ranges())
+
+    def segment_ranges(self) -> list[list[tuple[int, int]]]:
+        """Gradient-arena ranges that are final after each backward segment,
+        in the order the backward produces them: SYNC_GROUP layers at a time
+        from the top, then the rest with the embeddings and the final LN."""
+        L = self.cfg.layers
+        out = []
+        seg_top = L - 1
+        for l in reversed(range(L)):
+            # layers l .. seg_top are final (layer l-1's fcproj bias gradient,
+            # written at layer l, belongs to the next segment)
+            if (seg_top - l + 1 == self.SYNC_GROUP) and l > 0:
+                out.append([self._grad_range(l, seg_top)])
+                seg_top = l - 1
+        out.append([self._grad_range(0, seg_top), (0, self.table["h0.ln1_w"][0]),
+                     (self.table["lnf_w"][0], self.P)])
+        return out
 
     def _fwd_bwd_parts(self):
         """Forward + backward as a generator: after every SYNC_GROUP layers of
@@ -402,6 +419,8 @@ class GPTTrainer:
         self._ln_bwd(self.d_ln, self.x[L], self.view(P, "lnf_w"), self.lnf_stats[0],
                      self.lnf_stats[1], self.view(G, "lnf_w"), self.view(G, "lnf_b"),
                      self.view(G, f"h{L - 1}.fcproj_b"), accumulate=0)
+        segments = self.segment_ranges()
+        seg = 0
         seg_top = L - 1
         for l in reversed(range(L)):
             n = lambda k: f"h{l}.{k}"  # noqa: E731
@@ -445,7 +464,8 @@ class GPTTrainer:
             # layers l .. seg_top are final (layer l-1's fcproj bias gradient,
             # written just above, belongs to the next segment)
             if (seg_top - l + 1 == self.SYNC_GROUP) and l > 0:
-                yield [self._grad_range(l, seg_top)]
+                yield segments[seg]
+                seg += 1
                 seg_top = l - 1
         # embeddings: dwte += scatter(dresid) (tied: onto the lm-head
         # gradient; untied: onto zeros); dwpe = sum over the batch, written
@@ -455,8 +475,7 @@ class GPTTrainer:
         lib.call("magma_embedding_bwd_deterministic", _p(self.tokens), _p(self.dresid),
                  _p(self.view(G, "wte")), _p(self.view(G, "wpe")), self.B, cfg.seq, D, Vp, 0,
                  _p(self.emb_ws), self.emb_ws.numel() * 4, s)
-        yield [self._grad_range(0, seg_top), (0, self.table["h0.ln1_w"][0]),
-               (self.table["lnf_w"][0], self.P)]
+        yield segments[seg]
 
     def _dresid_operand(self) -> torch.Tensor:
         """The residual gradient as a GEMM operand: the BF16 copy the last
@@ -489,6 +508,48 @@ class GPTTrainer:
         lib.call("magma_adam_step_clipped", _p(self.params), _p(self.grads), _p(self.m),
                  _p(self.v), _p(self.shadow), self.P, lr, self.beta1, self.beta2, self.eps,
                  self.wd, self.t, grad_scale, _p(self.grad_norm), self.grad_clip, self._s())
+
+    def optimizer_step_sharded(self, sync) -> None:
+        """The optimiser step of sharded data parallelism (ZeRO stage 1) after a
+        backward whose finished ranges went through ``sync`` (a
+        dp.ShardSync: reduce-scatter in place, so this rank holds the summed
+        gradient of its slice of every range): the global norm from every
+        rank's sum of squares (gathered, added in rank order: the same on all
+        ranks), Adam on this rank's slices only, an in-place all-gather of the
+        updated F32 parameters, and the BF16 shadow rebuilt from them. The
+        1/world of the reference's mean is Adam's grad_scale, as in the
+        replicated step."""
+        lr = self.current_lr()
+        self.t += 1
+        s = self._s()
+        scale = 1.0 / sync.world
+        ranges = [r for seg in self.segment_ranges() for r in seg]
+        owned = [sync.owned(lo, hi) for lo, hi in ranges]
+        f4 = 4
+        P, G, M, V = (_p(t) for t in (self.params, self.grads, self.m, self.v))
+        if self.grad_clip is not None:
+            k = len(owned)
+            if getattr(self, "_sumsq", None) is None or self._sumsq.numel() < k * (sync.world + 1):
+                self._sumsq = torch.zeros(k * (sync.world + 1), dtype=torch.float32,
+                                          device=self.dev)
+            mine, every = self._sumsq[:k], self._sumsq[k:k * (sync.world + 1)]
+            for i, (a, b) in enumerate(owned):
+                lib.call("magma_grad_sumsq", G + a * f4, b - a, scale, mine.data_ptr() + 4 * i,
+                         _p(self.norm_ws), self.norm_ws.numel() * 4, s)
+            sync.comm.all_gather(mine, every, stream=s)
+            lib.call("magma_grad_norm_combine", _p(every), every.numel(), _p(self.grad_norm), s)
+        for a, b in owned:
+            if self.grad_clip is None:
+                lib.call("magma_adam_step", P + a * f4, G + a * f4, M + a * f4, V + a * f4, None,
+                         b - a, lr, self.beta1, self.beta2, self.eps, self.wd, self.t, scale, s)
+            else:
+                lib.call("magma_adam_step_clipped", P + a * f4, G + a * f4, M + a * f4,
+                         V + a * f4, None, b - a, lr, self.beta1, self.beta2, self.eps, self.wd,
+                         self.t, scale, _p(self.grad_norm), self.grad_clip, s)
+        for lo, hi in ranges:
+            sync.gather_range(self.params, lo, hi, stream=s)
+        if self.shadow is not None:
+            self._sync_shadow()
 
     # --------------------------------------------------------- checkpoints
     def save_checkpoint(self, path) -> None:

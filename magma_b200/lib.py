@@ -115,6 +115,8 @@ SIGNATURES = {
                                      _i64, _f, _vp]),
     "magma_grad_norm_workspace_size": (_i64, [_i64]),
     "magma_grad_norm": (None, [_vp, _i64, _f, _vp, _vp, _i64, _vp]),
+    "magma_grad_sumsq": (None, [_vp, _i64, _f, _vp, _vp, _i64, _vp]),
+    "magma_grad_norm_combine": (None, [_vp, _i64, _vp, _vp]),
     "magma_adam_step_clipped": (None, [_vp, _vp, _vp, _vp, _vp, _i64, _f, _f, _f, _f, _f, _i64,
                                        _f, _vp, _f, _vp]),
     "magma_lr_warmup_cosine": (None, [_f, _f, _i64, _i64, _i64, C.POINTER(_f)]),
@@ -173,6 +175,7 @@ KERNELS_PER_CALL = {
     "magma_convert": 1, "magma_scale": 1, "magma_mse_fwd_bwd": 1, "magma_memset": 0,
     # collectives run NCCL's kernels, not this library's
     "magma_allreduce": 0, "magma_reduce_scatter": 0, "magma_all_gather": 0,
+    "magma_grad_sumsq": 2, "magma_grad_norm_combine": 1,
 }
 
 _lib = None

@@ -161,7 +161,13 @@ class _Plan:
         wsb = max(lib.query("magma_bias_grad_workspace_size", rows, a.shape[1])
                   for a in self.acts[1:])
         self.ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
-        self.target = None
+        # K-split partials of the F32 GEMMs (forward, weight and input gradients)
+        wsg = 0
+        for lin in model.linears():
+            fi, fo = lin.shape
+            for m, n, k in ((rows, fo, fi), (fi, fo, rows), (rows, fi, fo)):
+                wsg = max(wsg, lib.query("magma_gemm_workspace_size", m, n, k, lib.F32))
+        self.gemm_ws = torch.empty(max(wsg, 256), dtype=torch.uint8, device=dev)
 
     def _s(self) -> int:
         return torch.cuda.current_stream(self.model.device).cuda_stream
@@ -169,7 +175,8 @@ class _Plan:
     def _gemm(self, a, b, c, m, n, k, lda, ldb, ldc, ta, tb, epi, bias=None, aux_in=None,
               aux_out=None):
         lib.call("magma_gemm", _p(a), _p(b), _p(c), m, n, k, lda, ldb, ldc, ta, tb, lib.F32,
-                 lib.F32, epi, _p(bias), _p(aux_in), _p(aux_out), None, 0, self._s())
+                 lib.F32, epi, _p(bias), _p(aux_in), _p(aux_out), _p(self.gemm_ws),
+                 self.gemm_ws.numel(), self._s())
 
     def forward(self, x: torch.Tensor | None = None) -> None:
         if x is not None:

@@ -64,11 +64,11 @@ def gemm_traffic_per_launch() -> int | None:
         return None
 
 
-def workload_config(world: int, batch: int) -> dict:
+def workload_config(world: int, batch: int, zero1: bool = False) -> dict:
     return {"workload": "GPT-2 small (124M: 12 layers, 12 heads, d_model 768, ctx 1024, vocab "
                         "50257, tied lm-head) BF16 train step, F32 master weights + Adam",
             "model": "gpt2-small-124M", "global_batch": batch * world, "seq_len": 1024,
-            "batch_per_gpu": batch, "parallelism": f"dp{world}",
+            "batch_per_gpu": batch, "parallelism": f"dp{world}" + (" zero1" if zero1 else ""),
             "l2": "no flush: each step streams >4 GB of weights and activations (L2 is 126 MB)"}
 
 
@@ -252,14 +252,61 @@ def config_lines(peaks: dict) -> dict:
         at.update(bound="tensor", peak=peaks["bf16_tflops"], unit="TFLOP/s",
                   frac=round(at["tflops"] / peaks["bf16_tflops"], 4),
                   peak_source="measured bf16_tflops (burst; kernels timed alone)")
+        if dt == "f32":  # the F32 path runs on the FFMA pipe, not the tensor cores
+            at.update(peak_ffma_nominal=FFMA_NOMINAL_TFLOPS,
+                      frac_ffma_nominal=round(at["tflops"] / FFMA_NOMINAL_TFLOPS, 4))
         out[name] = at
-    try:
-        from magma_b200 import mlp
+    from magma_b200 import mlp
 
-        out["mlp_f32"] = mlp.bench_step()
-    except ImportError:
-        pass
+    out["mlp_f32"] = mlp.bench_step()
+    out["char_gpt_f32"] = char_gpt_line()
     return out
+
+
+# F32 FFMA peak: 148 SMs x 128 FMA/clock x 2 FLOP x 1.965 GHz (nominal; the
+# pool measures no F32 figure)
+FFMA_NOMINAL_TFLOPS = 74.4
+
+
+def char_gpt_line(steps: int = 5, warmup: int = 2) -> dict:
+    """The char-level GPT training step in F32 at its configuration (vocab 65,
+    6 layers, 6 heads, d 384, ctx 256, batch 64 = 16384 tokens, Adam lr 3e-4),
+    forward+backward as CUDA graphs plus Adam, timed with CUDA events."""
+    import torch
+
+    from magma_b200 import lib
+    from magma_b200.gpt import GPTTrainer, char_gpt
+
+    cfg = char_gpt()
+    tr = GPTTrainer(cfg, 64, "f32", lr=3e-4, seed=0)
+    g = torch.Generator().manual_seed(7)
+    tok = torch.randint(0, cfg.vocab, (64, cfg.seq), generator=g, dtype=torch.int32)
+    tr.set_batch(tok, tok)
+    tr.capture()
+    for _ in range(warmup):
+        tr.run_fwd_bwd()
+        tr.optimizer_step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        tr.run_fwd_bwd()
+        tr.optimizer_step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    kinds = instrumented_step(tr, lib, torch)
+    flops = sum(kinds[k]["work"] for k in ("gemm", "attention_fwd", "attention_bwd")
+                if k in kinds)
+    tflops = flops / (ms / 1e3) / 1e12
+    return {"workload": "char-level GPT train step F32 (vocab 65, 6 layers, 6 heads, d 384, "
+                        "ctx 256, batch 64), Adam lr 3e-4",
+            "ms_per_step": round(ms, 3), "tokens_per_s": round(64 * cfg.seq / (ms / 1e3), 1),
+            "flops_per_step": flops, "tflops": round(tflops, 2), "bound": "FP32 FFMA",
+            "peak": FFMA_NOMINAL_TFLOPS, "unit": "TFLOP/s",
+            "frac": round(tflops / FFMA_NOMINAL_TFLOPS, 4),
+            "peak_source": "nominal F32 FFMA (148 SM x 128 FMA/clk x 2 x 1.965 GHz)",
+            "loss": round(float(tr.loss.item()), 4)}
 
 
 # ------------------------------------------------------------------- CPU baseline
@@ -385,6 +432,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["magma", "reference"], default="magma")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--zero1", action="store_true",
+                    help="N > 1: sharded optimiser state (reduce-scatter, Adam on 1/N, "
+                         "all-gather) instead of the replicated all-reduce step")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the standalone LayerNorm / attention / MLP configuration lines")
     args = ap.parse_args()
@@ -409,8 +459,10 @@ def main() -> None:
     tr = GPTTrainer(cfg, B, "bf16", lr=OPT["lr"], beta1=OPT["beta1"], beta2=OPT["beta2"],
                     weight_decay=OPT["wd"], seed=0, grad_clip=OPT["clip"],
                     lr_schedule=(OPT["warmup"], OPT["total"], OPT["min_lr"]))
-    # the gradient all-reduce goes through the library's C-ABI collectives
-    sync = dp.GradSync(comm=dp.Comm.from_process_group() if world > 1 else None)
+    # the gradient exchange goes through the library's C-ABI collectives
+    comm = dp.Comm.from_process_group() if world > 1 else None
+    sharded = args.zero1 and world > 1
+    sync = dp.ShardSync(comm) if sharded else dp.GradSync(comm=comm)
     gen = torch.Generator().manual_seed(1234 + rank)
     tok_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()
     tgt_h = torch.randint(0, cfg.vocab, (B, S), generator=gen, dtype=torch.int32).pin_memory()
@@ -420,8 +472,12 @@ def main() -> None:
         tr.capture()
 
     def step():
-        # gradient all-reduce per backward segment, overlapped with the rest
-        tr.optimizer_step(grad_scale=tr.run_fwd_bwd(sync=sync))
+        # gradient exchange per backward segment, overlapped with the rest
+        if sharded:
+            tr.run_fwd_bwd(sync=sync)
+            tr.optimizer_step_sharded(sync)
+        else:
+            tr.optimizer_step(grad_scale=tr.run_fwd_bwd(sync=sync))
 
     for _ in range(args.warmup):
         step()
@@ -510,7 +566,7 @@ def main() -> None:
     if rank != 0:
         if world > 1:
             dist.barrier()
-            sync.close()
+            comm.destroy()
             dist.destroy_process_group()
         return
     cpu = None
@@ -520,7 +576,7 @@ def main() -> None:
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "config": workload_config(world, B),
+        "data": "synthetic", "config": workload_config(world, B, sharded),
         "e2e": {"value": round(tokens_per_step / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": int(tok_h.numel() * 4 + tgt_h.numel() * 4),
                 "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4),
@@ -536,7 +592,7 @@ def main() -> None:
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
-        sync.close()
+        comm.destroy()
         dist.destroy_process_group()
 
 

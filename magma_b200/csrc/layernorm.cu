@@ -48,11 +48,12 @@ constexpr int kMaxBwdBlocks = 592;   // cap on per-CTA partial rows (4 x 148 SMs
 constexpr int kMaxGroups = 8;               // 4-element groups per lane: D <= 1024
 constexpr int kStreamSmem = 200 * 1024;     // dynamic shared memory for the rings
 constexpr int kBarBytes = 1024;             // mbarrier area at the start of it
-constexpr int kFwdRing = 3;                 // row buffers per warp, forward
-constexpr int kBwdRing = 2;                 // row buffers per warp, backward
-// Forward warps per CTA (128 registers per thread at 16; the widest rows,
-// G = 8, run 12).
-constexpr int fwd_max_warps(int groups) { return groups > 6 ? 12 : 16; }
+constexpr int kFwdRing = 5;                 // row buffers per warp, forward
+constexpr int kBwdRing = 3;                 // row buffers per warp, backward
+// Forward warps per CTA. With 12 warps and 5 row buffers each, a [8192, 768]
+// launch has every row's copy in flight from the start (4.6 rows per warp on
+// 148 SMs), so the loads of the last rows do not wait behind the first ones.
+constexpr int fwd_max_warps(int groups) { return groups > 6 ? 8 : 12; }
 // Backward warps per CTA: 12 keep 170 registers per thread; the widest rows
 // (G = 8) need more and run 8 warps.
 constexpr int bwd_max_warps(int groups, bool res = false) {
@@ -284,11 +285,21 @@ ln_bwd_stream(const TDY* __restrict__ dy, const TX* __restrict__ x,
       for (int i = 0; i < 4; ++i) dc[RES ? c : 0][i] = 0.f;
   }
   bool ok = true;
+  // Row statistics of this warp's rows, 32 rows at a time: lane i holds those
+  // of row j0 + i (loaded together, ahead of use), broadcast by shuffles.
+  float st_mean = 0.f, st_rstd = 0.f;
   for (int64_t j = 0; j < n; ++j) {
     const int slot = (int)(j % kBwdRing);
     const int64_t row = first + j * stride;
-    const float mean = mean_in[row];
-    const float rstd = rstd_in[row];
+    if ((j & 31) == 0) {
+      const int64_t jl = j + lane;
+      if (jl < n) {
+        st_mean = mean_in[first + jl * stride];
+        st_rstd = rstd_in[first + jl * stride];
+      }
+    }
+    const float mean = __shfl_sync(0xffffffffu, st_mean, (int)(j & 31));
+    const float rstd = __shfl_sync(0xffffffffu, st_rstd, (int)(j & 31));
     if (!mbar_wait(smem_u32(bars + slot), (uint32_t)((j / kBwdRing) & 1), err)) {
       drain_ring<kBwdRing>(bars, j, n < j + kBwdRing ? n : j + kBwdRing, err);
       ok = false;

@@ -645,8 +645,15 @@ class GPTTrainer:
         self.targets.copy_(targets, non_blocking=True)
 
     def train_step(self, tokens: torch.Tensor, targets: torch.Tensor, allreduce=None) -> float:
-        """Host tokens/targets [B, S] in, host loss out: H2D, fwd+bwd, DP sync, Adam, D2H."""
+        """Host tokens/targets [B, S] in, host loss out: H2D, fwd+bwd, DP sync, Adam, D2H.
+        `allreduce`: None (one GPU), a dp.GradSync (replicated step), a
+        dp.ShardSync (sharded optimiser step) or a blocking callable that
+        sums the gradient arena and returns the Adam grad_scale."""
         self.set_batch(tokens, targets)
+        if allreduce is not None and hasattr(allreduce, "owned"):
+            self.run_fwd_bwd(sync=allreduce)
+            self.optimizer_step_sharded(allreduce)
+            return float(self.loss.item())
         if allreduce is None or hasattr(allreduce, "launch"):
             scale = self.run_fwd_bwd(sync=allreduce)
         else:

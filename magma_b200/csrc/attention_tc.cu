@@ -3,28 +3,26 @@
 // Benchmarks/GPT2Shakespeare/Sources/main.swift:467-481; VJP chain
 // Sources/Core/Autodiff.swift:309-317,379-386), tiled 128 x 128.
 //
-// Every kernel has the same six-warp shape:
-//   warps 0-3  row math: thread r owns TMEM lane r (one query or key row);
-//   warp 4     TMA producer (4-D tensor maps straight over the caller's strided
-//              [B, H, S, D] views: Q/K/V can be read in place from the fused
-//              QKV projection, no head transposes);
-//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer.
-// Score tiles and accumulators live in TMEM; P / dS are written by the row
-// threads as BF16 into 128-byte-swizzled shared memory (the K-major operand
-// layout TMA produces) and fed back to the tensor cores.
-//
-// Forward (one CTA per 128-query tile, heaviest causal tiles first):
-//   S_j = Q K_j^T (TMEM, double-buffered) -> online softmax in registers
-//   (exp2, running max/sum) -> P_j (smem, double-buffered) -> PV_j = P_j V_j
-//   (TMEM, double-buffered) folded into a register accumulator two tiles
-//   later with the matching rescale. The MMA warp issues S_{j+1} while the row
-//   threads work on S_j. Outputs O (BF16) and the row log-sum-exp.
-// Backward, deterministic (no atomics), two kernels after the delta pre-pass:
-//   dK/dV: one CTA per 128-key tile, loop over query tiles: S^T = K Q^T,
-//     dP^T = V dO^T, P^T = exp(S^T*scale - lse), dS^T = P^T (dP^T - delta),
-//     dV += P^T dO, dK += dS^T Q (TMEM accumulators).
-//   dQ: one CTA per 128-query tile, loop over key tiles: S, dP, dS as above,
-//     dQ += dS K.
+// Kernels (each with a TMA producer warp over 4-D tensor maps straight on the
+// caller's strided [B, H, S, D] views — Q/K/V are read in place from the fused
+// QKV projection, no head transposes — and one warp that allocates TMEM and
+// issues the tcgen05.mma from a single thread; score tiles and accumulators
+// live in TMEM):
+//   attn_fwd_tc    one CTA per pair of 128-query tiles, two softmax warpgroups
+//                  (thread = query row) taking turns on the exponentials;
+//                  S_t = Q_t K_j^T in TMEM, P_t written back over S_t as BF16
+//                  and used from TMEM as the A operand of O_t += P_t V_j;
+//                  outputs O (BF16) and the row log-sum-exp.
+//   attn_delta_tc  delta = rowsum(dO * O) for the softmax VJP.
+//   attn_bwd_tc    one CTA per 128-key tile looping over its query tiles:
+//                  S^T = K Q^T, dP^T = V dO^T, P^T = exp(S^T*scale - lse),
+//                  dS^T = P^T (dP^T - delta); dV += P^T dO, dK += dS^T Q (TMEM
+//                  accumulators, P^T / dS^T as TMEM A operands), dQ_ij = dS K_j
+//                  drained as an F32 partial tile.
+//   attn_dq_reduce sums the dQ partials over key tiles in a fixed order
+//                  (deterministic, no atomics).
+//   attn_bwd_dkdv_tc / attn_bwd_dq_tc  two-pass backward for workspaces too
+//                  small for the partial tiles.
 // All mbarrier waits are bounded (they set the device error word and the
 // kernel winds down instead of hanging).
 #include <cuda.h>

@@ -48,12 +48,13 @@ constexpr int kMaxBwdBlocks = 592;   // cap on per-CTA partial rows (4 x 148 SMs
 constexpr int kMaxGroups = 8;               // 4-element groups per lane: D <= 1024
 constexpr int kStreamSmem = 200 * 1024;     // dynamic shared memory for the rings
 constexpr int kBarBytes = 1024;             // mbarrier area at the start of it
-constexpr int kFwdRing = 5;                 // row buffers per warp, forward
-constexpr int kBwdRing = 3;                 // row buffers per warp, backward
-// Forward warps per CTA. With 12 warps and 5 row buffers each, a [8192, 768]
-// launch has every row's copy in flight from the start (4.6 rows per warp on
-// 148 SMs), so the loads of the last rows do not wait behind the first ones.
-constexpr int fwd_max_warps(int groups) { return groups > 6 ? 8 : 12; }
+constexpr int kFwdRing = 3;                 // row buffers per warp, forward
+constexpr int kBwdRing = 2;                 // row buffers per warp, backward
+// Forward warps per CTA (128 registers per thread at 16; the widest rows,
+// G = 8, run 12). Deeper rings with fewer warps (5 buffers x 12 warps forward,
+// 3 x 12 backward) measured slower at [8192, 768] (7.1 -> 7.4 us forward,
+// 15.4 -> 16.6 us backward in A/B runs on one box).
+constexpr int fwd_max_warps(int groups) { return groups > 6 ? 12 : 16; }
 // Backward warps per CTA: 12 keep 170 registers per thread; the widest rows
 // (G = 8) need more and run 8 warps.
 constexpr int bwd_max_warps(int groups, bool res = false) {

@@ -291,6 +291,13 @@ class GPTTrainer:
                  lib.query("magma_bias_grad_workspace_size", T, 4 * D),
                  lib.query("magma_bias_grad_workspace_size", T, 3 * D))
         self.ws = torch.empty(max(ws, 1 << 20), dtype=torch.uint8, device=self.dev)
+        # scratch of the side stream's weight-gradient GEMMs and bias gradients
+        ws_side = max(max(lib.query("magma_gemm_workspace_size", m, n, k, self.DT)
+                          for m, n, k in gemm_shapes),
+                      lib.query("magma_bias_grad_workspace_size", T, 4 * D),
+                      lib.query("magma_bias_grad_workspace_size", T, 3 * D))
+        self.ws_side = torch.empty(max(ws_side, 1 << 20), dtype=torch.uint8, device=self.dev)
+        self.side = torch.cuda.Stream(self.dev)
         # attention geometry over the fused [B, S, 3, H, hd] projection
         S, hd = cfg.seq, cfg.head_dim
         self.qkv_strides = (C.c_int64 * 3)(S * 3 * D, hd, 3 * D)
@@ -299,10 +306,11 @@ class GPTTrainer:
 
     # -------------------------------------------------------------- primitives
     def _gemm(self, a, b, c, m, n, k, lda, ldb, ldc, ta, tb, epi, bias=None, aux_in=None,
-              aux_out=None, c_dtype=None):
+              aux_out=None, c_dtype=None, ws=None):
+        ws = self.ws if ws is None else ws
         lib.call("magma_gemm", _p(a), _p(b), _p(c), m, n, k, lda, ldb, ldc, ta, tb, self.DT,
                  c_dtype if c_dtype is not None else self.DT, epi, _p(bias), _p(aux_in),
-                 _p(aux_out), _p(self.ws), self.ws.numel(), self._s())
+                 _p(aux_out), _p(ws), ws.numel(), self._s())
 
     def _ln_fwd(self, x, w, b, y, mean, rstd):
         lib.call("magma_layernorm_fwd", _p(x), _p(w), _p(b), _p(y), _p(mean), _p(rstd), self.T,
@@ -317,10 +325,35 @@ class GPTTrainer:
                  _p(self.dresid), _p(copy), _p(dw), _p(db), _p(dcol), self.T, self.cfg.dim,
                  self.DT, accumulate, 0, _p(self.ws), self.ws.numel(), self._s())
 
-    def _bias_grad(self, dy, db, cols):
+    def _bias_grad(self, dy, db, cols, ws=None):
+        ws = self.ws if ws is None else ws
         lib.call("magma_bias_grad", _p(dy), _p(db), self.T, cols, cols,
-                 lib.F32 if dy.dtype == torch.float32 else lib.BF16, 0, _p(self.ws),
-                 self.ws.numel(), self._s())
+                 lib.F32 if dy.dtype == torch.float32 else lib.BF16, 0, _p(ws), ws.numel(),
+                 self._s())
+
+    # ------------------------------------------------ side stream (backward)
+    # The weight-gradient GEMMs and bias gradients of the backward do not feed
+    # the rest of the backward: they run on a second stream, ordered after the
+    # main stream's work they read, so they fill the SMs the input-gradient
+    # chain leaves idle (the last partial wave of its GEMMs, the gaps around
+    # small kernels). Events order the main stream's later writes to the
+    # buffers they read, and every segment joins both streams before its
+    # gradient ranges are handed to the data-parallel sync.
+    def _fork(self) -> None:
+        """The side stream waits for the work queued so far on the main stream."""
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.dev))
+        self.side.wait_event(ev)
+
+    def _side_mark(self) -> torch.cuda.Event:
+        ev = torch.cuda.Event()
+        ev.record(self.side)
+        return ev
+
+    def _wait(self, ev: torch.cuda.Event | None) -> None:
+        """The main stream waits for a side-stream event."""
+        if ev is not None:
+            torch.cuda.current_stream(self.dev).wait_event(ev)
 
     # ------------------------------------------------------------ fwd + bwd
     # layers per backward segment: the gradient sync of a finished segment
@@ -410,10 +443,13 @@ class GPTTrainer:
         lib.call("magma_reduce_sum", _p(self.losses), _p(self.loss), T, 1.0 / T, s)
 
         # ---------------------------------------------------------- backward
-        # lm-head: d(lnf) = dlogits . Wh ; dWh = dlogits^T . lnf
+        # lm-head: d(lnf) = dlogits . Wh (main) ; dWh = dlogits^T . lnf (side)
+        side, wss = self.side, self.ws_side
+        self._fork()
+        with torch.cuda.stream(side):
+            self._gemm(self.logits, self.lnf, self.view(G, head), Vp, D, T, Vp, D, D, 1, 0,
+                       E.EPI_NONE, c_dtype=lib.F32, ws=wss)
         self._gemm(self.logits, W(head), self.d_ln, T, D, Vp, Vp, D, D, 0, 0, E.EPI_NONE)
-        self._gemm(self.logits, self.lnf, self.view(G, head), Vp, D, T, Vp, D, D, 1, 0, E.EPI_NONE,
-                   c_dtype=lib.F32)
         # final LN: dresid = LN_bwd (written, not accumulated); its column sums
         # are the last block's fcproj bias gradient
         self._ln_bwd(self.d_ln, self.x[L], self.view(P, "lnf_w"), self.lnf_stats[0],
@@ -422,28 +458,41 @@ class GPTTrainer:
         segments = self.segment_ranges()
         seg = 0
         seg_top = L - 1
+        d_fc_free = dqkv_free = None  # side events after the last reads of d_fc / dqkv
         for l in reversed(range(L)):
             n = lambda k: f"h{l}.{k}"  # noqa: E731
             st = self.stats[l]
             dres = self._dresid_operand()
             # MLP: x_{l+1} = h + fcproj(gelu(fc(ln2(h))))
+            self._fork()
+            with torch.cuda.stream(side):
+                self._gemm(dres, self.fc_act[l], self.view(G, n("fcproj_w")), D, 4 * D, T, D,
+                           4 * D, 4 * D, 1, 0, E.EPI_NONE, c_dtype=lib.F32, ws=wss)
+                dres_read = self._side_mark()
+            self._wait(d_fc_free)  # the previous layer's side reads of d_fc are done
             self._gemm(dres, W(n("fcproj_w")), self.d_fc, T, 4 * D, D, D, 4 * D, 4 * D, 0, 0,
                        E.EPI_DGELU, aux_in=self.fc_pre[l])
-            self._gemm(dres, self.fc_act[l], self.view(G, n("fcproj_w")), D, 4 * D, T, D, 4 * D,
-                       4 * D, 1, 0, E.EPI_NONE, c_dtype=lib.F32)
+            self._fork()
+            with torch.cuda.stream(side):
+                self._gemm(self.d_fc, self.ln2[l], self.view(G, n("fc_w")), 4 * D, D, T, 4 * D, D,
+                           D, 1, 0, E.EPI_NONE, c_dtype=lib.F32, ws=wss)
+                self._bias_grad(self.d_fc, self.view(G, n("fc_b")), 4 * D, ws=wss)
+                d_fc_free = self._side_mark()
             self._gemm(self.d_fc, W(n("fc_w")), self.d_ln, T, D, 4 * D, 4 * D, D, D, 0, 0,
                        E.EPI_NONE)
-            self._gemm(self.d_fc, self.ln2[l], self.view(G, n("fc_w")), 4 * D, D, T, 4 * D, D, D,
-                       1, 0, E.EPI_NONE, c_dtype=lib.F32)
-            self._bias_grad(self.d_fc, self.view(G, n("fc_b")), 4 * D)
+            self._wait(dres_read)  # the LayerNorm VJP rewrites the residual gradient
             self._ln_bwd(self.d_ln, self.h[l], self.view(P, n("ln2_w")), st[2], st[3],
                          self.view(G, n("ln2_w")), self.view(G, n("ln2_b")),
                          self.view(G, n("proj_b")))
             dres = self._dresid_operand()
             # attention: h = x + proj(attn(qkv(ln1(x))))
+            self._fork()
+            with torch.cuda.stream(side):
+                self._gemm(dres, self.att[l], self.view(G, n("proj_w")), D, D, T, D, D, D, 1, 0,
+                           E.EPI_NONE, c_dtype=lib.F32, ws=wss)
+                dres_read = self._side_mark()
             self._gemm(dres, W(n("proj_w")), self.d_att, T, D, D, D, D, D, 0, 0, E.EPI_NONE)
-            self._gemm(dres, self.att[l], self.view(G, n("proj_w")), D, D, T, D, D, D, 1, 0,
-                       E.EPI_NONE, c_dtype=lib.F32)
+            self._wait(dqkv_free)  # the previous layer's side reads of dqkv are done
             q = self.qkv[l]
             es = q.element_size()
             dq = self.dqkv
@@ -452,11 +501,15 @@ class GPTTrainer:
                      dq.data_ptr() + D * es, dq.data_ptr() + 2 * D * es, self.B, cfg.heads,
                      cfg.seq, cfg.head_dim, self.qkv_strides, self.o_strides, self.scale, 1,
                      self.DT, _p(self.ws), self.ws.numel(), s)
+            self._fork()
+            with torch.cuda.stream(side):
+                self._gemm(self.dqkv, self.ln1[l], self.view(G, n("qkv_w")), 3 * D, D, T, 3 * D,
+                           D, D, 1, 0, E.EPI_NONE, c_dtype=lib.F32, ws=wss)
+                self._bias_grad(self.dqkv, self.view(G, n("qkv_b")), 3 * D, ws=wss)
+                dqkv_free = self._side_mark()
             self._gemm(self.dqkv, W(n("qkv_w")), self.d_ln, T, D, 3 * D, 3 * D, D, D, 0, 0,
                        E.EPI_NONE)
-            self._gemm(self.dqkv, self.ln1[l], self.view(G, n("qkv_w")), 3 * D, D, T, 3 * D, D, D,
-                       1, 0, E.EPI_NONE, c_dtype=lib.F32)
-            self._bias_grad(self.dqkv, self.view(G, n("qkv_b")), 3 * D)
+            self._wait(dres_read)
             self._ln_bwd(self.d_ln, self.x[l], self.view(P, n("ln1_w")), st[0], st[1],
                          self.view(G, n("ln1_w")), self.view(G, n("ln1_b")),
                          self.view(G, f"h{l - 1}.fcproj_b") if l > 0 else None,
@@ -464,11 +517,14 @@ class GPTTrainer:
             # layers l .. seg_top are final (layer l-1's fcproj bias gradient,
             # written just above, belongs to the next segment)
             if (seg_top - l + 1 == self.SYNC_GROUP) and l > 0:
+                self._wait(self._side_mark())  # the segment's gradients are complete
+                d_fc_free = dqkv_free = None  # covered by that join
                 yield segments[seg]
                 seg += 1
                 seg_top = l - 1
         # embeddings: dwte += scatter(dresid) (tied: onto the lm-head
         # gradient; untied: onto zeros); dwpe = sum over the batch, written
+        self._wait(self._side_mark())  # every side-stream gradient is complete
         if not cfg.tied:
             wte_g = self.view(G, "wte")
             lib.call("magma_memset", _p(wte_g), 0, wte_g.numel() * 4, s)

@@ -158,12 +158,17 @@ def instrumented_step(trainer, lib, torch):
     side.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
     lib.call = timed_call
+    # one stream, so that each call's events time that call alone (the timed
+    # steps run the backward's weight gradients on a second stream)
+    concurrent = getattr(trainer, "concurrent_wgrad", False)
+    trainer.concurrent_wgrad = False
     try:
         with torch.cuda.graph(g, stream=side):
             trainer.step_fwd_bwd()
             trainer.optimizer_step()
     finally:
         lib.call = orig
+        trainer.concurrent_wgrad = concurrent
     torch.cuda.current_stream().wait_stream(side)
     for _ in range(2):
         g.replay()

@@ -339,13 +339,24 @@ class GPTTrainer:
     # small kernels). Events order the main stream's later writes to the
     # buffers they read, and every segment joins both streams before its
     # gradient ranges are handed to the data-parallel sync.
+    # With concurrent_wgrad False everything runs on the current stream in the
+    # same order (the per-call timings of the bench's roofline use that form).
+    concurrent_wgrad = True
+
+    def _side_stream(self) -> torch.cuda.Stream:
+        return self.side if self.concurrent_wgrad else torch.cuda.current_stream(self.dev)
+
     def _fork(self) -> None:
         """The side stream waits for the work queued so far on the main stream."""
+        if not self.concurrent_wgrad:
+            return
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(self.dev))
         self.side.wait_event(ev)
 
-    def _side_mark(self) -> torch.cuda.Event:
+    def _side_mark(self) -> torch.cuda.Event | None:
+        if not self.concurrent_wgrad:
+            return None
         ev = torch.cuda.Event()
         ev.record(self.side)
         return ev
@@ -444,7 +455,7 @@ class GPTTrainer:
 
         # ---------------------------------------------------------- backward
         # lm-head: d(lnf) = dlogits . Wh (main) ; dWh = dlogits^T . lnf (side)
-        side, wss = self.side, self.ws_side
+        side, wss = self._side_stream(), self.ws_side
         self._fork()
         with torch.cuda.stream(side):
             self._gemm(self.logits, self.lnf, self.view(G, head), Vp, D, T, Vp, D, D, 1, 0,

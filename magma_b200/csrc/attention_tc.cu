@@ -64,6 +64,12 @@ __device__ __forceinline__ uint64_t desc_k(uint32_t addr) { return smem_desc_sw1
 __device__ __forceinline__ uint64_t desc_mn(uint32_t addr) {
   return smem_desc_sw128(addr, 8192, 1024);
 }
+// desc(addr + off) for a descriptor d = desc(addr): the start address sits in
+// the low 14 bits in 16-byte units, and shared-memory addresses stay below
+// 256 KB, so the sum never carries out of that field.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t off_bytes) {
+  return d + (uint64_t)(off_bytes >> 4);
+}
 
 // Address in a [128 rows x 128 cols] BF16 K-major SW128 operand (two 64-column
 // blocks of 16 KB) of the 16-byte chunk holding columns [8*chunk, 8*chunk+8)
@@ -122,12 +128,13 @@ __device__ __forceinline__ uint32_t align1024(uint8_t* raw, uint8_t** aligned_pt
 // that of tile 1, warp 8 is the TMA producer, warp 9 allocates TMEM and issues
 // the MMAs. Both tiles stream the same K/V tiles, so while one warpgroup
 // turns S_t into P_t the tensor cores work on the other tile:
-//   MMA order: S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) ...
-// TMEM: S_t at columns 128t (F32 128x128); P_t is written back as BF16 over
-// the first 64 columns of S_t and is the A operand of PV_t = P_t V_j, which
-// accumulates into O_t at columns 256 + 64t. tcgen05.mma executes in issue
-// order, so S_t(j+1), issued after PV_t(j), cannot overwrite P_t(j) early, and
-// the commit that reports S_t(j+1) done also covers PV_t(j). O_t and the row
+//   MMA order: S0(0) S1(0) | S0(1) PV0(0) S1(1) PV1(0) | S0(2) PV0(1) ...
+// TMEM: S_t at columns 128t (F32 128x128), O_t at 256 + 64t, P_t (BF16
+// pairs, the TMEM A operand of PV_t = P_t V_j) at 384 + 64t. A warpgroup
+// releases S_t's columns (s_free) as soon as its exponential pass has read
+// the last of them, so S_t(j+1) is computed while the pass finishes and while
+// the other warpgroup runs its own; before it writes P_t(j) or rescales O_t
+// it waits for PV_t(j-1) (pv_done). O_t and the row
 // sum are rescaled only when a row maximum grows by more than 2^8 (otherwise
 // the stale maximum is kept: P <= 2^8, exact after the final division).
 constexpr int kFwdStages = 3;
@@ -135,8 +142,8 @@ constexpr int kFwdThreads = 320;                 // 8 softmax warps + producer +
 constexpr int kFwdQ = 0;                         // Q tiles 0, 1 (2 x 16 KB)
 constexpr int kFwdKv = 2 * kTileBytes;           // K, V per stage
 constexpr int kFwdBar = kFwdKv + kFwdStages * 2 * kTileBytes;
-// q_full, kv_full[3], kv_empty[3], s_full[2], p_full[2], pv_done[2], done
-constexpr int kFwdNumBars = 14;
+// q_full, kv_full[3], kv_empty[3], s_full[2], s_free[2], p_full[2], pv_done[2], done
+constexpr int kFwdNumBars = 16;
 constexpr int kFwdSmem = kFwdBar + kFwdNumBars * 8 + 16 + 1024;
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -154,9 +161,10 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   auto kv_full = [&](int st) { return bars + 8u * (1 + st); };
   auto kv_empty = [&](int st) { return bars + 8u * (4 + st); };
   auto s_full = [&](int t) { return bars + 8u * (7 + t); };
-  auto p_full = [&](int t) { return bars + 8u * (9 + t); };
-  auto pv_done = [&](int t) { return bars + 8u * (11 + t); };
-  const uint32_t done_bar = bars + 8u * 13;
+  auto s_free = [&](int t) { return bars + 8u * (9 + t); };
+  auto p_full = [&](int t) { return bars + 8u * (11 + t); };
+  auto pv_done = [&](int t) { return bars + 8u * (13 + t); };
+  const uint32_t done_bar = bars + 8u * 15;
   const uint32_t tslot = bars + 8u * kFwdNumBars;
   uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kFwdBar + 8 * kFwdNumBars);
 
@@ -187,6 +195,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full(t), 1);
+      mbar_init(s_free(t), 4);
       mbar_init(p_full(t), 4);
       mbar_init(pv_done(t), 1);
     }
@@ -200,6 +209,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
   auto tS = [&](int t) { return tmem + (uint32_t)(t * kTile); };
   auto tO = [&](int t) { return tmem + 256u + (uint32_t)(t * kHd); };
+  auto tP = [&](int t) { return tmem + 384u + (uint32_t)(t * kHd); };
 
   if (warp == 8) {
     if (lane == 0) {
@@ -237,24 +247,29 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         tc_fence_after();
         return true;
       };
+      // Descriptors are formed once; every instruction then adds an immediate
+      // byte offset >> 4 (desc_add), which keeps the single issuing thread's
+      // scalar work per tcgen05.mma to one add.
+      const uint64_t dq0 = desc_k(sQ(0)), dk0 = desc_k(sK(0)), dv0 = desc_mn(sV(0));
       auto issue_s = [&](int t, int j) {
         const int st = j % kFwdStages;
+        const uint64_t dq = desc_add(dq0, (uint32_t)t * kTileBytes);
+        const uint64_t dk = desc_add(dk0, (uint32_t)st * 2 * kTileBytes);
+        const uint32_t d = tS(t);
 #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk)
-          mma_bf16_ss(tS(t), desc_k(sQ(t) + kk * 32), desc_k(sK(st) + kk * 32), idS,
-                      kk > 0 ? 1u : 0u);
+          mma_bf16_ss(d, desc_add(dq, kk * 32), desc_add(dk, kk * 32), idS, kk > 0 ? 1u : 0u);
         mma_commit(s_full(t));
       };
-      auto issue_pv = [&](int t, int j) -> bool {
-        if (!mbar_wait(p_full(t), (uint32_t)(j & 1), a.err)) return false;
-        tc_fence_after();
+      auto issue_pv = [&](int t, int j) {
         const int st = j % kFwdStages;
+        const uint64_t dv = desc_add(dv0, (uint32_t)st * 2 * kTileBytes);
+        const uint32_t d = tO(t), pa = tP(t);
+        const uint32_t acc = j > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          mma_bf16_ts(tO(t), tS(t) + kk * 8, desc_mn(sV(st) + kk * 2048), idPV,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(d, pa + kk * 8, desc_add(dv, kk * 2048), idPV, kk > 0 ? 1u : acc);
         mma_commit(pv_done(t));
-        return true;
       };
       if (ok && n_kv > 0) {
         ok = wait_kv(0);
@@ -267,11 +282,18 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         for (int t = 0; t < 2 && ok; ++t) {
           const int nk = t ? nk1 : nk0;
           if (j >= nk) continue;
-          if (!issue_pv(t, j)) { ok = false; break; }
+          // S_t(j+1) as soon as warpgroup t has read all of S_t(j)
           if (j + 1 < nk) {
-            if (!wait_kv(j + 1)) { ok = false; break; }
+            if (!mbar_wait(s_free(t), (uint32_t)(j & 1), a.err) || !wait_kv(j + 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
             issue_s(t, j + 1);
           }
+          if (!mbar_wait(p_full(t), (uint32_t)(j & 1), a.err)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
         }
         if (ok) mma_commit(kv_empty(j % kFwdStages));
       }
@@ -288,6 +310,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t srow = tS(t) + lane_off;
     const uint32_t orow = tO(t) + lane_off;
+    const uint32_t prow = tP(t) + lane_off;
     const float sl2 = a.scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -340,29 +363,35 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m_run, mx * sl2);
-        if (j == 0) {
-          m_run = m_new == -INFINITY ? 0.f : m_new;
-        } else if (__any_sync(0xffffffffu, m_new > m_run + kRescaleLog2)) {
-          // O_t holds PV_t(0 .. j-1) (complete: covered by the S_t(j) commit).
-          const float alpha = ex2_approx(m_run - m_new);
-          m_run = m_new;
-          l_run *= alpha;
+        // PV_t(j-1) has read P_t and added into O_t before either is touched
+        if (j >= 1 && !mbar_wait(pv_done(t), (uint32_t)((j - 1) & 1), a.err)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          if (j == 0) {
+            m_run = m_new == -INFINITY ? 0.f : m_new;
+          } else if (__any_sync(0xffffffffu, m_new > m_run + kRescaleLog2)) {
+            const float alpha = ex2_approx(m_run - m_new);
+            m_run = m_new;
+            l_run *= alpha;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t o[32];
-            tmem_ld32(orow + half * 32, o);
-            tmem_wait_ld();
+            for (int half = 0; half < 2; ++half) {
+              uint32_t o[32];
+              tmem_ld32(orow + half * 32, o);
+              tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(orow + half * 32, o);
+              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+              tmem_st32(orow + half * 32, o);
+            }
+            tmem_wait_st();
           }
-          tmem_wait_st();
         }
       }
-      // pass 2: P = exp2(S * scale * log2(e) - m), written back over S as
-      // BF16. The first half of the row is read from TMEM before the turn
-      // starts, the second half while the first is exponentiated; the turn is
-      // handed on as soon as the last exponential is issued.
+      // pass 2: P = exp2(S * scale * log2(e) - m) as BF16 pairs into P_t's
+      // columns. The first half of the row is read from TMEM before the turn
+      // starts, the rest while the first is exponentiated; once the last
+      // column is read S_t's columns are released for S_t(j+1), and the turn
+      // is handed on as soon as the last exponential is issued.
       uint32_t va[2][32];
       if (ok) {
         tmem_ld32(srow, va[0]);
@@ -373,8 +402,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       if (ok) {
         float rs4[4] = {0.f, 0.f, 0.f, 0.f};
         // Exponentiates 32 columns starting at column c of S (v) into 16
-        // packed BF16 pairs stored over BF16 columns [c/2, c/2 + 16) (S
-        // columns already read).
+        // packed BF16 pairs stored at P_t's columns [c/2, c/2 + 16).
         auto exp32 = [&](const uint32_t (&v)[32], int c) {
           uint32_t pk[16];
 #pragma unroll
@@ -388,17 +416,20 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             rs4[e & 3] += p0 + p1;
             pk[e] = pack_bf16(p0, p1);
           }
-          tmem_st16(srow + c / 2, pk);
+          tmem_st16(prow + c / 2, pk);
         };
         uint32_t vb[32];
-        tmem_ld32(srow + 64, vb);  // lands while columns 0-63 are exponentiated
         exp32(va[0], 0);
+        tmem_ld32(srow + 64, vb);  // lands while columns 32-63 are exponentiated
         exp32(va[1], 32);
         tmem_wait_ld();
         uint32_t vc[32];
         tmem_ld32(srow + 96, vc);
         exp32(vb, 64);
         tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free(t));  // all of S_t(j) is in registers
         exp32(vc, 96);
         if (give_turn) named_barrier_arrive(2 - t, 256);
         l_run += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
@@ -863,17 +894,21 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // dQ partials are summed over j in a fixed order by attn_dq_reduce
 // (deterministic; no atomics).
 // Warps 0-7: element math, thread = key row (TMEM lane quarter warp % 4) x
-// one half of the 128 query columns (warp / 4); warp 8: TMA producer;
-// warp 9: TMEM allocator and MMA issuer.
-constexpr int kBwThreads = 320;
+// one half of the 128 query columns (warp / 4); warp 8: TMA producer, which
+// also stages each query tile's row terms (lse in log2 units, delta); warp 9:
+// TMEM allocator and MMA issuer; warp 10: sends the dQ partial tiles to the
+// workspace with bulk copies.
+constexpr int kBwThreads = 352;
 constexpr int kBwK = 0;
 constexpr int kBwV = kTileBytes;
-constexpr int kBwQdo = 2 * kTileBytes;                      // 2 stages x (Q, dO)
-constexpr int kBwDST = kBwQdo + 2 * 2 * kTileBytes;         // 2 buffers x 32 KB
-constexpr int kBwStats = kBwDST + 2 * 2 * kTileBytes;       // lse2[128], delta[128]
-constexpr int kBwBar = kBwStats + 2 * kTile * 4;
-// kv_full, qdo_full[2], qdo_empty[2], st_full, pds_full, dq_full[2], dq_free[2], final
-constexpr int kBwNumBars = 12;
+constexpr int kBwQdoStages = 3;
+constexpr int kBwQdo = 2 * kTileBytes;                      // 3 stages x (Q, dO)
+constexpr int kBwDST = kBwQdo + kBwQdoStages * 2 * kTileBytes;  // 2 buffers x 32 KB
+constexpr int kBwStats = kBwDST + 2 * 2 * kTileBytes;       // 3 stages x (lse2[128], delta[128])
+constexpr int kBwBar = kBwStats + kBwQdoStages * 2 * kTile * 4;
+// kv_full, qdo_full[3], qdo_empty[3], stats_full[3], st_full, st_free, pds_full, pt_free,
+// dq_full, dq_free, staged, stage_free, final
+constexpr int kBwNumBars = 19;
 constexpr int kBwSmem = kBwBar + kBwNumBars * 8 + 16 + 1024;
 constexpr int kDqTileFloats = kTile * kHd;                  // one F32 dQ partial tile
 
@@ -898,15 +933,26 @@ __device__ __forceinline__ void store_row_packed(uint32_t base, int r, int c32,
                  pk[4 * q + 3]);
 }
 
-// Pipeline over query tiles it = 0, 1, ...:
-//   MMA warp:   S(0) | [P(it) ready] dV(it) dK(it) S(it+1) dQ(it) | ...
-//   math warps: softmax(it) -> P(it) ready -> drain dQ(it-1) -> softmax(it+1)
-// P^T and dS^T are written back into TMEM over the S^T and dP^T columns each
-// thread has read (thread half h: columns [64h, 64h+32)) and are the A
-// operands of dV and dK, read from TMEM; dS^T also goes to shared memory as
-// the MN-major A operand of dQ. dQ alternates between two TMEM buffers, dS^T
-// between two shared buffers, so dQ(it) and the drain of dQ(it-1) run under
-// the exponentials of tile it+1.
+// Pipeline over query tiles it = 0, 1, ... (TC = tensor-core issue order):
+//   TC:    S(0) | S(it+1) dV(it) dK(it) dQ(it) | S(it+2) dV(it+1) ...
+//   math:  load S^T, dP^T(it) -> [S^T/dP^T free] -> P^T, dS^T -> [ready]
+//          -> drain dQ(it-1) -> load S^T, dP^T(it+1) -> ...
+// Each math thread loads its 64 columns of S^T and dP^T into registers and
+// releases those TMEM columns at once (st_free), so S(it+1) and dP(it+1) run
+// on the tensor cores while it computes P^T and dS^T of tile it. P^T goes to
+// its own 64 TMEM columns (BF16 pairs; the TMEM A operand of dV), dS^T to a
+// double-buffered 128-byte-swizzled shared tile (the K-major A operand of dK
+// and, read MN-major, of dQ). Once dQ(it) has completed, dS^T buffer it & 1
+// is free: the drain of dQ(it) writes the F32 partial tile there in the
+// workspace layout and warp 10 sends it out with one bulk copy, releasing the
+// buffer (stage_free) when the copy has read it; math(it+2) waits for that
+// before writing its dS^T. The row terms of each query tile arrive with its
+// Q / dO stage (stats_full). The math warps wait only on mbarriers.
+// P^T's TMEM columns are rewritten one tile later, after pt_free (committed
+// after dV(it)); the single dQ accumulator is drained (dq_free) before dQ(it+1)
+// is issued.
+// TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384),
+// dQ [384,448), P^T [448,512).
 __global__ void __launch_bounds__(kBwThreads, 1)
 attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -918,17 +964,22 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   auto sQ = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes; };
   auto sdO = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes + kTileBytes; };
   auto sDST = [&](int pb) { return base + kBwDST + pb * 2 * kTileBytes; };
-  float* lse_s = reinterpret_cast<float*>(sp + kBwStats);           // [128], log2 units
-  float* delta_s = reinterpret_cast<float*>(sp + kBwStats + kTile * 4);
+  // row terms of stage st: lse (log2 units) [128], then delta [128]
+  auto stats = [&](int st) { return reinterpret_cast<float*>(sp + kBwStats + st * 2 * kTile * 4); };
   const uint32_t bars = base + kBwBar;
   const uint32_t kv_full = bars;
   auto qdo_full = [&](int st) { return bars + 8u * (1 + st); };
-  auto qdo_empty = [&](int st) { return bars + 8u * (3 + st); };
-  const uint32_t st_full = bars + 8u * 5;
-  const uint32_t pds_full = bars + 8u * 6;
-  auto dq_full = [&](int db) { return bars + 8u * (7 + db); };
-  auto dq_free = [&](int db) { return bars + 8u * (9 + db); };
-  const uint32_t final_bar = bars + 8u * 11;
+  auto qdo_empty = [&](int st) { return bars + 8u * (4 + st); };
+  auto stats_full = [&](int st) { return bars + 8u * (7 + st); };
+  const uint32_t st_full = bars + 8u * 10;
+  const uint32_t st_free = bars + 8u * 11;
+  const uint32_t pds_full = bars + 8u * 12;
+  const uint32_t pt_free = bars + 8u * 13;
+  const uint32_t dq_full = bars + 8u * 14;
+  const uint32_t dq_free = bars + 8u * 15;
+  const uint32_t staged = bars + 8u * 16;
+  const uint32_t stage_free = bars + 8u * 17;
+  const uint32_t final_bar = bars + 8u * 18;
   const uint32_t tslot = bars + 8u * kBwNumBars;
   uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kBwBar + 8 * kBwNumBars);
 
@@ -944,6 +995,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   const int k0 = kt * kTile;
   const int first_q = a.causal ? kt : 0;
   const int n_it = n_t - first_q;
+  const int64_t bh = (int64_t)b * a.H + h;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmQ);
@@ -951,14 +1003,19 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     prefetch_tensormap(&tmV);
     prefetch_tensormap(&tmdO);
     mbar_init(kv_full, 1);
-    for (int st = 0; st < 2; ++st) {
+    for (int st = 0; st < kBwQdoStages; ++st) {
       mbar_init(qdo_full(st), 1);
       mbar_init(qdo_empty(st), 1);
-      mbar_init(dq_full(st), 1);
-      mbar_init(dq_free(st), 8);
+      mbar_init(stats_full(st), 32);
     }
     mbar_init(st_full, 1);
+    mbar_init(st_free, 8);
     mbar_init(pds_full, 8);
+    mbar_init(pt_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 8);
+    mbar_init(staged, 8);
+    mbar_init(stage_free, 1);
     mbar_init(final_bar, 1);
     fence_barrier_init();
   }
@@ -968,43 +1025,78 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot_ptr);
   const uint32_t tST = tmem, tDPT = tmem + 128, tDV = tmem + 256, tDK = tmem + 320;
-  auto tDQ = [&](int db) { return tmem + 384u + (uint32_t)(db * kHd); };
+  const uint32_t tDQ = tmem + 384, tPT = tmem + 448;
 
   if (warp == 8) {
+    // ------------------- TMA producer and row terms (whole warp) -------------------
+    bool ok = true;
     if (lane == 0) {
-      bool ok = true;
       mbar_expect_tx(kv_full, 2 * kTileBytes);
       tma_load_4d(sK, &tmK, 0, k0, h, b, kv_full);
       tma_load_4d(sV, &tmV, 0, k0, h, b, kv_full);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it & 1;
-        const int q0 = (first_q + it) * kTile;
-        if (!mbar_wait(qdo_empty(st), (uint32_t)(((it >> 1) & 1) ^ 1), a.err)) {
-          ok = false;
-          break;
-        }
+    }
+    for (int it = 0; it < n_it && ok; ++it) {
+      const int st = it % kBwQdoStages;
+      const int q0 = (first_q + it) * kTile;
+      if (!mbar_wait(qdo_empty(st), (uint32_t)(((it / kBwQdoStages) & 1) ^ 1), a.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      if (lane == 0) {
         mbar_expect_tx(qdo_full(st), 2 * kTileBytes);
         tma_load_4d(sQ(st), &tmQ, 0, q0, h, b, qdo_full(st));
         tma_load_4d(sdO(st), &tmdO, 0, q0, h, b, qdo_full(st));
       }
-      for (int it = n_it; it < n_it + 2 && ok; ++it) {
-        const int st = it & 1;
-        if (!mbar_wait(qdo_empty(st), (uint32_t)(((it >> 1) & 1) ^ 1), a.err)) ok = false;
+      // lse (log2 units) and delta of query rows q0 + 4 lane .. +3
+      float* sts = stats(st);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int row = 4 * lane + k, qi = q0 + row;
+        sts[row] = qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
+        sts[kTile + row] = qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
       }
+      mbar_arrive(stats_full(st));
+    }
+    if (lane == 0) {
+      for (int it = n_it; it < n_it + kBwQdoStages && ok; ++it) {
+        const int st = it % kBwQdoStages;
+        if (!mbar_wait(qdo_empty(st), (uint32_t)(((it / kBwQdoStages) & 1) ^ 1), a.err)) ok = false;
+      }
+    }
+  } else if (warp == 10) {
+    // ------------- dQ partial tiles: shared staging -> workspace -------------
+    if (lane == 0) {
+      float* part_base = dq_part + bh * dq_slots(n_t, a.causal) * kDqTileFloats;
+      for (int it = 0; it < n_it; ++it) {
+        if (!mbar_wait(staged, (uint32_t)(it & 1), a.err)) break;
+        bulk_store(part_base + dq_slot(first_q + it, kt, n_t, a.causal) * kDqTileFloats,
+                   sDST(it & 1), kDqTileFloats * 4);
+        bulk_commit_group();
+        bulk_wait_group_read<0>();
+        mbar_arrive(stage_free);
+      }
+      bulk_wait_group_all();  // the partials are in the workspace before exit
     }
   } else if (warp == 9) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
       constexpr uint32_t idG = idesc_bf16_f32(kTile, kHd, 0, 1);   // A K-major, B MN-major
       constexpr uint32_t idQ = idesc_bf16_f32(kTile, kHd, 1, 1);   // A MN-major (dS from dS^T)
+      // Descriptors formed once; each instruction adds an immediate offset.
+      const uint64_t dK_k = desc_k(sK), dV_k = desc_k(sV), dK_mn = desc_mn(sK);
+      const uint64_t dQ_k0 = desc_k(sQ(0)), dO_k0 = desc_k(sdO(0));
+      const uint64_t dQ_mn0 = desc_mn(sQ(0)), dO_mn0 = desc_mn(sdO(0));
+      const uint64_t dS_k0 = desc_k(sDST(0));
+      const uint64_t dS_mn0 = smem_desc_sw128(sDST(0), 16384, 1024);
+      constexpr uint32_t kStage = 2 * kTileBytes;  // bytes between Q/dO stages, dS^T buffers
       auto issue_s = [&](int it) -> bool {
-        const int st = it & 1;
-        if (!mbar_wait(qdo_full(st), (uint32_t)((it >> 1) & 1), a.err)) return false;
+        const int st = it % kBwQdoStages;
+        if (!mbar_wait(qdo_full(st), (uint32_t)((it / kBwQdoStages) & 1), a.err)) return false;
         tc_fence_after();
+        const uint64_t dq = desc_add(dQ_k0, st * kStage), dd = desc_add(dO_k0, st * kStage);
 #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk) {
-          mma_bf16_ss(tST, desc_k(sK + kk * 32), desc_k(sQ(st) + kk * 32), idS, kk > 0 ? 1u : 0u);
-          mma_bf16_ss(tDPT, desc_k(sV + kk * 32), desc_k(sdO(st) + kk * 32), idS,
+          mma_bf16_ss(tST, desc_add(dK_k, kk * 32), desc_add(dq, kk * 32), idS, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tDPT, desc_add(dV_k, kk * 32), desc_add(dd, kk * 32), idS,
                       kk > 0 ? 1u : 0u);
         }
         mma_commit(st_full);
@@ -1013,35 +1105,39 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       bool ok = mbar_wait(kv_full, 0, a.err);
       if (ok && n_it > 0) ok = issue_s(0);
       for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it & 1, pb = it & 1;
+        const int st = it % kBwQdoStages, pb = it & 1;
+        // math(it) holds S^T / dP^T in registers: the next tile's go in
+        if (!mbar_wait(st_free, (uint32_t)(it & 1), a.err)) { ok = false; break; }
+        tc_fence_after();
+        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
         if (!mbar_wait(pds_full, (uint32_t)(it & 1), a.err)) { ok = false; break; }
         tc_fence_after();
-        // dV += P^T dO, dK += dS^T Q with P^T / dS^T read from TMEM: queries
-        // [0, 64) at columns [0, 32), queries [64, 128) at columns [64, 96).
+        // dV += P^T dO (P^T from TMEM), dK += dS^T Q (dS^T K-major from smem)
+        const uint64_t dmn = desc_add(dO_mn0, st * kStage), qmn = desc_add(dQ_mn0, st * kStage);
+        const uint64_t dsk = desc_add(dS_k0, pb * kStage);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t acol = (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
-          mma_bf16_ts(tDV, tST + acol, desc_mn(sdO(st) + kk * 2048), idG,
-                      (it > 0 || kk > 0) ? 1u : 0u);
-          mma_bf16_ts(tDK, tDPT + acol, desc_mn(sQ(st) + kk * 2048), idG,
-                      (it > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          mma_bf16_ts(tDV, tPT + kk * 8, desc_add(dmn, kk * 2048), idG, acc);
+          mma_bf16_ss(tDK, desc_add(dsk, (kk >> 2) * 16384 + (kk & 3) * 32),
+                      desc_add(qmn, kk * 2048), idG, acc);
         }
         mma_commit(qdo_empty(st));
-        // S(it+1) overwrites P^T / dS^T(it): issued after the MMAs reading them
-        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
-        // dQ buffer pb was last used by dQ(it-2); its drain must be done
-        if (it >= 2 && !mbar_wait(dq_free(pb), (uint32_t)(((it - 2) >> 1) & 1), a.err)) {
+        mma_commit(pt_free);
+        // the single dQ accumulator: dQ(it-1) drained before dQ(it)
+        if (it >= 1 && !mbar_wait(dq_free, (uint32_t)((it - 1) & 1), a.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
         // dQ_ij = dS K_j: A = dS^T read MN-major (query blocks of 64 are 16 KB
         // apart), B = K_j MN-major; 16 keys per step = 16 rows of 128 bytes.
+        const uint64_t dsm = desc_add(dS_mn0, pb * kStage);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          mma_bf16_ss(tDQ(pb), smem_desc_sw128(sDST(pb) + kk * 2048, 16384, 1024),
-                      desc_mn(sK + kk * 2048), idQ, kk > 0 ? 1u : 0u);
-        mma_commit(dq_full(pb));
+          mma_bf16_ss(tDQ, desc_add(dsm, kk * 2048), desc_add(dK_mn, kk * 2048), idQ,
+                      kk > 0 ? 1u : 0u);
+        mma_commit(dq_full);
       }
       mma_commit(final_bar);
       mbar_wait(final_bar, 0, a.err);
@@ -1054,103 +1150,119 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int cbase = half * 64;        // this thread's query columns [cbase, cbase + 64)
     const float sl2 = a.scale * kLog2e;
-    const int64_t bh = (int64_t)b * a.H + h;
-    float* part_base = dq_part + bh * dq_slots(n_t, a.causal) * kDqTileFloats;
-    const int t = threadIdx.x;  // 0..255: lse (t < 128) or delta of query row t & 127
-    auto load_stat = [&](int it) -> float {
-      const int qi = (first_q + it) * kTile + (t & 127);
-      if (t < 128) return qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
-      return qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
-    };
-    // Drains dQ(it) (TMEM buffer it & 1): row r, column groups 8*half .. +8.
+    // Drains dQ(it) (row r, column groups 8*half .. +8) into dS^T buffer
+    // it & 1, free since dQ(it) completed, in the partial-tile layout (float4
+    // index (column / 4) * 128 + row); warp 10 sends it on.
     auto drain = [&](int it, bool ok) -> bool {
-      const int db = it & 1;
-      if (ok && !mbar_wait(dq_full(db), (uint32_t)((it >> 1) & 1), a.err)) ok = false;
+      if (ok && !mbar_wait(dq_full, (uint32_t)(it & 1), a.err)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) return false;
       tc_fence_after();
       uint32_t v[32];
-      tmem_ld32(tDQ(db) + lane_off + half * 32, v);
+      tmem_ld32(tDQ + lane_off + half * 32, v);
       tmem_wait_ld();
-      float4* dst = reinterpret_cast<float4*>(
-          part_base + dq_slot(first_q + it, kt, n_t, a.causal) * kDqTileFloats);
-#pragma unroll
-      for (int g = 0; g < 8; ++g)
-        dst[(half * 8 + g) * kTile + r] =
-            make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
-                        __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free(db));
+      if (lane == 0) mbar_arrive(dq_free);
+      const uint32_t stage = sDST(it & 1);
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        st_shared_v4(stage + (uint32_t)(((half * 8 + g) * kTile + r) * 16), v[4 * g],
+                     v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(staged);
       return true;
     };
     bool ok = true;
-    float stat = n_it > 0 ? load_stat(0) : 0.f;
     for (int it = 0; it < n_it; ++it) {
-      const int pb = it & 1;
+      const int st = it % kBwQdoStages, pb = it & 1;
       const int qt = first_q + it;
       const int q0 = qt * kTile;
-      (t < 128 ? lse_s[t] : delta_s[t - 128]) = stat;
-      if (it + 1 < n_it) stat = load_stat(it + 1);  // lands during this tile
-      named_barrier(1, 256);
       if (ok && !mbar_wait(st_full, (uint32_t)(it & 1), a.err)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        const bool diag = a.causal && qt == kt;
-        const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
-        // P^T and dS^T for this thread's 64 query columns, 32 at a time; the
-        // masked variant only runs on the diagonal tile and a ragged edge.
-        auto chunk = [&](auto masked_c, int c) {
-          constexpr bool kMasked = decltype(masked_c)::value;
-          const int col = cbase + 32 * c;
-          uint32_t vs[32], vd[32];
-          tmem_ld32(tST + lane_off + col, vs);
-          tmem_ld32(tDPT + lane_off + col, vd);
-          const float4* l4 = reinterpret_cast<const float4*>(lse_s + col);
-          const float4* d4 = reinterpret_cast<const float4*>(delta_s + col);
-          tmem_wait_ld();
-          uint32_t pp[16], pd[16];
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            const float4 lv = l4[g], dv4 = d4[g];
-            const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
-            const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
-            float pe[4], de[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int e = 4 * g + u;
-              pe[u] = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
-              de[u] = pe[u] * (__uint_as_float(vd[e]) - dl[u]);
-              if (kMasked) {
-                const int qg = q0 + col + e;
-                if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe[u] = de[u] = 0.f;
-              }
-            }
-            pp[2 * g] = pack_bf16(pe[0], pe[1]);
-            pp[2 * g + 1] = pack_bf16(pe[2], pe[3]);
-            pd[2 * g] = pack_bf16(de[0], de[1]);
-            pd[2 * g + 1] = pack_bf16(de[2], de[3]);
-          }
-          // BF16 columns [64*half + 16*c, +16): S^T / dP^T columns this thread
-          // has already read
-          tmem_st16(tST + lane_off + cbase + 16 * c, pp);
-          tmem_st16(tDPT + lane_off + cbase + 16 * c, pd);
-          store_row_packed(sDST(pb), r, col >> 5, pd);
-        };
-        if (diag || tail) {
-          chunk(std::true_type{}, 0);
-          chunk(std::true_type{}, 1);
-        } else {
-          chunk(std::false_type{}, 0);
-          chunk(std::false_type{}, 1);
-        }
-        tmem_wait_st();
-        fence_proxy_async_smem();
+        // this thread's 64 columns of S^T and dP^T, then the columns are free
+        uint32_t vs0[32], vs1[32], vd0[32], vd1[32];
+        tmem_ld32(tST + lane_off + cbase, vs0);
+        tmem_ld32(tST + lane_off + cbase + 32, vs1);
+        tmem_ld32(tDPT + lane_off + cbase, vd0);
+        tmem_ld32(tDPT + lane_off + cbase + 32, vd1);
+        tmem_wait_ld();
         tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(st_free);
+        // row terms of this tile; P^T's TMEM columns read by dV(it-1)
+        if (!mbar_wait(stats_full(st), (uint32_t)((it / kBwQdoStages) & 1), a.err)) ok = false;
+        if (it >= 1 && !mbar_wait(pt_free, (uint32_t)((it - 1) & 1), a.err)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          const float* lse_s = stats(st);
+          const float* delta_s = lse_s + kTile;
+          const bool diag = a.causal && qt == kt;
+          const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
+          // P^T (to TMEM) and dS^T (packed, kept in pd) for 32 of this
+          // thread's query columns; the masked variant only runs on the
+          // diagonal tile and a ragged edge.
+          auto chunk = [&](auto masked_c, auto c_c, const uint32_t(&vs)[32],
+                           const uint32_t(&vd)[32], uint32_t(&pd)[16]) {
+            constexpr bool kMasked = decltype(masked_c)::value;
+            constexpr int c = decltype(c_c)::value;
+            const int col = cbase + 32 * c;
+            const float4* l4 = reinterpret_cast<const float4*>(lse_s + col);
+            const float4* d4 = reinterpret_cast<const float4*>(delta_s + col);
+            uint32_t pp[16];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const float4 lv = l4[g], dv4 = d4[g];
+              const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
+              const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
+              float pe[4], de[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int e = 4 * g + u;
+                pe[u] = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
+                de[u] = pe[u] * (__uint_as_float(vd[e]) - dl[u]);
+                if (kMasked) {
+                  const int qg = q0 + col + 4 * g + u;
+                  if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe[u] = de[u] = 0.f;
+                }
+              }
+              pp[2 * g] = pack_bf16(pe[0], pe[1]);
+              pp[2 * g + 1] = pack_bf16(pe[2], pe[3]);
+              pd[2 * g] = pack_bf16(de[0], de[1]);
+              pd[2 * g + 1] = pack_bf16(de[2], de[3]);
+            }
+            // P^T: queries [64 half + 32 c, +32) = TMEM columns 32 half + 16 c
+            tmem_st16(tPT + lane_off + 32 * half + 16 * c, pp);
+          };
+          using c0 = std::integral_constant<int, 0>;
+          using c1 = std::integral_constant<int, 1>;
+          uint32_t pd0[16], pd1[16];
+          if (diag || tail) {
+            chunk(std::true_type{}, c0{}, vs0, vd0, pd0);
+            chunk(std::true_type{}, c1{}, vs1, vd1, pd1);
+          } else {
+            chunk(std::false_type{}, c0{}, vs0, vd0, pd0);
+            chunk(std::false_type{}, c1{}, vs1, vd1, pd1);
+          }
+          // dS^T buffer pb was last the staging of dQ(it-2): its bulk copy has
+          // read it (issued a tile ago, so this wait is normally satisfied)
+          if (it >= 2 && !mbar_wait(stage_free, (uint32_t)(it & 1), a.err)) ok = false;
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            store_row_packed(sDST(pb), r, cbase >> 5, pd0);
+            store_row_packed(sDST(pb), r, (cbase >> 5) + 1, pd1);
+          }
+          tmem_wait_st();
+          fence_proxy_async_smem();
+          tc_fence_before();
+          __syncwarp();
+          if (ok && lane == 0) mbar_arrive(pds_full);
+        }
       }
-      named_barrier(2, 256);  // every thread is done with the row terms of this tile
-      if (ok && lane == 0) mbar_arrive(pds_full);
       if (it >= 1) ok = drain(it - 1, ok) && ok;
     }
     if (n_it >= 1) ok = drain(n_it - 1, ok) && ok;
@@ -1352,7 +1464,8 @@ magma_status_t attention_bwd_tc(const void* q, const void* k, const void* v, con
   a.err = device_error_word();
   dim3 grid((unsigned)ceil_div(S, kTile), (unsigned)H, (unsigned)B);
   const size_t dbytes = attention_bwd_tc_delta_bytes(B, H, S);
-  if (ws_bytes >= dbytes + attention_bwd_tc_partials_bytes(B, H, S, causal)) {
+  if (ws_bytes >= dbytes + attention_bwd_tc_partials_bytes(B, H, S, causal) &&
+      aligned16(workspace)) {
     float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dbytes);
     if (magma_status_t st = set_smem_attr<3>(attn_bwd_tc, kBwSmem)) return st;
     attn_bwd_tc<<<grid, kBwThreads, kBwSmem, s>>>(mq, mk, mv, mdo, a, part);

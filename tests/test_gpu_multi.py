@@ -1,7 +1,8 @@
 """Data parallelism on two GPUs through the library's collectives (needs 2 GPUs).
 
 Two ranks (one process per GPU, NCCL under the C ABI, NVLS off) train the same
-small GPT from the same initial parameters on different token batches:
+small GPT from the same initial parameters on different token batches, in the
+two data-parallel forms:
 
 * replicated: the gradient of each finished backward segment is all-reduced
   (GradSync) and every rank runs the full Adam step with grad_scale 1/2 — the
@@ -9,8 +10,22 @@ small GPT from the same initial parameters on different token batches:
 * sharded (ZeRO stage 1): the segments are reduce-scattered (ShardSync), each
   rank runs Adam on its half, the parameters are all-gathered.
 
-After three steps both ranks of each mode hold identical parameters, and the
-two modes agree to F32 rounding of the summation order (1e-6 of the norm).
+What must hold, and how exactly:
+
+* the backward is deterministic, and the reduce-scattered gradient slice a
+  rank owns equals the all-reduced gradient there bit for bit (with two ranks
+  both are the same a + b per element);
+* one optimiser step from the same state gives the same parameters in both
+  forms up to the summation order of the global gradient norm (the sharded
+  form adds per-slice sums of squares): within 1e-6 of the parameter norm;
+* over three F32 steps the two forms stay within 1e-5 (no BF16 rounding of
+  the weights between steps);
+* over three BF16 steps both replicas of each form stay identical, and the
+  two forms agree to the BF16 weight rounding: a parameter one ulp apart
+  can round to a different BF16 weight, which changes the next gradients at
+  the 1e-3 level, and Adam's normalisation carries that into the small
+  updates (measured 2.7e-4 of the parameter norm after three steps);
+  the losses agree within 1e-3.
 """
 import os
 import socket
@@ -33,6 +48,13 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _trainer(precision):
+    from magma_b200.gpt import GPTConfig, GPTTrainer
+
+    return GPTTrainer(GPTConfig(**KW), 2, precision, lr=1e-3, seed=0, weight_decay=0.1,
+                      grad_clip=0.5)
+
+
 def _rank_main(rank, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE="2", LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -40,7 +62,6 @@ def _rank_main(rank, port, q):
         import torch.distributed as dist
 
         from magma_b200 import dp
-        from magma_b200.gpt import GPTConfig, GPTTrainer
 
         dp.init_from_env(backend="nccl", timeout_s=60)
         torch.cuda.set_device(rank)
@@ -49,21 +70,56 @@ def _rank_main(rank, port, q):
         tok = torch.randint(0, KW["vocab"], (2, KW["seq"]), generator=g, dtype=torch.int32)
         tgt = torch.randint(0, KW["vocab"], (2, KW["seq"]), generator=g, dtype=torch.int32)
         out = {}
-        for mode in ("replicated", "sharded"):
-            tr = GPTTrainer(GPTConfig(**KW), 2, "bf16", lr=1e-3, seed=0, weight_decay=0.1,
-                            grad_clip=0.5)
-            tr.set_batch(tok, tgt)
-            tr.capture()
-            sync = dp.GradSync(comm=comm) if mode == "replicated" else dp.ShardSync(comm)
-            for _ in range(3):
-                scale = tr.run_fwd_bwd(sync=sync)
-                if mode == "replicated":
-                    tr.optimizer_step(grad_scale=scale)
-                else:
-                    tr.optimizer_step_sharded(sync)
-            torch.cuda.synchronize()
-            out[mode] = tr.params.cpu().numpy()
-            out[mode + "_loss"] = float(tr.loss.item())
+
+        # gradients and one step from the same state (BF16 trainer)
+        tr = _trainer("bf16")
+        tr.set_batch(tok, tgt)
+        tr.capture()
+        tr.run_fwd_bwd()
+        g_local = tr.grads.clone()
+        tr.run_fwd_bwd()
+        out["deterministic"] = bool(torch.equal(g_local, tr.grads))
+        rep_sync, shard_sync = dp.GradSync(comm=comm), dp.ShardSync(comm)
+        tr.run_fwd_bwd(sync=rep_sync)
+        g_rep = tr.grads.clone()
+        tr.run_fwd_bwd(sync=shard_sync)
+        torch.cuda.synchronize()
+        ranges = [r for seg in tr.segment_ranges() for r in seg]
+        owned_equal = True
+        for lo, hi in ranges:
+            a, b = shard_sync.owned(lo, hi)
+            owned_equal &= bool(torch.equal(tr.grads[a:b], g_rep[a:b]))
+        out["owned_equal"] = owned_equal
+        g_shard = tr.grads.clone()
+        state = [t.clone() for t in (tr.params, tr.m, tr.v)]
+        tr.grads.copy_(g_rep)
+        tr.optimizer_step(grad_scale=0.5)
+        torch.cuda.synchronize()
+        out["step1_replicated"] = tr.params.cpu().numpy()
+        for t, s in zip((tr.params, tr.m, tr.v), state):
+            t.copy_(s)
+        tr.t = 0
+        tr.grads.copy_(g_shard)
+        tr.optimizer_step_sharded(shard_sync)
+        torch.cuda.synchronize()
+        out["step1_sharded"] = tr.params.cpu().numpy()
+
+        # three steps in each form, F32 and BF16
+        for precision in ("f32", "bf16"):
+            for mode in ("replicated", "sharded"):
+                tr = _trainer(precision)
+                tr.set_batch(tok, tgt)
+                tr.capture()
+                sync = dp.GradSync(comm=comm) if mode == "replicated" else dp.ShardSync(comm)
+                for _ in range(3):
+                    scale = tr.run_fwd_bwd(sync=sync)
+                    if mode == "replicated":
+                        tr.optimizer_step(grad_scale=scale)
+                    else:
+                        tr.optimizer_step_sharded(sync)
+                torch.cuda.synchronize()
+                out[f"{precision}_{mode}"] = tr.params.cpu().numpy()
+                out[f"{precision}_{mode}_loss"] = float(tr.loss.item())
         comm.destroy()
         dist.barrier()
         dist.destroy_process_group()
@@ -72,6 +128,11 @@ def _rank_main(rank, port, q):
         import traceback
 
         q.put((rank, traceback.format_exc() + repr(e)))
+
+
+def _rel(a, b):
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    return float(np.linalg.norm(a64 - b64) / np.linalg.norm(b64))
 
 
 def test_two_gpu_replicated_and_sharded_steps_agree():
@@ -94,11 +155,13 @@ def test_two_gpu_replicated_and_sharded_steps_agree():
     for rank, out in res.items():
         assert isinstance(out, dict), out
     a, b = res[0], res[1]
-    # replicas stay in sync in both modes
-    assert np.array_equal(a["replicated"], b["replicated"])
-    assert np.array_equal(a["sharded"], b["sharded"])
-    # the two modes agree to the summation order
-    d = np.linalg.norm(a["sharded"].astype(np.float64) - a["replicated"])
-    assert d <= 1e-6 * np.linalg.norm(a["replicated"].astype(np.float64)), d
-    # and the step changed the parameters
-    assert a["replicated_loss"] == pytest.approx(a["sharded_loss"], rel=1e-5)
+    for r in (a, b):
+        assert r["deterministic"]
+        assert r["owned_equal"]
+        assert _rel(r["step1_sharded"], r["step1_replicated"]) <= 1e-6
+    for key in ("f32_replicated", "f32_sharded", "bf16_replicated", "bf16_sharded"):
+        assert np.array_equal(a[key], b[key]), key  # replicas stay in sync
+    assert _rel(a["f32_sharded"], a["f32_replicated"]) <= 1e-5
+    assert _rel(a["bf16_sharded"], a["bf16_replicated"]) <= 1e-3
+    assert a["bf16_sharded_loss"] == pytest.approx(a["bf16_replicated_loss"], rel=1e-3)
+    assert a["f32_sharded_loss"] == pytest.approx(a["f32_replicated_loss"], rel=1e-5)

@@ -893,23 +893,38 @@ attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // is the K-major A operand of dK and, read MN-major, the A operand of dQ. The
 // dQ partials are summed over j in a fixed order by attn_dq_reduce
 // (deterministic; no atomics).
+// Persistent: one CTA per SM walks a static list of work units (a key tile of
+// one head), heaviest first, in a snake order over the CTAs (round r takes
+// units r*G .. r*G+G-1, even rounds in CTA order, odd rounds reversed), which
+// balances the causal units' unequal sizes to within a few per cent of the
+// mean. Pipelines run on across units: the producer prefetches the next
+// unit's K (double-buffered) and V (single, reloaded once the unit's last
+// S^T/dP^T have read it) and its Q / dO stages while the current unit ends.
 // Warps 0-7: element math, thread = key row (TMEM lane quarter warp % 4) x
 // one half of the 128 query columns (warp / 4); warp 8: TMA producer, which
 // also stages each query tile's row terms (lse in log2 units, delta); warp 9:
 // TMEM allocator and MMA issuer; warp 10: sends the dQ partial tiles to the
 // workspace with bulk copies.
 constexpr int kBwThreads = 352;
-constexpr int kBwK = 0;
-constexpr int kBwV = kTileBytes;
 constexpr int kBwQdoStages = 3;
-constexpr int kBwQdo = 2 * kTileBytes;                      // 3 stages x (Q, dO)
+constexpr int kBwK = 0;                                     // 2 buffers x 16 KB
+constexpr int kBwV = 2 * kTileBytes;
+constexpr int kBwQdo = 3 * kTileBytes;                      // 3 stages x (Q, dO)
 constexpr int kBwDST = kBwQdo + kBwQdoStages * 2 * kTileBytes;  // 2 buffers x 32 KB
 constexpr int kBwStats = kBwDST + 2 * 2 * kTileBytes;       // 3 stages x (lse2[128], delta[128])
 constexpr int kBwBar = kBwStats + kBwQdoStages * 2 * kTile * 4;
-// kv_full, qdo_full[3], qdo_empty[3], stats_full[3], st_full, st_free, pds_full, pt_free,
-// dq_full, dq_free, staged, stage_free, final
-constexpr int kBwNumBars = 19;
+// k_full[2], k_empty[2], v_full, v_empty, qdo_full[3], qdo_empty[3], stats_full[3],
+// st_full, st_free, pds_full, pt_free, dq_full, dq_free, staged, stage_free,
+// acc_full, acc_empty, final
+constexpr int kBwNumBars = 26;
 constexpr int kBwSmem = kBwBar + kBwNumBars * 8 + 16 + 1024;
+static_assert(kBwSmem <= 232448, "backward shared memory");
+
+// The r-th unit of CTA c among G CTAs (snake order), or -1 past the end.
+__device__ __forceinline__ int bw_unit(int r, int c, int G, int U) {
+  const int u = r * G + ((r & 1) ? G - 1 - c : c);
+  return u < U ? u : -1;
+}
 constexpr int kDqTileFloats = kTile * kHd;                  // one F32 dQ partial tile
 
 // Index of the dQ partial of (query tile i, key tile j) among a head's slots.
@@ -933,24 +948,26 @@ __device__ __forceinline__ void store_row_packed(uint32_t base, int r, int c32,
                  pk[4 * q + 3]);
 }
 
-// Pipeline over query tiles it = 0, 1, ... (TC = tensor-core issue order):
-//   TC:    S(0) | S(it+1) dV(it) dK(it) dQ(it) | S(it+2) dV(it+1) ...
-//   math:  load S^T, dP^T(it) -> [S^T/dP^T free] -> P^T, dS^T -> [ready]
-//          -> drain dQ(it-1) -> load S^T, dP^T(it+1) -> ...
+// Pipeline over the CTA's query-tile iterations g = 0, 1, ... (across its
+// units; TC = tensor-core issue order):
+//   TC:    S(0) | S(g+1) dV(g) dK(g) dQ(g) | S(g+2) dV(g+1) ...
+//   math:  load S^T, dP^T(g) -> [S^T/dP^T free] -> P^T, dS^T -> [ready]
+//          -> drain dQ(g-1) -> load S^T, dP^T(g+1) -> ...   (and, after a
+//          unit's last iteration, dV / dK of the unit -> [accumulators free])
 // Each math thread loads its 64 columns of S^T and dP^T into registers and
-// releases those TMEM columns at once (st_free), so S(it+1) and dP(it+1) run
-// on the tensor cores while it computes P^T and dS^T of tile it. P^T goes to
+// releases those TMEM columns at once (st_free), so S(g+1) and dP(g+1) run on
+// the tensor cores while it computes P^T and dS^T of iteration g. P^T goes to
 // its own 64 TMEM columns (BF16 pairs; the TMEM A operand of dV), dS^T to a
 // double-buffered 128-byte-swizzled shared tile (the K-major A operand of dK
-// and, read MN-major, of dQ). Once dQ(it) has completed, dS^T buffer it & 1
-// is free: the drain of dQ(it) writes the F32 partial tile there in the
+// and, read MN-major, of dQ). Once dQ(g) has completed, dS^T buffer g & 1 is
+// free: the drain of dQ(g) writes the F32 partial tile there in the
 // workspace layout and warp 10 sends it out with one bulk copy, releasing the
-// buffer (stage_free) when the copy has read it; math(it+2) waits for that
-// before writing its dS^T. The row terms of each query tile arrive with its
-// Q / dO stage (stats_full). The math warps wait only on mbarriers.
-// P^T's TMEM columns are rewritten one tile later, after pt_free (committed
-// after dV(it)); the single dQ accumulator is drained (dq_free) before dQ(it+1)
-// is issued.
+// buffer (stage_free) when the copy has read it; the dS^T of iteration g+2
+// waits for that. The row terms of each query tile arrive with its Q / dO
+// stage (stats_full). P^T's TMEM columns are rewritten one iteration later,
+// after pt_free (committed after dV(g)); the single dQ accumulator is drained
+// (dq_free) before dQ(g+1) is issued; a unit's first dV / dK wait until the
+// previous unit's have been read out (acc_empty).
 // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384),
 // dQ [384,448), P^T [448,512).
 __global__ void __launch_bounds__(kBwThreads, 1)
@@ -960,49 +977,68 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sp;
   const uint32_t base = align1024(smem_raw, &sp);
-  const uint32_t sK = base + kBwK, sV = base + kBwV;
+  auto sK = [&](int kb) { return base + kBwK + kb * kTileBytes; };
+  const uint32_t sV = base + kBwV;
   auto sQ = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes; };
   auto sdO = [&](int st) { return base + kBwQdo + st * 2 * kTileBytes + kTileBytes; };
   auto sDST = [&](int pb) { return base + kBwDST + pb * 2 * kTileBytes; };
   // row terms of stage st: lse (log2 units) [128], then delta [128]
   auto stats = [&](int st) { return reinterpret_cast<float*>(sp + kBwStats + st * 2 * kTile * 4); };
   const uint32_t bars = base + kBwBar;
-  const uint32_t kv_full = bars;
-  auto qdo_full = [&](int st) { return bars + 8u * (1 + st); };
-  auto qdo_empty = [&](int st) { return bars + 8u * (4 + st); };
-  auto stats_full = [&](int st) { return bars + 8u * (7 + st); };
-  const uint32_t st_full = bars + 8u * 10;
-  const uint32_t st_free = bars + 8u * 11;
-  const uint32_t pds_full = bars + 8u * 12;
-  const uint32_t pt_free = bars + 8u * 13;
-  const uint32_t dq_full = bars + 8u * 14;
-  const uint32_t dq_free = bars + 8u * 15;
-  const uint32_t staged = bars + 8u * 16;
-  const uint32_t stage_free = bars + 8u * 17;
-  const uint32_t final_bar = bars + 8u * 18;
+  auto k_full = [&](int kb) { return bars + 8u * kb; };
+  auto k_empty = [&](int kb) { return bars + 8u * (2 + kb); };
+  const uint32_t v_full = bars + 8u * 4;
+  const uint32_t v_empty = bars + 8u * 5;
+  auto qdo_full = [&](int st) { return bars + 8u * (6 + st); };
+  auto qdo_empty = [&](int st) { return bars + 8u * (9 + st); };
+  auto stats_full = [&](int st) { return bars + 8u * (12 + st); };
+  const uint32_t st_full = bars + 8u * 15;
+  const uint32_t st_free = bars + 8u * 16;
+  const uint32_t pds_full = bars + 8u * 17;
+  const uint32_t pt_free = bars + 8u * 18;
+  const uint32_t dq_full = bars + 8u * 19;
+  const uint32_t dq_free = bars + 8u * 20;
+  const uint32_t staged = bars + 8u * 21;
+  const uint32_t stage_free = bars + 8u * 22;
+  const uint32_t acc_full = bars + 8u * 23;
+  const uint32_t acc_empty = bars + 8u * 24;
+  const uint32_t final_bar = bars + 8u * 25;
   const uint32_t tslot = bars + 8u * kBwNumBars;
   uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kBwBar + 8 * kBwNumBars);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_t = (a.S + kTile - 1) / kTile;
-  // Linear dispatch order with the key tile varying slowest: key tile 0 has
-  // the most query tiles under causal, so the heaviest blocks start first and
-  // the lightest fill the tail.
-  const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
-  const int heads = (int)(gridDim.y * gridDim.z);
-  const int kt = lin / heads;
-  const int h = (lin % heads) % (int)gridDim.y, b = (lin % heads) / (int)gridDim.y;
-  const int k0 = kt * kTile;
-  const int first_q = a.causal ? kt : 0;
-  const int n_it = n_t - first_q;
-  const int64_t bh = (int64_t)b * a.H + h;
+  const int heads = a.H * a.B;
+  const int U = n_t * heads;
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  // unit u: key tile u / heads (varying slowest: heaviest causal units first)
+  struct Unit {
+    int kt, h, b, first_q, n_it;
+    int64_t bh;
+  };
+  auto unit = [&](int u) {
+    Unit w;
+    w.kt = u / heads;
+    const int hb = u % heads;
+    w.h = hb % a.H;
+    w.b = hb / a.H;
+    w.first_q = a.causal ? w.kt : 0;
+    w.n_it = n_t - w.first_q;
+    w.bh = (int64_t)w.b * a.H + w.h;
+    return w;
+  };
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
     prefetch_tensormap(&tmdO);
-    mbar_init(kv_full, 1);
+    for (int kb = 0; kb < 2; ++kb) {
+      mbar_init(k_full(kb), 1);
+      mbar_init(k_empty(kb), 1);
+    }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
     for (int st = 0; st < kBwQdoStages; ++st) {
       mbar_init(qdo_full(st), 1);
       mbar_init(qdo_empty(st), 1);
@@ -1016,6 +1052,8 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     mbar_init(dq_free, 8);
     mbar_init(staged, 8);
     mbar_init(stage_free, 1);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 8);
     mbar_init(final_bar, 1);
     fence_barrier_init();
   }
@@ -1030,49 +1068,73 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   if (warp == 8) {
     // ------------------- TMA producer and row terms (whole warp) -------------------
     bool ok = true;
-    if (lane == 0) {
-      mbar_expect_tx(kv_full, 2 * kTileBytes);
-      tma_load_4d(sK, &tmK, 0, k0, h, b, kv_full);
-      tma_load_4d(sV, &tmV, 0, k0, h, b, kv_full);
-    }
-    for (int it = 0; it < n_it && ok; ++it) {
-      const int st = it % kBwQdoStages;
-      const int q0 = (first_q + it) * kTile;
-      if (!mbar_wait(qdo_empty(st), (uint32_t)(((it / kBwQdoStages) & 1) ^ 1), a.err)) ok = false;
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
+    int g = 0;
+    for (int r = 0;; ++r) {
+      const int u = bw_unit(r, c, G, U);
+      if (u < 0) break;
+      const Unit w = unit(u);
+      const int kb = r & 1;
       if (lane == 0) {
-        mbar_expect_tx(qdo_full(st), 2 * kTileBytes);
-        tma_load_4d(sQ(st), &tmQ, 0, q0, h, b, qdo_full(st));
-        tma_load_4d(sdO(st), &tmdO, 0, q0, h, b, qdo_full(st));
+        // K buffer kb was last read by unit r-2, V by unit r-1
+        if (!mbar_wait(k_empty(kb), (uint32_t)(((r >> 1) & 1) ^ 1), a.err)) ok = false;
+        if (ok) {
+          mbar_expect_tx(k_full(kb), kTileBytes);
+          tma_load_4d(sK(kb), &tmK, 0, w.kt * kTile, w.h, w.b, k_full(kb));
+        }
+        if (ok && !mbar_wait(v_empty, (uint32_t)((r & 1) ^ 1), a.err)) ok = false;
+        if (ok) {
+          mbar_expect_tx(v_full, kTileBytes);
+          tma_load_4d(sV, &tmV, 0, w.kt * kTile, w.h, w.b, v_full);
+        }
       }
-      // lse (log2 units) and delta of query rows q0 + 4 lane .. +3
-      float* sts = stats(st);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      for (int it = 0; it < w.n_it && ok; ++it, ++g) {
+        const int st = g % kBwQdoStages;
+        const int q0 = (w.first_q + it) * kTile;
+        if (!mbar_wait(qdo_empty(st), (uint32_t)(((g / kBwQdoStages) & 1) ^ 1), a.err)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_expect_tx(qdo_full(st), 2 * kTileBytes);
+          tma_load_4d(sQ(st), &tmQ, 0, q0, w.h, w.b, qdo_full(st));
+          tma_load_4d(sdO(st), &tmdO, 0, q0, w.h, w.b, qdo_full(st));
+        }
+        // lse (log2 units) and delta of query rows q0 + 4 lane .. +3
+        float* sts = stats(st);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int row = 4 * lane + k, qi = q0 + row;
-        sts[row] = qi < a.S ? a.lse[bh * a.S + qi] * kLog2e : INFINITY;
-        sts[kTile + row] = qi < a.S ? a.delta[bh * a.S + qi] : 0.f;
+        for (int k = 0; k < 4; ++k) {
+          const int row = 4 * lane + k, qi = q0 + row;
+          sts[row] = qi < a.S ? a.lse[w.bh * a.S + qi] * kLog2e : INFINITY;
+          sts[kTile + row] = qi < a.S ? a.delta[w.bh * a.S + qi] : 0.f;
+        }
+        mbar_arrive(stats_full(st));
       }
-      mbar_arrive(stats_full(st));
+      if (!ok) break;
     }
-    if (lane == 0) {
-      for (int it = n_it; it < n_it + kBwQdoStages && ok; ++it) {
-        const int st = it % kBwQdoStages;
-        if (!mbar_wait(qdo_empty(st), (uint32_t)(((it / kBwQdoStages) & 1) ^ 1), a.err)) ok = false;
+    if (lane == 0) {  // every stage loaded above has been consumed before the producer leaves
+      for (int k = g; k < g + kBwQdoStages && ok; ++k) {
+        const int st = k % kBwQdoStages;
+        if (!mbar_wait(qdo_empty(st), (uint32_t)(((k / kBwQdoStages) & 1) ^ 1), a.err)) ok = false;
       }
     }
   } else if (warp == 10) {
     // ------------- dQ partial tiles: shared staging -> workspace -------------
     if (lane == 0) {
-      float* part_base = dq_part + bh * dq_slots(n_t, a.causal) * kDqTileFloats;
-      for (int it = 0; it < n_it; ++it) {
-        if (!mbar_wait(staged, (uint32_t)(it & 1), a.err)) break;
-        bulk_store(part_base + dq_slot(first_q + it, kt, n_t, a.causal) * kDqTileFloats,
-                   sDST(it & 1), kDqTileFloats * 4);
-        bulk_commit_group();
-        bulk_wait_group_read<0>();
-        mbar_arrive(stage_free);
+      bool ok = true;
+      int g = 0;
+      for (int r = 0; ok; ++r) {
+        const int u = bw_unit(r, c, G, U);
+        if (u < 0) break;
+        const Unit w = unit(u);
+        float* part_base = dq_part + w.bh * dq_slots(n_t, a.causal) * kDqTileFloats;
+        for (int it = 0; it < w.n_it; ++it, ++g) {
+          if (!mbar_wait(staged, (uint32_t)(g & 1), a.err)) { ok = false; break; }
+          bulk_store(part_base + dq_slot(w.first_q + it, w.kt, n_t, a.causal) * kDqTileFloats,
+                     sDST(g & 1), kDqTileFloats * 4);
+          bulk_commit_group();
+          bulk_wait_group_read<0>();
+          mbar_arrive(stage_free);
+        }
       }
       bulk_wait_group_all();  // the partials are in the workspace before exit
     }
@@ -1082,62 +1144,90 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       constexpr uint32_t idG = idesc_bf16_f32(kTile, kHd, 0, 1);   // A K-major, B MN-major
       constexpr uint32_t idQ = idesc_bf16_f32(kTile, kHd, 1, 1);   // A MN-major (dS from dS^T)
       // Descriptors formed once; each instruction adds an immediate offset.
-      const uint64_t dK_k = desc_k(sK), dV_k = desc_k(sV), dK_mn = desc_mn(sK);
+      const uint64_t dK_k0 = desc_k(sK(0)), dK_mn0 = desc_mn(sK(0)), dV_k = desc_k(sV);
       const uint64_t dQ_k0 = desc_k(sQ(0)), dO_k0 = desc_k(sdO(0));
       const uint64_t dQ_mn0 = desc_mn(sQ(0)), dO_mn0 = desc_mn(sdO(0));
       const uint64_t dS_k0 = desc_k(sDST(0));
       const uint64_t dS_mn0 = smem_desc_sw128(sDST(0), 16384, 1024);
       constexpr uint32_t kStage = 2 * kTileBytes;  // bytes between Q/dO stages, dS^T buffers
-      auto issue_s = [&](int it) -> bool {
-        const int st = it % kBwQdoStages;
-        if (!mbar_wait(qdo_full(st), (uint32_t)((it / kBwQdoStages) & 1), a.err)) return false;
+      auto issue_s = [&](int g, uint64_t dkk) -> bool {
+        const int st = g % kBwQdoStages;
+        if (!mbar_wait(qdo_full(st), (uint32_t)((g / kBwQdoStages) & 1), a.err)) return false;
         tc_fence_after();
         const uint64_t dq = desc_add(dQ_k0, st * kStage), dd = desc_add(dO_k0, st * kStage);
 #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk) {
-          mma_bf16_ss(tST, desc_add(dK_k, kk * 32), desc_add(dq, kk * 32), idS, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tST, desc_add(dkk, kk * 32), desc_add(dq, kk * 32), idS, kk > 0 ? 1u : 0u);
           mma_bf16_ss(tDPT, desc_add(dV_k, kk * 32), desc_add(dd, kk * 32), idS,
                       kk > 0 ? 1u : 0u);
         }
         mma_commit(st_full);
         return true;
       };
-      bool ok = mbar_wait(kv_full, 0, a.err);
-      if (ok && n_it > 0) ok = issue_s(0);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it % kBwQdoStages, pb = it & 1;
-        // math(it) holds S^T / dP^T in registers: the next tile's go in
-        if (!mbar_wait(st_free, (uint32_t)(it & 1), a.err)) { ok = false; break; }
-        tc_fence_after();
-        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
-        if (!mbar_wait(pds_full, (uint32_t)(it & 1), a.err)) { ok = false; break; }
-        tc_fence_after();
-        // dV += P^T dO (P^T from TMEM), dK += dS^T Q (dS^T K-major from smem)
-        const uint64_t dmn = desc_add(dO_mn0, st * kStage), qmn = desc_add(dQ_mn0, st * kStage);
-        const uint64_t dsk = desc_add(dS_k0, pb * kStage);
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          mma_bf16_ts(tDV, tPT + kk * 8, desc_add(dmn, kk * 2048), idG, acc);
-          mma_bf16_ss(tDK, desc_add(dsk, (kk >> 2) * 16384 + (kk & 3) * 32),
-                      desc_add(qmn, kk * 2048), idG, acc);
-        }
-        mma_commit(qdo_empty(st));
-        mma_commit(pt_free);
-        // the single dQ accumulator: dQ(it-1) drained before dQ(it)
-        if (it >= 1 && !mbar_wait(dq_free, (uint32_t)((it - 1) & 1), a.err)) {
+      bool ok = true;
+      int g = 0;
+      for (int r = 0; ok; ++r) {
+        const int u = bw_unit(r, c, G, U);
+        if (u < 0) break;
+        const Unit w = unit(u);
+        const int kb = r & 1;
+        if (!mbar_wait(k_full(kb), (uint32_t)((r >> 1) & 1), a.err) ||
+            !mbar_wait(v_full, (uint32_t)(r & 1), a.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // dQ_ij = dS K_j: A = dS^T read MN-major (query blocks of 64 are 16 KB
-        // apart), B = K_j MN-major; 16 keys per step = 16 rows of 128 bytes.
-        const uint64_t dsm = desc_add(dS_mn0, pb * kStage);
+        const uint64_t dkk = desc_add(dK_k0, kb * kTileBytes);
+        const uint64_t dkmn = desc_add(dK_mn0, kb * kTileBytes);
+        if (!issue_s(g, dkk)) { ok = false; break; }
+        if (w.n_it == 1) mma_commit(v_empty);  // the unit's last S^T / dP^T read V
+        for (int it = 0; it < w.n_it; ++it, ++g) {
+          const int st = g % kBwQdoStages, pb = g & 1;
+          // math(g) holds S^T / dP^T in registers: the next tile's go in
+          if (!mbar_wait(st_free, (uint32_t)(g & 1), a.err)) { ok = false; break; }
+          tc_fence_after();
+          if (it + 1 < w.n_it) {
+            if (!issue_s(g + 1, dkk)) { ok = false; break; }
+            if (it + 2 == w.n_it) mma_commit(v_empty);
+          }
+          if (!mbar_wait(pds_full, (uint32_t)(g & 1), a.err)) { ok = false; break; }
+          // the previous unit's dV / dK have been read out
+          if (it == 0 && r >= 1 && !mbar_wait(acc_empty, (uint32_t)((r - 1) & 1), a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // dV += P^T dO (P^T from TMEM), dK += dS^T Q (dS^T K-major from smem)
+          const uint64_t dmn = desc_add(dO_mn0, st * kStage), qmn = desc_add(dQ_mn0, st * kStage);
+          const uint64_t dsk = desc_add(dS_k0, pb * kStage);
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)
-          mma_bf16_ss(tDQ, desc_add(dsm, kk * 2048), desc_add(dK_mn, kk * 2048), idQ,
-                      kk > 0 ? 1u : 0u);
-        mma_commit(dq_full);
+          for (int kk = 0; kk < kTile / 16; ++kk) {
+            const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+            mma_bf16_ts(tDV, tPT + kk * 8, desc_add(dmn, kk * 2048), idG, acc);
+            mma_bf16_ss(tDK, desc_add(dsk, (kk >> 2) * 16384 + (kk & 3) * 32),
+                        desc_add(qmn, kk * 2048), idG, acc);
+          }
+          mma_commit(qdo_empty(st));
+          mma_commit(pt_free);
+          // the single dQ accumulator: dQ(g-1) drained before dQ(g)
+          if (g >= 1 && !mbar_wait(dq_free, (uint32_t)((g - 1) & 1), a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // dQ_ij = dS K_j: A = dS^T read MN-major (query blocks of 64 are 16 KB
+          // apart), B = K_j MN-major; 16 keys per step = 16 rows of 128 bytes.
+          const uint64_t dsm = desc_add(dS_mn0, pb * kStage);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            mma_bf16_ss(tDQ, desc_add(dsm, kk * 2048), desc_add(dkmn, kk * 2048), idQ,
+                        kk > 0 ? 1u : 0u);
+          mma_commit(dq_full);
+          if (it + 1 == w.n_it) {
+            mma_commit(acc_full);     // the unit's dV / dK are final
+            mma_commit(k_empty(kb));  // and its K has been read for the last time
+          }
+        }
       }
       mma_commit(final_bar);
       mbar_wait(final_bar, 0, a.err);
@@ -1145,16 +1235,15 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   } else {
     // ------------------------------ element math ------------------------------
     const int quarter = warp & 3, half = warp >> 2;
-    const int r = quarter * 32 + lane;  // key row within the tile / dQ row
-    const int kg = k0 + r;
+    const int r_row = quarter * 32 + lane;  // key row within the tile / dQ row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int cbase = half * 64;        // this thread's query columns [cbase, cbase + 64)
+    const int cbase = half * 64;            // this thread's query columns [cbase, cbase + 64)
     const float sl2 = a.scale * kLog2e;
-    // Drains dQ(it) (row r, column groups 8*half .. +8) into dS^T buffer
-    // it & 1, free since dQ(it) completed, in the partial-tile layout (float4
+    // Drains dQ(g) (row r_row, column groups 8*half .. +8) into dS^T buffer
+    // g & 1, free since dQ(g) completed, in the partial-tile layout (float4
     // index (column / 4) * 128 + row); warp 10 sends it on.
-    auto drain = [&](int it, bool ok) -> bool {
-      if (ok && !mbar_wait(dq_full, (uint32_t)(it & 1), a.err)) ok = false;
+    auto drain = [&](int g, bool ok) -> bool {
+      if (ok && !mbar_wait(dq_full, (uint32_t)(g & 1), a.err)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) return false;
       tc_fence_after();
@@ -1164,141 +1253,153 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      const uint32_t stage = sDST(it & 1);
+      const uint32_t stage = sDST(g & 1);
 #pragma unroll
-      for (int g = 0; g < 8; ++g)
-        st_shared_v4(stage + (uint32_t)(((half * 8 + g) * kTile + r) * 16), v[4 * g],
-                     v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+      for (int gg = 0; gg < 8; ++gg)
+        st_shared_v4(stage + (uint32_t)(((half * 8 + gg) * kTile + r_row) * 16), v[4 * gg],
+                     v[4 * gg + 1], v[4 * gg + 2], v[4 * gg + 3]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(staged);
       return true;
     };
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int st = it % kBwQdoStages, pb = it & 1;
-      const int qt = first_q + it;
-      const int q0 = qt * kTile;
-      if (ok && !mbar_wait(st_full, (uint32_t)(it & 1), a.err)) ok = false;
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc_fence_after();
-        // this thread's 64 columns of S^T and dP^T, then the columns are free
-        uint32_t vs0[32], vs1[32], vd0[32], vd1[32];
-        tmem_ld32(tST + lane_off + cbase, vs0);
-        tmem_ld32(tST + lane_off + cbase + 32, vs1);
-        tmem_ld32(tDPT + lane_off + cbase, vd0);
-        tmem_ld32(tDPT + lane_off + cbase + 32, vd1);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(st_free);
-        // row terms of this tile; P^T's TMEM columns read by dV(it-1)
-        if (!mbar_wait(stats_full(st), (uint32_t)((it / kBwQdoStages) & 1), a.err)) ok = false;
-        if (it >= 1 && !mbar_wait(pt_free, (uint32_t)((it - 1) & 1), a.err)) ok = false;
+    int g = 0;
+    for (int r = 0;; ++r) {
+      const int u = bw_unit(r, c, G, U);
+      if (u < 0) break;
+      const Unit w = unit(u);
+      const int k0 = w.kt * kTile;
+      const int kg = k0 + r_row;
+      for (int it = 0; it < w.n_it; ++it, ++g) {
+        const int st = g % kBwQdoStages, pb = g & 1;
+        const int qt = w.first_q + it;
+        const int q0 = qt * kTile;
+        if (ok && !mbar_wait(st_full, (uint32_t)(g & 1), a.err)) ok = false;
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           tc_fence_after();
-          const float* lse_s = stats(st);
-          const float* delta_s = lse_s + kTile;
-          const bool diag = a.causal && qt == kt;
-          const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
-          // P^T (to TMEM) and dS^T (packed, kept in pd) for 32 of this
-          // thread's query columns; the masked variant only runs on the
-          // diagonal tile and a ragged edge.
-          auto chunk = [&](auto masked_c, auto c_c, const uint32_t(&vs)[32],
-                           const uint32_t(&vd)[32], uint32_t(&pd)[16]) {
-            constexpr bool kMasked = decltype(masked_c)::value;
-            constexpr int c = decltype(c_c)::value;
-            const int col = cbase + 32 * c;
-            const float4* l4 = reinterpret_cast<const float4*>(lse_s + col);
-            const float4* d4 = reinterpret_cast<const float4*>(delta_s + col);
-            uint32_t pp[16];
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const float4 lv = l4[g], dv4 = d4[g];
-              const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
-              const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
-              float pe[4], de[4];
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int e = 4 * g + u;
-                pe[u] = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[u]));
-                de[u] = pe[u] * (__uint_as_float(vd[e]) - dl[u]);
-                if (kMasked) {
-                  const int qg = q0 + col + 4 * g + u;
-                  if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe[u] = de[u] = 0.f;
-                }
-              }
-              pp[2 * g] = pack_bf16(pe[0], pe[1]);
-              pp[2 * g + 1] = pack_bf16(pe[2], pe[3]);
-              pd[2 * g] = pack_bf16(de[0], de[1]);
-              pd[2 * g + 1] = pack_bf16(de[2], de[3]);
-            }
-            // P^T: queries [64 half + 32 c, +32) = TMEM columns 32 half + 16 c
-            tmem_st16(tPT + lane_off + 32 * half + 16 * c, pp);
-          };
-          using c0 = std::integral_constant<int, 0>;
-          using c1 = std::integral_constant<int, 1>;
-          uint32_t pd0[16], pd1[16];
-          if (diag || tail) {
-            chunk(std::true_type{}, c0{}, vs0, vd0, pd0);
-            chunk(std::true_type{}, c1{}, vs1, vd1, pd1);
-          } else {
-            chunk(std::false_type{}, c0{}, vs0, vd0, pd0);
-            chunk(std::false_type{}, c1{}, vs1, vd1, pd1);
-          }
-          // dS^T buffer pb was last the staging of dQ(it-2): its bulk copy has
-          // read it (issued a tile ago, so this wait is normally satisfied)
-          if (it >= 2 && !mbar_wait(stage_free, (uint32_t)(it & 1), a.err)) ok = false;
-          ok = __all_sync(0xffffffffu, ok);
-          if (ok) {
-            store_row_packed(sDST(pb), r, cbase >> 5, pd0);
-            store_row_packed(sDST(pb), r, (cbase >> 5) + 1, pd1);
-          }
-          tmem_wait_st();
-          fence_proxy_async_smem();
+          // this thread's 64 columns of S^T and dP^T, then the columns are free
+          uint32_t vs0[32], vs1[32], vd0[32], vd1[32];
+          tmem_ld32(tST + lane_off + cbase, vs0);
+          tmem_ld32(tST + lane_off + cbase + 32, vs1);
+          tmem_ld32(tDPT + lane_off + cbase, vd0);
+          tmem_ld32(tDPT + lane_off + cbase + 32, vd1);
+          tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (ok && lane == 0) mbar_arrive(pds_full);
+          if (lane == 0) mbar_arrive(st_free);
+          // row terms of this tile; P^T's TMEM columns read by dV(g-1)
+          if (!mbar_wait(stats_full(st), (uint32_t)((g / kBwQdoStages) & 1), a.err)) ok = false;
+          if (g >= 1 && !mbar_wait(pt_free, (uint32_t)((g - 1) & 1), a.err)) ok = false;
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            tc_fence_after();
+            const float* lse_s = stats(st);
+            const float* delta_s = lse_s + kTile;
+            const bool diag = a.causal && qt == w.kt;
+            const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
+            // P^T (to TMEM) and dS^T (packed, kept in pd) for 32 of this
+            // thread's query columns; the masked variant only runs on the
+            // diagonal tile and a ragged edge.
+            auto chunk = [&](auto masked_c, auto c_c, const uint32_t(&vs)[32],
+                             const uint32_t(&vd)[32], uint32_t(&pd)[16]) {
+              constexpr bool kMasked = decltype(masked_c)::value;
+              constexpr int cc = decltype(c_c)::value;
+              const int col = cbase + 32 * cc;
+              const float4* l4 = reinterpret_cast<const float4*>(lse_s + col);
+              const float4* d4 = reinterpret_cast<const float4*>(delta_s + col);
+              uint32_t pp[16];
+#pragma unroll
+              for (int gg = 0; gg < 8; ++gg) {
+                const float4 lv = l4[gg], dv4 = d4[gg];
+                const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
+                const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
+                float pe[4], de[4];
+#pragma unroll
+                for (int uu = 0; uu < 4; ++uu) {
+                  const int e = 4 * gg + uu;
+                  pe[uu] = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[uu]));
+                  de[uu] = pe[uu] * (__uint_as_float(vd[e]) - dl[uu]);
+                  if (kMasked) {
+                    const int qg = q0 + col + 4 * gg + uu;
+                    if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe[uu] = de[uu] = 0.f;
+                  }
+                }
+                pp[2 * gg] = pack_bf16(pe[0], pe[1]);
+                pp[2 * gg + 1] = pack_bf16(pe[2], pe[3]);
+                pd[2 * gg] = pack_bf16(de[0], de[1]);
+                pd[2 * gg + 1] = pack_bf16(de[2], de[3]);
+              }
+              // P^T: queries [64 half + 32 cc, +32) = TMEM columns 32 half + 16 cc
+              tmem_st16(tPT + lane_off + 32 * half + 16 * cc, pp);
+            };
+            using c0 = std::integral_constant<int, 0>;
+            using c1 = std::integral_constant<int, 1>;
+            uint32_t pd0[16], pd1[16];
+            if (diag || tail) {
+              chunk(std::true_type{}, c0{}, vs0, vd0, pd0);
+              chunk(std::true_type{}, c1{}, vs1, vd1, pd1);
+            } else {
+              chunk(std::false_type{}, c0{}, vs0, vd0, pd0);
+              chunk(std::false_type{}, c1{}, vs1, vd1, pd1);
+            }
+            // dS^T buffer pb was last the staging of dQ(g-2): its bulk copy has
+            // read it (issued an iteration ago, so this wait is normally met)
+            if (g >= 2 && !mbar_wait(stage_free, (uint32_t)(g & 1), a.err)) ok = false;
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) {
+              store_row_packed(sDST(pb), r_row, cbase >> 5, pd0);
+              store_row_packed(sDST(pb), r_row, (cbase >> 5) + 1, pd1);
+            }
+            tmem_wait_st();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(pds_full);
+          }
         }
+        if (g >= 1) ok = drain(g - 1, ok) && ok;
       }
-      if (it >= 1) ok = drain(it - 1, ok) && ok;
-    }
-    if (n_it >= 1) ok = drain(n_it - 1, ok) && ok;
-    if (ok && !mbar_wait(final_bar, 0, a.err)) ok = false;
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
+      // the unit's dV and dK (dK scaled by the softmax scale)
+      if (ok && !mbar_wait(acc_full, (uint32_t)(r & 1), a.err)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
       tmem_ld32(tDV + lane_off + half * 32, v0);
       tmem_ld32(tDK + lane_off + half * 32, v1);
       tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
       if (kg < a.S) {
         const int64_t off =
-            (int64_t)b * a.qs0 + (int64_t)h * a.qs1 + (int64_t)kg * a.qs2 + half * 32;
+            (int64_t)w.b * a.qs0 + (int64_t)w.h * a.qs1 + (int64_t)kg * a.qs2 + half * 32;
         __nv_bfloat16* dvp = static_cast<__nv_bfloat16*>(a.dv) + off;
         __nv_bfloat16* dkp = static_cast<__nv_bfloat16*>(a.dk) + off;
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 u, w;
-          u.x = pack_bf16(__uint_as_float(v0[8 * g + 0]), __uint_as_float(v0[8 * g + 1]));
-          u.y = pack_bf16(__uint_as_float(v0[8 * g + 2]), __uint_as_float(v0[8 * g + 3]));
-          u.z = pack_bf16(__uint_as_float(v0[8 * g + 4]), __uint_as_float(v0[8 * g + 5]));
-          u.w = pack_bf16(__uint_as_float(v0[8 * g + 6]), __uint_as_float(v0[8 * g + 7]));
-          w.x = pack_bf16(__uint_as_float(v1[8 * g + 0]) * a.scale,
-                          __uint_as_float(v1[8 * g + 1]) * a.scale);
-          w.y = pack_bf16(__uint_as_float(v1[8 * g + 2]) * a.scale,
-                          __uint_as_float(v1[8 * g + 3]) * a.scale);
-          w.z = pack_bf16(__uint_as_float(v1[8 * g + 4]) * a.scale,
-                          __uint_as_float(v1[8 * g + 5]) * a.scale);
-          w.w = pack_bf16(__uint_as_float(v1[8 * g + 6]) * a.scale,
-                          __uint_as_float(v1[8 * g + 7]) * a.scale);
-          reinterpret_cast<uint4*>(dvp)[g] = u;
-          reinterpret_cast<uint4*>(dkp)[g] = w;
+        for (int gg = 0; gg < 4; ++gg) {
+          uint4 uv, wk;
+          uv.x = pack_bf16(__uint_as_float(v0[8 * gg + 0]), __uint_as_float(v0[8 * gg + 1]));
+          uv.y = pack_bf16(__uint_as_float(v0[8 * gg + 2]), __uint_as_float(v0[8 * gg + 3]));
+          uv.z = pack_bf16(__uint_as_float(v0[8 * gg + 4]), __uint_as_float(v0[8 * gg + 5]));
+          uv.w = pack_bf16(__uint_as_float(v0[8 * gg + 6]), __uint_as_float(v0[8 * gg + 7]));
+          wk.x = pack_bf16(__uint_as_float(v1[8 * gg + 0]) * a.scale,
+                           __uint_as_float(v1[8 * gg + 1]) * a.scale);
+          wk.y = pack_bf16(__uint_as_float(v1[8 * gg + 2]) * a.scale,
+                           __uint_as_float(v1[8 * gg + 3]) * a.scale);
+          wk.z = pack_bf16(__uint_as_float(v1[8 * gg + 4]) * a.scale,
+                           __uint_as_float(v1[8 * gg + 5]) * a.scale);
+          wk.w = pack_bf16(__uint_as_float(v1[8 * gg + 6]) * a.scale,
+                           __uint_as_float(v1[8 * gg + 7]) * a.scale);
+          reinterpret_cast<uint4*>(dvp)[gg] = uv;
+          reinterpret_cast<uint4*>(dkp)[gg] = wk;
         }
       }
     }
+    if (g >= 1) ok = drain(g - 1, ok) && ok;
+    if (ok && !mbar_wait(final_bar, 0, a.err)) ok = false;
   }
   tc_fence_before();
   __syncthreads();
@@ -1468,7 +1569,10 @@ magma_status_t attention_bwd_tc(const void* q, const void* k, const void* v, con
       aligned16(workspace)) {
     float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dbytes);
     if (magma_status_t st = set_smem_attr<3>(attn_bwd_tc, kBwSmem)) return st;
-    attn_bwd_tc<<<grid, kBwThreads, kBwSmem, s>>>(mq, mk, mv, mdo, a, part);
+    // persistent: one CTA per SM over the n_t * H * B key-tile units
+    const int64_t units = ceil_div(S, kTile) * H * B;
+    const int ctas = (int)(units < num_sms() ? units : num_sms());
+    attn_bwd_tc<<<ctas, kBwThreads, kBwSmem, s>>>(mq, mk, mv, mdo, a, part);
     if (magma_status_t st = check_launch("attention_bwd_tcgen05")) return st;
     attn_dq_reduce<<<grid, 256, 0, s>>>(part, static_cast<__nv_bfloat16*>(dq), (int)S, (int)H,
                                         causal, scale, qs[0], qs[1], qs[2]);

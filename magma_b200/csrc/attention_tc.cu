@@ -122,28 +122,42 @@ __device__ __forceinline__ uint32_t align1024(uint8_t* raw, uint8_t** aligned_pt
   return base;
 }
 
+// The r-th work unit of CTA c among G persistent CTAs (snake order: round r
+// takes units r*G .. r*G+G-1, even rounds in CTA order, odd rounds
+// reversed), or -1 past the end.
+__device__ __forceinline__ int bw_unit(int r, int c, int G, int U) {
+  const int u = r * G + ((r & 1) ? G - 1 - c : c);
+  return u < U ? u : -1;
+}
+
 // =============================================================== forward
-// One CTA per pair of 128-query tiles (t = 0, 1: query rows q0 .. q0+255),
-// heaviest causal pairs first. Warps 0-3 run the softmax of tile 0, warps 4-7
-// that of tile 1, warp 8 is the TMA producer, warp 9 allocates TMEM and issues
-// the MMAs. Both tiles stream the same K/V tiles, so while one warpgroup
-// turns S_t into P_t the tensor cores work on the other tile:
+// Persistent: one CTA per SM walks a static list of work units (a pair of
+// 128-query tiles t = 0, 1 of one head, query rows q0 .. q0+255), heaviest
+// causal pairs first, in the same snake order over the CTAs as the backward.
+// Warps 0-3 run the softmax of tile 0, warps 4-7 that of tile 1, warp 8 is
+// the TMA producer (Q double-buffered per unit, K/V through a 3-stage ring
+// that runs on across units), warp 9 allocates TMEM and issues the MMAs. Both
+// tiles stream the same K/V tiles, so while one warpgroup turns S_t into P_t
+// the tensor cores work on the other tile:
 //   MMA order: S0(0) S1(0) | S0(1) PV0(0) S1(1) PV1(0) | S0(2) PV0(1) ...
 // TMEM: S_t at columns 128t (F32 128x128), O_t at 256 + 64t, P_t (BF16
 // pairs, the TMEM A operand of PV_t = P_t V_j) at 384 + 64t. A warpgroup
 // releases S_t's columns (s_free) as soon as its exponential pass has read
-// the last of them, so S_t(j+1) is computed while the pass finishes and while
-// the other warpgroup runs its own; before it writes P_t(j) or rescales O_t
-// it waits for PV_t(j-1) (pv_done). O_t and the row
-// sum are rescaled only when a row maximum grows by more than 2^8 (otherwise
-// the stale maximum is kept: P <= 2^8, exact after the final division).
+// the last of them, so S_t(j+1) (or the next unit's S_t(0)) is computed while
+// the pass finishes and while the other warpgroup runs its own; before it
+// writes P_t or rescales or reads O_t it waits for the previous PV_t
+// (pv_done). O_t and the row sum are rescaled only when a row maximum grows
+// by more than 2^8 (otherwise the stale maximum is kept: P <= 2^8, exact
+// after the final division). Barrier phases count a warpgroup's steps over
+// all its units.
 constexpr int kFwdStages = 3;
 constexpr int kFwdThreads = 320;                 // 8 softmax warps + producer + MMA
-constexpr int kFwdQ = 0;                         // Q tiles 0, 1 (2 x 16 KB)
-constexpr int kFwdKv = 2 * kTileBytes;           // K, V per stage
+constexpr int kFwdQ = 0;                         // 2 buffers x Q tiles 0, 1 (4 x 16 KB)
+constexpr int kFwdKv = 4 * kTileBytes;           // K, V per stage
 constexpr int kFwdBar = kFwdKv + kFwdStages * 2 * kTileBytes;
-// q_full, kv_full[3], kv_empty[3], s_full[2], s_free[2], p_full[2], pv_done[2], done
-constexpr int kFwdNumBars = 16;
+// q_full[2], q_empty[2], kv_full[3], kv_empty[3], s_full[2], s_free[2], p_full[2],
+// pv_done[2], done
+constexpr int kFwdNumBars = 19;
 constexpr int kFwdSmem = kFwdBar + kFwdNumBars * 8 + 16 + 1024;
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -153,42 +167,56 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sp;
   const uint32_t base = align1024(smem_raw, &sp);
-  auto sQ = [&](int t) { return base + kFwdQ + t * kTileBytes; };
+  auto sQ = [&](int qb, int t) { return base + kFwdQ + (2 * qb + t) * kTileBytes; };
   auto sK = [&](int st) { return base + kFwdKv + st * 2 * kTileBytes; };
   auto sV = [&](int st) { return base + kFwdKv + st * 2 * kTileBytes + kTileBytes; };
   const uint32_t bars = base + kFwdBar;
-  const uint32_t q_full = bars;
-  auto kv_full = [&](int st) { return bars + 8u * (1 + st); };
-  auto kv_empty = [&](int st) { return bars + 8u * (4 + st); };
-  auto s_full = [&](int t) { return bars + 8u * (7 + t); };
-  auto s_free = [&](int t) { return bars + 8u * (9 + t); };
-  auto p_full = [&](int t) { return bars + 8u * (11 + t); };
-  auto pv_done = [&](int t) { return bars + 8u * (13 + t); };
-  const uint32_t done_bar = bars + 8u * 15;
+  auto q_full = [&](int qb) { return bars + 8u * qb; };
+  auto q_empty = [&](int qb) { return bars + 8u * (2 + qb); };
+  auto kv_full = [&](int st) { return bars + 8u * (4 + st); };
+  auto kv_empty = [&](int st) { return bars + 8u * (7 + st); };
+  auto s_full = [&](int t) { return bars + 8u * (10 + t); };
+  auto s_free = [&](int t) { return bars + 8u * (12 + t); };
+  auto p_full = [&](int t) { return bars + 8u * (14 + t); };
+  auto pv_done = [&](int t) { return bars + 8u * (16 + t); };
+  const uint32_t done_bar = bars + 8u * 18;
   const uint32_t tslot = bars + 8u * kFwdNumBars;
   uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(sp + kFwdBar + 8 * kFwdNumBars);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (a.S + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
-  // Blocks are dispatched in linear index order; the pair index varies
-  // slowest so that every head's heaviest pair (most key tiles under causal)
-  // starts first and the lightest ones fill the tail.
-  const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
-  const int heads = (int)(gridDim.y * gridDim.z);
-  const int qt0 = 2 * (n_pairs - 1 - lin / heads);
-  const bool has1 = qt0 + 1 < n_qt;
-  const int h = (lin % heads) % (int)gridDim.y, b = (lin % heads) / (int)gridDim.y;
-  // key tiles visited by query tile t
-  const int nk0 = a.causal ? qt0 + 1 : n_qt;
-  const int nk1 = has1 ? (a.causal ? qt0 + 2 : n_qt) : 0;
-  const int n_kv = nk0 > nk1 ? nk0 : nk1;
+  const int heads = a.H * a.B;
+  const int U = n_pairs * heads;
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  // unit u: query-tile pair n_pairs - 1 - u / heads (varying slowest, so the
+  // heaviest causal pairs come first), head u % heads
+  struct Unit {
+    int qt0, h, b, nk0, nk1, n_kv;
+    bool has1;
+  };
+  auto unit = [&](int u) {
+    Unit w;
+    w.qt0 = 2 * (n_pairs - 1 - u / heads);
+    w.has1 = w.qt0 + 1 < n_qt;
+    const int hb = u % heads;
+    w.h = hb % a.H;
+    w.b = hb / a.H;
+    // key tiles visited by query tile t
+    w.nk0 = a.causal ? w.qt0 + 1 : n_qt;
+    w.nk1 = w.has1 ? (a.causal ? w.qt0 + 2 : n_qt) : 0;
+    w.n_kv = w.nk0 > w.nk1 ? w.nk0 : w.nk1;
+    return w;
+  };
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
-    mbar_init(q_full, 1);
+    for (int qb = 0; qb < 2; ++qb) {
+      mbar_init(q_full(qb), 1);
+      mbar_init(q_empty(qb), 1);
+    }
     for (int st = 0; st < kFwdStages; ++st) {
       mbar_init(kv_full(st), 1);
       mbar_init(kv_empty(st), 1);
@@ -214,55 +242,67 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   if (warp == 8) {
     if (lane == 0) {
       bool ok = true;
-      mbar_expect_tx(q_full, (has1 ? 2 : 1) * kTileBytes);
-      tma_load_4d(sQ(0), &tmQ, 0, qt0 * kTile, h, b, q_full);
-      if (has1) tma_load_4d(sQ(1), &tmQ, 0, (qt0 + 1) * kTile, h, b, q_full);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % kFwdStages;
-        if (!mbar_wait(kv_empty(st), (uint32_t)(((j / kFwdStages) & 1) ^ 1), a.err)) {
-          ok = false;
-          break;
+      int gk = 0;  // K/V tiles loaded so far (ring position)
+      for (int r = 0; ok; ++r) {
+        const int u = bw_unit(r, c, G, U);
+        if (u < 0) break;
+        const Unit w = unit(u);
+        const int qb = r & 1;
+        // Q buffer qb was last read by unit r-2
+        if (!mbar_wait(q_empty(qb), (uint32_t)(((r >> 1) & 1) ^ 1), a.err)) { ok = false; break; }
+        mbar_expect_tx(q_full(qb), (w.has1 ? 2 : 1) * kTileBytes);
+        tma_load_4d(sQ(qb, 0), &tmQ, 0, w.qt0 * kTile, w.h, w.b, q_full(qb));
+        if (w.has1) tma_load_4d(sQ(qb, 1), &tmQ, 0, (w.qt0 + 1) * kTile, w.h, w.b, q_full(qb));
+        for (int j = 0; j < w.n_kv; ++j, ++gk) {
+          const int st = gk % kFwdStages;
+          if (!mbar_wait(kv_empty(st), (uint32_t)(((gk / kFwdStages) & 1) ^ 1), a.err)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(kv_full(st), 2 * kTileBytes);
+          tma_load_4d(sK(st), &tmK, 0, j * kTile, w.h, w.b, kv_full(st));
+          tma_load_4d(sV(st), &tmV, 0, j * kTile, w.h, w.b, kv_full(st));
         }
-        mbar_expect_tx(kv_full(st), 2 * kTileBytes);
-        tma_load_4d(sK(st), &tmK, 0, j * kTile, h, b, kv_full(st));
-        tma_load_4d(sV(st), &tmV, 0, j * kTile, h, b, kv_full(st));
       }
-      // every stage issued above has been consumed before the producer leaves
-      for (int j = n_kv; j < n_kv + kFwdStages && ok; ++j) {
-        const int st = j % kFwdStages;
-        if (!mbar_wait(kv_empty(st), (uint32_t)(((j / kFwdStages) & 1) ^ 1), a.err)) ok = false;
+      // every stage loaded above has been consumed before the producer leaves
+      for (int k = gk; k < gk + kFwdStages && ok; ++k) {
+        const int st = k % kFwdStages;
+        if (!mbar_wait(kv_empty(st), (uint32_t)(((k / kFwdStages) & 1) ^ 1), a.err)) ok = false;
       }
     }
   } else if (warp == 9) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(kTile, kTile, 0, 0);
       constexpr uint32_t idPV = idesc_bf16_f32(kTile, kHd, 0, 1);
-      bool ok = mbar_wait(q_full, 0, a.err);
-      int kv_ready = -1;  // highest key tile whose K/V have been waited for
-      auto wait_kv = [&](int j) -> bool {
-        if (j <= kv_ready) return true;
-        kv_ready = j;
-        if (!mbar_wait(kv_full(j % kFwdStages), (uint32_t)((j / kFwdStages) & 1), a.err))
-          return false;
-        tc_fence_after();
-        return true;
-      };
+      bool ok = true;
+      int gk = 0;             // K/V tiles consumed so far
+      int ns[2] = {0, 0};     // S_t issued so far (all units)
+      int np[2] = {0, 0};     // PV_t issued so far
       // Descriptors are formed once; every instruction then adds an immediate
       // byte offset >> 4 (desc_add), which keeps the single issuing thread's
       // scalar work per tcgen05.mma to one add.
-      const uint64_t dq0 = desc_k(sQ(0)), dk0 = desc_k(sK(0)), dv0 = desc_mn(sV(0));
-      auto issue_s = [&](int t, int j) {
-        const int st = j % kFwdStages;
-        const uint64_t dq = desc_add(dq0, (uint32_t)t * kTileBytes);
+      const uint64_t dq0 = desc_k(sQ(0, 0)), dk0 = desc_k(sK(0)), dv0 = desc_mn(sV(0));
+      // S_t of K/V tile at ring position kg, Q buffer qb; waits for S_t's
+      // columns to be free (the previous S_t read by its warpgroup)
+      auto issue_s = [&](int t, int qb, int kg) -> bool {
+        if (ns[t] >= 1 && !mbar_wait(s_free(t), (uint32_t)((ns[t] - 1) & 1), a.err)) return false;
+        const int st = kg % kFwdStages;
+        if (!mbar_wait(kv_full(st), (uint32_t)((kg / kFwdStages) & 1), a.err)) return false;
+        tc_fence_after();
+        const uint64_t dq = desc_add(dq0, (uint32_t)(2 * qb + t) * kTileBytes);
         const uint64_t dk = desc_add(dk0, (uint32_t)st * 2 * kTileBytes);
         const uint32_t d = tS(t);
 #pragma unroll
         for (int kk = 0; kk < kHd / 16; ++kk)
           mma_bf16_ss(d, desc_add(dq, kk * 32), desc_add(dk, kk * 32), idS, kk > 0 ? 1u : 0u);
         mma_commit(s_full(t));
+        ++ns[t];
+        return true;
       };
-      auto issue_pv = [&](int t, int j) {
-        const int st = j % kFwdStages;
+      auto issue_pv = [&](int t, int j, int kg) -> bool {
+        if (!mbar_wait(p_full(t), (uint32_t)(np[t] & 1), a.err)) return false;
+        tc_fence_after();
+        const int st = kg % kFwdStages;
         const uint64_t dv = desc_add(dv0, (uint32_t)st * 2 * kTileBytes);
         const uint32_t d = tO(t), pa = tP(t);
         const uint32_t acc = j > 0 ? 1u : 0u;
@@ -270,32 +310,32 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         for (int kk = 0; kk < kTile / 16; ++kk)
           mma_bf16_ts(d, pa + kk * 8, desc_add(dv, kk * 2048), idPV, kk > 0 ? 1u : acc);
         mma_commit(pv_done(t));
+        ++np[t];
+        return true;
       };
-      if (ok && n_kv > 0) {
-        ok = wait_kv(0);
-        if (ok) {
-          issue_s(0, 0);
-          if (nk1 > 0) issue_s(1, 0);
+      for (int r = 0; ok; ++r) {
+        const int u = bw_unit(r, c, G, U);
+        if (u < 0) break;
+        const Unit w = unit(u);
+        const int qb = r & 1;
+        if (!mbar_wait(q_full(qb), (uint32_t)((r >> 1) & 1), a.err)) { ok = false; break; }
+        if (w.n_kv > 0) {
+          if (!issue_s(0, qb, gk)) { ok = false; break; }
+          if (w.nk1 > 0 && !issue_s(1, qb, gk)) { ok = false; break; }
         }
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        for (int t = 0; t < 2 && ok; ++t) {
-          const int nk = t ? nk1 : nk0;
-          if (j >= nk) continue;
-          // S_t(j+1) as soon as warpgroup t has read all of S_t(j)
-          if (j + 1 < nk) {
-            if (!mbar_wait(s_free(t), (uint32_t)(j & 1), a.err) || !wait_kv(j + 1)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(t, j + 1);
+        for (int j = 0; j < w.n_kv && ok; ++j) {
+          for (int t = 0; t < 2 && ok; ++t) {
+            const int nk = t ? w.nk1 : w.nk0;
+            if (j >= nk) continue;
+            // S_t(j+1) as soon as warpgroup t has read all of S_t(j)
+            if (j + 1 < nk && !issue_s(t, qb, gk + j + 1)) { ok = false; break; }
+            if (!issue_pv(t, j, gk + j)) { ok = false; break; }
           }
-          if (!mbar_wait(p_full(t), (uint32_t)(j & 1), a.err)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j);
+          if (ok) mma_commit(kv_empty((gk + j) % kFwdStages));
         }
-        if (ok) mma_commit(kv_empty(j % kFwdStages));
+        if (!ok) break;
+        gk += w.n_kv;
+        mma_commit(q_empty(qb));
       }
       mma_commit(done_bar);
       mbar_wait(done_bar, 0, a.err);
@@ -303,24 +343,29 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   } else {
     // ---------------------------- softmax warpgroups ----------------------------
     const int t = warp >> 2;
-    const int nk = t ? nk1 : nk0;
-    const int qt = qt0 + t;
-    const int r = (warp & 3) * 32 + lane;
-    const int qg = qt * kTile + r;
+    const int r_row = (warp & 3) * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t srow = tS(t) + lane_off;
     const uint32_t orow = tO(t) + lane_off;
     const uint32_t prow = tP(t) + lane_off;
     const float sl2 = a.scale * kLog2e;
-    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    int gs = 0;  // this warpgroup's steps over all its units (barrier phases)
+    for (int r = 0; ok; ++r) {
+    const int u = bw_unit(r, c, G, U);
+    if (u < 0) break;
+    const Unit w = unit(u);
+    const int nk = t ? w.nk1 : w.nk0;
+    const int qt = w.qt0 + t;
+    const int qg = qt * kTile + r_row;
+    float m_run = -INFINITY, l_run = 0.f;
     // The two warpgroups take turns on the exponential pass (MUFU is the
     // bottleneck unit): tile 0 step j, tile 1 step j, tile 0 step j+1, ...
     // Named barrier 1 + t hands the turn to warpgroup t. A warpgroup that hit
     // a wait limit keeps the turn protocol (skipping its work) so the other
     // one is never left at a named barrier.
-    const int nk_other = t ? nk0 : nk1;
-    for (int j = 0; j < nk; ++j) {
+    const int nk_other = t ? w.nk0 : w.nk1;
+    for (int j = 0; j < nk; ++j, ++gs) {
       // waits for the other warpgroup's step j-1 (t = 0) or step j (t = 1)
       const bool wait_turn = t ? (j < nk_other) : (j >= 1 && j - 1 < nk_other);
       // hands over after step j to its step j (t = 0) or step j+1 (t = 1)
@@ -334,7 +379,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       int lim = 127;  // last unmasked column of this row
       if (diag) lim = qg - k0;
       if (tail && a.S - 1 - k0 < lim) lim = a.S - 1 - k0;
-      if (ok && !mbar_wait(s_full(t), (uint32_t)(j & 1), a.err)) ok = false;
+      if (ok && !mbar_wait(s_full(t), (uint32_t)(gs & 1), a.err)) ok = false;
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform for the collective TMEM ops
       if (ok) {
         tc_fence_after();
@@ -363,8 +408,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m_run, mx * sl2);
-        // PV_t(j-1) has read P_t and added into O_t before either is touched
-        if (j >= 1 && !mbar_wait(pv_done(t), (uint32_t)((j - 1) & 1), a.err)) ok = false;
+        // the previous PV_t has read P_t and added into O_t before either is
+        // touched (at a unit's first step: the last PV_t of the unit before)
+        if (gs >= 1 && !mbar_wait(pv_done(t), (uint32_t)((gs - 1) & 1), a.err)) ok = false;
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           tc_fence_after();
@@ -443,7 +489,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         if (lane == 0) mbar_arrive(p_full(t));
       }
     }
-    if (ok && nk > 0 && !mbar_wait(pv_done(t), (uint32_t)((nk - 1) & 1), a.err)) ok = false;
+    if (ok && nk > 0 && !mbar_wait(pv_done(t), (uint32_t)((gs - 1) & 1), a.err)) ok = false;
     ok = __all_sync(0xffffffffu, ok);
     if (ok && nk > 0) {
       tc_fence_after();
@@ -454,18 +500,19 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       if (qg < a.S) {
         float of[kHd];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          of[c] = __uint_as_float(o0[c]);
-          of[32 + c] = __uint_as_float(o1[c]);
+        for (int cc = 0; cc < 32; ++cc) {
+          of[cc] = __uint_as_float(o0[cc]);
+          of[32 + cc] = __uint_as_float(o1[cc]);
         }
         const float inv = 1.0f / l_run;
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.o) + (int64_t)b * a.os0 +
-                             (int64_t)h * a.os1 + (int64_t)qg * a.os2;
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.o) + (int64_t)w.b * a.os0 +
+                             (int64_t)w.h * a.os1 + (int64_t)qg * a.os2;
         store_global_row64(dst, of, inv);
         if (a.lse != nullptr)
-          a.lse[((int64_t)b * a.H + h) * a.S + qg] = m_run * kLn2 + logf(l_run);
+          a.lse[((int64_t)w.b * a.H + w.h) * a.S + qg] = m_run * kLn2 + logf(l_run);
       }
     }
+    }  // units
   }
   tc_fence_before();
   __syncthreads();
@@ -920,11 +967,6 @@ constexpr int kBwNumBars = 26;
 constexpr int kBwSmem = kBwBar + kBwNumBars * 8 + 16 + 1024;
 static_assert(kBwSmem <= 232448, "backward shared memory");
 
-// The r-th unit of CTA c among G CTAs (snake order), or -1 past the end.
-__device__ __forceinline__ int bw_unit(int r, int c, int G, int U) {
-  const int u = r * G + ((r & 1) ? G - 1 - c : c);
-  return u < U ? u : -1;
-}
 constexpr int kDqTileFloats = kTile * kHd;                  // one F32 dQ partial tile
 
 // Index of the dQ partial of (query tile i, key tile j) among a head's slots.
@@ -1526,8 +1568,10 @@ magma_status_t attention_fwd_tc(const void* q, const void* k, const void* v, voi
   a.qs0 = qs[0]; a.qs1 = qs[1]; a.qs2 = qs[2];
   a.err = device_error_word();
   if (magma_status_t st = set_smem_attr<0>(attn_fwd_tc, kFwdSmem)) return st;
-  dim3 grid((unsigned)ceil_div(ceil_div(S, kTile), 2), (unsigned)H, (unsigned)B);
-  attn_fwd_tc<<<grid, kFwdThreads, kFwdSmem, s>>>(mq, mk, mv, a);
+  // persistent: one CTA per SM over the query-tile pairs of every head
+  const int64_t units = ceil_div(ceil_div(S, kTile), 2) * H * B;
+  const int ctas = (int)(units < num_sms() ? units : num_sms());
+  attn_fwd_tc<<<ctas, kFwdThreads, kFwdSmem, s>>>(mq, mk, mv, a);
   return check_launch("attention_fwd_tcgen05");
 }
 

@@ -264,7 +264,7 @@ def config_lines(peaks: dict) -> dict:
     from magma_b200 import mlp
 
     out["mlp_f32"] = mlp.bench_step()
-    out["char_gpt_f32"] = char_gpt_line()
+    out["char_gpt_f32"] = char_gpt_line(peaks)
     return out
 
 
@@ -273,7 +273,7 @@ def config_lines(peaks: dict) -> dict:
 FFMA_NOMINAL_TFLOPS = 74.4
 
 
-def char_gpt_line(steps: int = 5, warmup: int = 2) -> dict:
+def char_gpt_line(peaks: dict, steps: int = 5, warmup: int = 2) -> dict:
     """The char-level GPT training step in F32 at its configuration (vocab 65,
     6 layers, 6 heads, d 384, ctx 256, batch 64 = 16384 tokens, Adam lr 3e-4),
     forward+backward as CUDA graphs plus Adam, timed with CUDA events."""
@@ -304,13 +304,31 @@ def char_gpt_line(steps: int = 5, warmup: int = 2) -> dict:
     flops = sum(kinds[k]["work"] for k in ("gemm", "attention_fwd", "attention_bwd")
                 if k in kinds)
     tflops = flops / (ms / 1e3) / 1e12
+    # The F32 contractions large enough for it run on the BF16 tensor cores
+    # as six BF16 products per F32 product (three-term split, 2 M N K x 6
+    # tensor FLOPs); the small ones and attention run on FFMA.
+    gemm = kinds.get("gemm", {"ms": 0.0, "work": 0.0})
+    att_ms = sum(kinds[k]["ms"] for k in ("attention_fwd", "attention_bwd") if k in kinds)
+    att_work = sum(kinds[k]["work"] for k in ("attention_fwd", "attention_bwd") if k in kinds)
+    gemm_tensor = 6 * gemm["work"] / (gemm["ms"] / 1e3) / 1e12 if gemm["ms"] else 0.0
+    att_tflops = att_work / (att_ms / 1e3) / 1e12 if att_ms else 0.0
     return {"workload": "char-level GPT train step F32 (vocab 65, 6 layers, 6 heads, d 384, "
                         "ctx 256, batch 64), Adam lr 3e-4",
             "ms_per_step": round(ms, 3), "tokens_per_s": round(64 * cfg.seq / (ms / 1e3), 1),
-            "flops_per_step": flops, "tflops": round(tflops, 2), "bound": "FP32 FFMA",
-            "peak": FFMA_NOMINAL_TFLOPS, "unit": "TFLOP/s",
-            "frac": round(tflops / FFMA_NOMINAL_TFLOPS, 4),
-            "peak_source": "nominal F32 FFMA (148 SM x 128 FMA/clk x 2 x 1.965 GHz)",
+            "flops_per_step": flops, "tflops": round(tflops, 2),
+            "unit": "TFLOP/s (F32 products)",
+            "gemm": {"ms_per_step": round(gemm["ms"], 3),
+                     "tflops_f32": round(gemm["work"] / (gemm["ms"] / 1e3) / 1e12, 1)
+                     if gemm["ms"] else None,
+                     "bound": "tensor (BF16, three-term split: 6 BF16 products per F32 product)",
+                     "tensor_tflops": round(gemm_tensor, 1),
+                     "peak": peaks["bf16_tflops_sustained"],
+                     "frac": round(gemm_tensor / peaks["bf16_tflops_sustained"], 4),
+                     "peak_source": "measured bf16_tflops_sustained"},
+            "attention": {"ms_per_step": round(att_ms, 3), "tflops": round(att_tflops, 2),
+                          "bound": "FP32 FFMA", "peak": FFMA_NOMINAL_TFLOPS,
+                          "frac": round(att_tflops / FFMA_NOMINAL_TFLOPS, 4),
+                          "peak_source": "nominal F32 FFMA (148 SM x 128 FMA/clk x 2 x 1.965 GHz)"},
             "loss": round(float(tr.loss.item()), 4)}
 
 

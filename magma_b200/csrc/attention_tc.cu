@@ -1476,36 +1476,60 @@ attn_delta_tc(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restri
 }
 
 // dQ[b, h, q] = scale * sum over key tiles j (in order) of the F32 partials
-// of query tile i -> BF16 (caller's strided layout). One CTA per (i, h, b);
-// thread = 4 consecutive columns of 8 rows.
+// of query tile i -> BF16 (caller's strided layout). One CTA per (i, h, b).
+// Thread = one 4-column group of 8 rows: the partials of a group are read
+// with every load of the key-tile loop issued before the additions (512
+// contiguous bytes per warp load), the sums go to a row-major shared tile,
+// and the BF16 rows leave as whole 128-byte row segments (8 threads x 16 B).
 __global__ void __launch_bounds__(256)
 attn_dq_reduce(const float* __restrict__ dq_part, __nv_bfloat16* __restrict__ dq, int S, int H,
                int causal, float scale, int64_t qs0, int64_t qs1, int64_t qs2) {
+  __shared__ float sum_s[kTile][kHd + 4];  // row pitch 68 floats: conflict-free float4 rows
   const int n_t = (S + kTile - 1) / kTile;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int64_t bh = (int64_t)b * H + h;
-  const float* base = dq_part + bh * dq_slots(n_t, causal) * kDqTileFloats;
+  const float4* base = reinterpret_cast<const float4*>(dq_part + bh * dq_slots(n_t, causal) *
+                                                                     kDqTileFloats);
   const int j_end = causal ? qt + 1 : n_t;
+  const int64_t slot0 = dq_slot(qt, 0, n_t, causal);  // a query tile's slots are consecutive
+  constexpr int kGroups = kDqTileFloats / 4;             // float4 groups per tile
 #pragma unroll 1
-  for (int g = threadIdx.x; g < kDqTileFloats / 4; g += blockDim.x) {
+  for (int g = threadIdx.x; g < kGroups; g += blockDim.x) {
     const int row = g % kTile, col = (g / kTile) * 4;  // column-group-major tiles
+    float4 t[8];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < j_end; ++j) {
-      const float4 t = reinterpret_cast<const float4*>(
-          base + dq_slot(qt, j, n_t, causal) * kDqTileFloats)[g];
-      acc.x += t.x;
-      acc.y += t.y;
-      acc.z += t.z;
-      acc.w += t.w;
+    for (int j0 = 0; j0 < j_end; j0 += 8) {
+      const int nj = j_end - j0 < 8 ? j_end - j0 : 8;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < nj) t[k] = base[(slot0 + j0 + k) * kGroups + g];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < nj) {
+          acc.x += t[k].x;
+          acc.y += t[k].y;
+          acc.z += t[k].z;
+          acc.w += t[k].w;
+        }
     }
+    *reinterpret_cast<float4*>(&sum_s[row][col]) = acc;
+  }
+  __syncthreads();
+  // rows of 64 columns: 8 threads x 8 columns per row, 32 rows per pass
+  const int cg = threadIdx.x & 7;
+#pragma unroll 1
+  for (int row = threadIdx.x >> 3; row < kTile; row += blockDim.x >> 3) {
     const int q = qt * kTile + row;
-    if (q < S) {
-      uint2 u;
-      u.x = pack_bf16(acc.x * scale, acc.y * scale);
-      u.y = pack_bf16(acc.z * scale, acc.w * scale);
-      *reinterpret_cast<uint2*>(dq + (int64_t)b * qs0 + (int64_t)h * qs1 + (int64_t)q * qs2 +
-                                col) = u;
-    }
+    if (q >= S) continue;
+    const float4 lo = *reinterpret_cast<const float4*>(&sum_s[row][8 * cg]);
+    const float4 hi = *reinterpret_cast<const float4*>(&sum_s[row][8 * cg + 4]);
+    uint4 u;
+    u.x = pack_bf16(lo.x * scale, lo.y * scale);
+    u.y = pack_bf16(lo.z * scale, lo.w * scale);
+    u.z = pack_bf16(hi.x * scale, hi.y * scale);
+    u.w = pack_bf16(hi.z * scale, hi.w * scale);
+    *reinterpret_cast<uint4*>(dq + (int64_t)b * qs0 + (int64_t)h * qs1 + (int64_t)q * qs2 +
+                              8 * cg) = u;
   }
 }
 

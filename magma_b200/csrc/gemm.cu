@@ -1498,6 +1498,118 @@ magma_status_t launch_simt(const void* a, const void* b, void* c, int64_t M, int
   return MAGMA_OK;
 }
 
+// ---- F32 contraction on the BF16 tensor cores (three-term split) -----------
+// An F32 operand x is split into three BF16 terms, x1 = RN(x), x2 = RN(x -
+// x1), x3 = RN(x - x1 - x2) (each difference is exact in F32), which carry 24
+// significant bits between them. The product sum_k a b is then formed as the
+// six products whose magnitude reaches 2^-16 of a b, a1 b1 + a1 b2 + a2 b1 +
+// a1 b3 + a2 b2 + a3 b1 (the dropped terms a2 b3, a3 b2, a3 b3 are below 2^-24
+// relative), by one BF16 GEMM over a K six times as long:
+//   A' = [a1 | a1 | a2 | a1 | a2 | a3],  B' = [b1 | b2 | b1 | b3 | b2 | b1]
+// (each segment Kp = K rounded up to a multiple of 8 columns, zero padded),
+// accumulated in F32 by the tensor cores, with the epilogue of the F32 call.
+constexpr uint32_t kSplitPatA = (1u << 0) | (1u << 2) | (2u << 4) | (1u << 6) | (2u << 8) | (3u << 10);
+constexpr uint32_t kSplitPatB = (1u << 0) | (2u << 2) | (1u << 4) | (3u << 6) | (2u << 8) | (1u << 10);
+// below this many multiply-adds the one-pass FFMA kernel is used
+constexpr double kBf16x3MinMacs = 134217728.0;
+
+// dst [R][6 Kp] (BF16, row-major) from the F32 matrix element (r, k) =
+// src[r * rs + k * ks], r < R, k < Kc (zero for Kc <= k < Kp); segment s of a
+// row holds term (pat >> 2s) & 3 of every element. 32 x 32 tiles through
+// shared memory, so both the reads (along whichever index is contiguous) and
+// the writes (along k) are coalesced.
+__global__ void __launch_bounds__(256)
+split_bf16x3(const float* __restrict__ src, int64_t R, int64_t Kc, int64_t rs, int64_t ks,
+             int64_t Kp, uint32_t pat, __nv_bfloat16* __restrict__ dst) {
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t r0 = (int64_t)blockIdx.y * 32, k0 = (int64_t)blockIdx.x * 32;
+  const bool kcontig = ks == 1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int a = ty + 8 * i;
+    // (r, k) of this thread's read: consecutive threads along the contiguous index
+    const int rl = kcontig ? a : tx, kl = kcontig ? tx : a;
+    const int64_t r = r0 + rl, k = k0 + kl;
+    tile[rl][kl] = (r < R && k < Kc) ? src[r * rs + k * ks] : 0.f;
+  }
+  __syncthreads();
+  const int64_t ld = 6 * Kp;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rl = ty + 8 * i;
+    const int64_t r = r0 + rl, k = k0 + tx;
+    if (r >= R || k >= Kp) continue;
+    const float x = tile[rl][tx];
+    __nv_bfloat16 t[4];
+    t[1] = __float2bfloat16_rn(x);
+    const float e1 = __fsub_rn(x, __bfloat162float(t[1]));
+    t[2] = __float2bfloat16_rn(e1);
+    t[3] = __float2bfloat16_rn(__fsub_rn(e1, __bfloat162float(t[2])));
+    __nv_bfloat16* row = dst + r * ld + k;
+#pragma unroll
+    for (int sgm = 0; sgm < 6; ++sgm) row[sgm * Kp] = t[(pat >> (2 * sgm)) & 3];
+  }
+}
+
+int64_t bf16x3_kp(int64_t K) { return ceil_div(K, 8) * 8; }
+
+// Workspace of the three-term path: A' and B' (each 256-byte aligned), then
+// the split-K partials of the BF16 plan over K' = 6 Kp.
+size_t bf16x3_workspace(int64_t M, int64_t N, int64_t K, int epi, TcPlan* plan_out) {
+  const int64_t kp = bf16x3_kp(K);
+  const size_t a_bytes = ((size_t)M * 6 * kp * 2 + 255) & ~(size_t)255;
+  const size_t b_bytes = ((size_t)N * 6 * kp * 2 + 255) & ~(size_t)255;
+  const TcPlan plan = choose_plan(M, N, 6 * kp, epi, true);
+  if (plan_out) *plan_out = plan;
+  const size_t part = plan.splits > 1 ? (size_t)plan.splits * M * N * sizeof(float) : 0;
+  return a_bytes + b_bytes + part;
+}
+
+bool bf16x3_eligible(int64_t M, int64_t N, int64_t K) {
+  return (double)M * (double)N * (double)K >= kBf16x3MinMacs;
+}
+
+// op(A) [M x K] . op(B) [K x N] in F32 through the split (ta / tb as in
+// magma_gemm), output of type TC with epilogue e. Returns MAGMA_UNAVAILABLE
+// (nothing launched) when the workspace is too small, so the caller can take
+// the FFMA kernel instead.
+template <typename TC>
+magma_status_t gemm_f32_bf16x3(const float* a, const float* b, void* c, int64_t M, int64_t N,
+                               int64_t K, int64_t lda, int64_t ldb, int ta, int tb,
+                               const EpiArgs& e, void* workspace, size_t workspace_bytes,
+                               cudaStream_t s) {
+  TcPlan plan;
+  const size_t need = bf16x3_workspace(M, N, K, e.epi, &plan);
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < need ||
+      e.epi == MAGMA_EPI_ROWSTATS)
+    return MAGMA_UNAVAILABLE;
+  const int64_t kp = bf16x3_kp(K), kq = 6 * kp;
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* a2 = reinterpret_cast<__nv_bfloat16*>(w);
+  __nv_bfloat16* b2 = reinterpret_cast<__nv_bfloat16*>(
+      w + (((size_t)M * kq * 2 + 255) & ~(size_t)255));
+  float* part = reinterpret_cast<float*>(
+      reinterpret_cast<uint8_t*>(b2) + (((size_t)N * kq * 2 + 255) & ~(size_t)255));
+  // op(A)(i, k): A[i*lda + k] (ta = 0) or A[k*lda + i]; op(B)(k, j) taken as
+  // B'(j, k): B[j*ldb + k] (tb = 1) or B[k*ldb + j]
+  split_bf16x3<<<dim3((unsigned)ceil_div(kp, 32), (unsigned)ceil_div(M, 32)), 256, 0, s>>>(
+      a, M, K, ta ? 1 : lda, ta ? lda : 1, kp, kSplitPatA, a2);
+  if (magma_status_t st = check_launch("gemm_f32 split A")) return st;
+  split_bf16x3<<<dim3((unsigned)ceil_div(kp, 32), (unsigned)ceil_div(N, 32)), 256, 0, s>>>(
+      b, N, K, tb ? ldb : 1, tb ? 1 : ldb, kp, kSplitPatB, b2);
+  if (magma_status_t st = check_launch("gemm_f32 split B")) return st;
+  auto al8 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 7u) == 0; };
+  const int vec_ok = (e.ldc % 2) == 0 && al8(c) && al8(e.aux_in) && al8(e.aux_out);
+  const int vec8_ok = (e.ldc % 8) == 0 && aligned16(c);
+  const int epi_vec8 = vec8_ok && aligned16(e.aux_in) && aligned16(e.aux_out) && aligned16(e.bias);
+  const double a_bytes = 2.0 * (double)M * (double)kq, b_bytes = 2.0 * (double)N * (double)kq;
+  const int n_fast = (a_bytes > 64e6 && a_bytes >= b_bytes && N > (plan.pair ? 256 : 128)) ? 1 : 0;
+  TcArgs args{M, N, kq, c, e, device_error_word(), vec_ok, vec8_ok, epi_vec8, 0, plan.splits,
+              plan.kb_per_split, part, n_fast};
+  return dispatch_plan<TC>(plan, a2, b2, M, N, kq, kq, kq, 0, 1, args, s);
+}
+
 }  // namespace
 }  // namespace magma
 
@@ -1507,7 +1619,20 @@ extern "C" {
 
 size_t magma_gemm_workspace_size(int64_t m, int64_t n, int64_t k, magma_dtype_t ab_dtype) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;
-  if (ab_dtype == MAGMA_DTYPE_F32) return simt_workspace(m, n, k);
+  if (ab_dtype == MAGMA_DTYPE_F32) {
+    // the three-term tensor-core path where it applies (largest over the
+    // epilogue classes), else the FFMA kernel's split-K partials
+    size_t need = simt_workspace(m, n, k);
+    if (bf16x3_eligible(m, n, k)) {
+      static const int kEpisF[] = {MAGMA_EPI_NONE, MAGMA_EPI_BIAS_RESIDUAL, MAGMA_EPI_BIAS_GELU,
+                                   MAGMA_EPI_DGELU};
+      for (int epi : kEpisF) {
+        const size_t w = bf16x3_workspace(m, n, k, epi, nullptr);
+        if (w > need) need = w;
+      }
+    }
+    return need;
+  }
   if (ab_dtype != MAGMA_DTYPE_BF16) return 0;
   // The plan depends on the epilogue and output type, which this query does
   // not take: return the largest split workspace over the epilogue classes.
@@ -1584,6 +1709,18 @@ magma_status_t magma_gemm(const void* a, const void* b, void* c, int64_t m, int6
   MAGMA_REQUIRE(epilogue != MAGMA_EPI_ROWSTATS,
                 "magma_gemm: ROWSTATS needs the tensor-core path (16-byte aligned operands, "
                 "lda and ldb multiples of 8)");
+  if (ab_dtype == MAGMA_DTYPE_F32 && k > 0 && bf16x3_eligible(m, n, k)) {
+    // F32-accurate contraction on the tensor cores (three-term BF16 split);
+    // falls through to the FFMA kernel when the workspace is too small
+    const magma_status_t st =
+        c32 ? gemm_f32_bf16x3<float>(static_cast<const float*>(a), static_cast<const float*>(b), c,
+                                     m, n, k, lda, ldb, trans_a, trans_b, e, workspace,
+                                     workspace_bytes, s)
+            : gemm_f32_bf16x3<__nv_bfloat16>(static_cast<const float*>(a),
+                                             static_cast<const float*>(b), c, m, n, k, lda, ldb,
+                                             trans_a, trans_b, e, workspace, workspace_bytes, s);
+    if (st != MAGMA_UNAVAILABLE) return st;
+  }
   if (ab_dtype == MAGMA_DTYPE_F32)
     return c32 ? launch_simt<float, float>(a, b, c, m, n, k, lda, ldb, trans_a, trans_b, e,
                                            workspace, workspace_bytes, s)

@@ -363,6 +363,53 @@ def test_gemm_f32_matches_oracle(cuda, oracle, m, n, k, ta, tb):
     close(out.cpu(), ref, 1e-4)
 
 
+@pytest.mark.parametrize("m,n,k,ta,tb", [(4096, 1536, 384, 1, 0), (1536, 2048, 1024, 0, 0),
+                                          (384, 1536, 4096, 1, 1), (3000, 700, 1000, 0, 1)])
+def test_gemm_f32_tensor_core_split_matches_f64(cuda, m, n, k, ta, tb):
+    """F32 contractions large enough for the three-term BF16 split on the
+    tensor cores (every operand layout, ragged sizes) against a float64
+    product of the same F32 inputs, elementwise at rel 1e-4."""
+    from magma_b200 import ops
+
+    g = torch.Generator().manual_seed(m + 7 * n + 13 * k)
+    a = torch.randn((k, m) if ta else (m, k), generator=g)
+    b = torch.randn((n, k) if tb else (k, n), generator=g)
+    out = ops.gemm(a.cuda(), b.cuda(), trans_a=bool(ta), trans_b=bool(tb))
+    ref = (a.double().T if ta else a.double()) @ (b.double().T if tb else b.double())
+    close(out.cpu(), ref, 1e-4)
+
+
+def test_gemm_f32_tensor_core_split_epilogues(cuda):
+    """Bias + GELU (with the pre-activation), residual and GELU' epilogues of
+    the three-term path against float64 references at rel 1e-4."""
+    from magma_b200 import ops, lib
+
+    m, n, k = 8192, 1536, 384
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((m, k), generator=g)
+    w = 0.05 * torch.randn((n, k), generator=g)
+    bias = torch.randn(n, generator=g)
+    resid = torch.randn((m, n), generator=g)
+    pre64 = x.double() @ w.double().T + bias.double()
+    c = 0.7978845608
+    gelu64 = 0.5 * pre64 * (1 + torch.tanh(c * (pre64 + 0.044715 * pre64 ** 3)))
+    dev = lambda t: t.cuda()  # noqa: E731
+    pre = torch.empty((m, n), device="cuda")
+    y = ops.gemm(dev(x), dev(w), trans_b=True, epilogue=lib.EPI_BIAS_GELU, bias=dev(bias),
+                 aux_out=pre)
+    close(pre.cpu(), pre64, 1e-4)
+    close(y.cpu(), gelu64, 1e-4)
+    r = ops.gemm(dev(x), dev(w), trans_b=True, epilogue=lib.EPI_BIAS_RESIDUAL, bias=dev(bias),
+                 aux_in=dev(resid))
+    close(r.cpu(), pre64 + resid.double(), 1e-4)
+    acc64 = x.double() @ w.double().T
+    u = c * (resid.double() + 0.044715 * resid.double() ** 3)
+    t_ = torch.tanh(u)
+    dg = 0.5 * (1 + t_) + 0.5 * resid.double() * (1 - t_ * t_) * c * (1 + 3 * 0.044715 * resid.double() ** 2)
+    d = ops.gemm(dev(x), dev(w), trans_b=True, epilogue=lib.EPI_DGELU, aux_in=dev(resid))
+    close(d.cpu(), acc64 * dg, 1e-4)
+
+
 def test_gemm_rejects_bad_arguments(cuda):
     from magma_b200 import ops, lib
 

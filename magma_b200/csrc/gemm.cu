@@ -1289,7 +1289,18 @@ splitk_reduce(const float* __restrict__ ws, int splits, int64_t M, int64_t N, TC
         const int64_t i = row * N + c * 4;
         float acc[4];
         load4(ws + i, acc);
-        for (int sp = 1; sp < splits; ++sp) {
+        int sp = 1;
+        // four planes' loads in flight before their adds (same addition order)
+        for (; sp + 3 < splits; sp += 4) {
+          float t[4][4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) load4(ws + (int64_t)(sp + j) * plane + i, t[j]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[k] += t[j][k];
+        }
+        for (; sp < splits; ++sp) {
           float t[4];
           load4(ws + (int64_t)sp * plane + i, t);
 #pragma unroll

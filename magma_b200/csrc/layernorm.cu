@@ -429,32 +429,50 @@ ln_bwd_generic(const TDY* __restrict__ dy, const TX* __restrict__ x,
 }
 
 // Sums per-CTA partial rows: out_k[c] (+)= sum_b part[b][k*dim + c] for the
-// outputs k = 0, 1, 2 (dgamma, dbeta, dcol; a null output is skipped). A 32 x 8
-// CTA covers 32 columns; row y of threads sums partials b = y, y+8, ... in
-// order, then the 8 sums are added in y order (fixed order: deterministic).
-__global__ void __launch_bounds__(256)
+// outputs k = 0, 1, 2 (dgamma, dbeta, dcol; a null output is skipped). A
+// 32 x 32 CTA covers 32 columns; row y of threads sums partials b = y, y+32,
+// ... in order, issuing the loads of 8 rows before the first add (the kernel
+// is load-latency bound: ~150 partial rows of a few KB), then the 32 sums are
+// added in y order (fixed order: deterministic).
+constexpr int kReduceRows = 32;
+__global__ void __launch_bounds__(32 * kReduceRows)
 reduce_partials(const float* __restrict__ part, int nblocks, int width, float* __restrict__ out0,
                 float* __restrict__ out1, float* __restrict__ out2, int dim, int accumulate) {
-  __shared__ float red[8][33];
+  __shared__ float red[kReduceRows][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + tx;
   float s = 0.f;
   if (c < width) {
-#pragma unroll 4
-    for (int b = ty; b < nblocks; b += 8) s += part[(int64_t)b * width + c];
+    for (int b0 = ty; b0 < nblocks; b0 += 8 * kReduceRows) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int b = b0 + j * kReduceRows;
+        v[j] = b < nblocks ? part[(int64_t)b * width + c] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (b0 + j * kReduceRows < nblocks) s += v[j];
+    }
   }
   red[ty][tx] = s;
   __syncthreads();
   if (ty == 0 && c < width) {
     float t = red[0][tx];
 #pragma unroll
-    for (int y = 1; y < 8; ++y) t += red[y][tx];
+    for (int y = 1; y < kReduceRows; ++y) t += red[y][tx];
     const int k = c / dim;
     float* out = k == 0 ? out0 : (k == 1 ? out1 : out2);
     if (out == nullptr) return;
     float* dst = out + (c - k * dim);
     *dst = accumulate ? *dst + t : t;
   }
+}
+
+void launch_reduce_partials(const float* part, int nblocks, int width, float* out0, float* out1,
+                            float* out2, int dim, int accumulate, cudaStream_t stream) {
+  reduce_partials<<<(width + 31) / 32, 32 * kReduceRows, 0, stream>>>(part, nblocks, width, out0,
+                                                                      out1, out2, dim, accumulate);
 }
 
 int bwd_blocks(int64_t rows) {
@@ -575,8 +593,7 @@ magma_status_t launch_bwd(const void* dy, const void* x, const float* gamma, con
   if (magma_status_t s = check_launch("layernorm_bwd")) return s;
   if (dgamma != nullptr || dbeta != nullptr) {
     int width = 2 * dim;
-    reduce_partials<<<(width + 31) / 32, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
-                                                           nullptr, dim, acc_params);
+    launch_reduce_partials(part, blocks, width, dgamma, dbeta, nullptr, dim, acc_params, stream);
     if (magma_status_t s = check_launch("layernorm_bwd_reduce")) return s;
   }
   return MAGMA_OK;
@@ -635,8 +652,7 @@ magma_status_t launch_bwd_noalloc(const void* dy, const void* x, const float* ga
   if (magma_status_t s = check_launch("layernorm_bwd_noalloc")) return s;
   if (dgamma != nullptr || dbeta != nullptr) {
     const int width = 2 * dim;
-    reduce_partials<<<(width + 31) / 32, 256, 0, stream>>>(part, blocks, width, dgamma, dbeta,
-                                                           nullptr, dim, acc_params);
+    launch_reduce_partials(part, blocks, width, dgamma, dbeta, nullptr, dim, acc_params, stream);
     if (magma_status_t s = check_launch("layernorm_bwd_noalloc_reduce")) return s;
   }
   return MAGMA_OK;
@@ -801,8 +817,7 @@ magma_status_t magma_layernorm_bwd_residual(const void* dy, const float* x, cons
   MAGMA_REQUIRE(launched, "magma_layernorm_bwd_residual: shape not supported by the row kernels");
   if (dgamma != nullptr || dbeta != nullptr || dcol != nullptr) {
     const int width = 3 * d;
-    reduce_partials<<<(width + 31) / 32, 256, 0, s>>>(part, blocks, width, dgamma, dbeta, dcol, d,
-                                                      accumulate_params);
+    launch_reduce_partials(part, blocks, width, dgamma, dbeta, dcol, d, accumulate_params, s);
     if (magma_status_t s2 = check_launch("layernorm_bwd_residual_reduce")) return s2;
   }
   return MAGMA_OK;

@@ -29,10 +29,12 @@
 // which covers x.W^T (forward), dY.W (input gradient) and X^T.dY (weight
 // gradient) without copies.
 //
-// F32 path: a register-blocked FFMA kernel (128x128 tile, 8x8 per thread).
-// It is the F32-accurate contraction for the F32 configurations (a single
-// TF32 product rounds its operands to 10 mantissa bits, which misses a 1e-4
-// relative tolerance) and the path for shapes TMA cannot describe.
+// F32 path: contractions of at least 2^27 multiply-adds run on the same
+// tensor-core kernel through a three-term BF16 split of both operands (six
+// BF16 products per F32 product, F32 accumulation; a single TF32 or BF16
+// product would miss a 1e-4 relative tolerance). Smaller ones, calls without
+// the split's workspace and the row-statistics epilogue use a register-blocked
+// FFMA kernel (128x128 tile, 8x8 per thread), as do shapes TMA cannot describe.
 #include <cuda.h>
 
 #include <cstdio>

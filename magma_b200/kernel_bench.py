@@ -5,7 +5,9 @@
 Times each library call standalone with CUDA events after warm-up and prints
 one JSON object per kernel: duration and achieved TFLOP/s (contractions) or
 GB/s (memory-bound kernels, algorithmic bytes). ``name`` restricts the GEMM
-set to one shape (e.g. ``fc_fwd``) — handy under a profiler. ``configs`` times
+set to one shape (e.g. ``fc_fwd``) and ``configs`` to one configuration
+(``layernorm``, ``attention_bf16``, ``attention_f32``) — handy under a
+profiler. ``configs`` times
 the standalone benchmark configurations: LayerNorm F32 at [8192, 768] and
 causal attention at [8, 12, 1024, 64] in BF16 and F32, each cycling through
 buffer sets larger than L2.
@@ -282,8 +284,13 @@ def main(argv=None) -> None:
     if a.what in ("all", "ce"):
         res += bench_ce(a.reps)
     if a.what in ("all", "configs"):
-        res += [bench_layernorm_f32(a.reps), bench_attention_config(a.reps, torch.bfloat16),
-                bench_attention_config(max(2, a.reps // 10), torch.float32)]
+        cfgs = {"layernorm": lambda: bench_layernorm_f32(a.reps),
+                "attention_bf16": lambda: bench_attention_config(a.reps, torch.bfloat16),
+                "attention_f32": lambda: bench_attention_config(max(2, a.reps // 10),
+                                                                torch.float32)}
+        if a.what == "configs" and a.name is not None and a.name not in cfgs:
+            raise SystemExit(f"unknown configuration {a.name!r}: one of {sorted(cfgs)}")
+        res += [f() for k, f in cfgs.items() if a.what == "all" or a.name in (None, k)]
     for r in res:
         print(json.dumps(r), flush=True)
 

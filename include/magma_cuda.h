@@ -202,7 +202,9 @@ MAGMA_API magma_status_t magma_layernorm_bwd_residual(const void* dy, const floa
  *   trans_a = 0: A stored [m, k] (lda >= k); 1: A stored [k, m] (lda >= m).
  *   trans_b = 0: B stored [k, n] (ldb >= n); 1: B stored [n, k] (ldb >= k).
  *   c stored [m, n] (ldc >= n). ab_dtype F32 or BF16; BF16 runs on the tcgen05
- *   tensor cores with F32 accumulation, F32 runs an F32 FFMA kernel.
+ *   tensor cores with F32 accumulation; F32 runs on the same tensor cores
+ *   through a three-term BF16 split of both operands when m*n*k >= 2^27 and
+ *   the workspace holds the split (else, and for ROWSTATS, an F32 FFMA kernel).
  *   c_dtype F32 or BF16. bias is F32 [n]. aux_in / aux_out are [m, n] with
  *   leading dimension ldc: aux_in F32 for BIAS_RESIDUAL, else c_dtype-typed
  *   pre-activations; aux_out has c_dtype.

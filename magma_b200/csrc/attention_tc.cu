@@ -436,20 +436,28 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         tmem_ld32(srow, va[0]);
         tmem_ld32(srow + 32, va[1]);
         tmem_wait_ld();
-        float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+        // The pass is issue-bound: the scaled arguments and the row sums are
+        // formed two columns per instruction (packed F32 pairs; same rounding
+        // per element as scalar FMA/add), the row sum in two pair
+        // accumulators.
+        unsigned long long rs2[2] = {0ull, 0ull};
+        const unsigned long long sl22 = f2_pack(sl2, sl2), nm2 = f2_pack(-m_run, -m_run);
         // Exponentiates 32 columns starting at column c of S (v) into 16
         // packed BF16 pairs stored at P_t's columns [c/2, c/2 + 16).
         auto exp32 = [&](const uint32_t (&v)[32], int c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            float p0 = ex2_approx(fmaf(__uint_as_float(v[2 * e]), sl2, -m_run));
-            float p1 = ex2_approx(fmaf(__uint_as_float(v[2 * e + 1]), sl2, -m_run));
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])),
+                             sl22, nm2), x0, x1);
+            float p0 = ex2_approx(x0);
+            float p1 = ex2_approx(x1);
             if (masked_tile) {
               if (c + 2 * e > lim) p0 = 0.f;
               if (c + 2 * e + 1 > lim) p1 = 0.f;
             }
-            rs4[e & 3] += p0 + p1;
+            rs2[e & 1] = f2_add(rs2[e & 1], f2_pack(p0, p1));
             pk[e] = pack_bf16(p0, p1);
           }
           tmem_st16(prow + c / 2, pk);
@@ -467,7 +475,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free(t));  // all of S_t(j) is in registers
         exp32(vc, 96);
-        l_run += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+        {
+          float a0, a1, b0, b1;
+          f2_unpack(rs2[0], a0, a1);
+          f2_unpack(rs2[1], b0, b1);
+          l_run += (a0 + a1) + (b0 + b1);
+        }
         tmem_wait_st();
       }
       if (ok) {
@@ -1128,12 +1141,13 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           tma_load_4d(sQ(st), &tmQ, 0, q0, w.h, w.b, qdo_full(st));
           tma_load_4d(sdO(st), &tmdO, 0, q0, w.h, w.b, qdo_full(st));
         }
-        // lse (log2 units) and delta of query rows q0 + 4 lane .. +3
+        // -lse (log2 units; the addend of the exponent) and delta of query
+        // rows q0 + 4 lane .. +3
         float* sts = stats(st);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int row = 4 * lane + k, qi = q0 + row;
-          sts[row] = qi < a.S ? a.lse[w.bh * a.S + qi] * kLog2e : INFINITY;
+          sts[row] = qi < a.S ? -(a.lse[w.bh * a.S + qi] * kLog2e) : -INFINITY;
           sts[kTile + row] = qi < a.S ? a.delta[w.bh * a.S + qi] : 0.f;
         }
         mbar_arrive(stats_full(st));
@@ -1324,8 +1338,9 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
             tc_fence_after();
-            const float* lse_s = stats(st);
+            const float* lse_s = stats(st);  // -lse in log2 units
             const float* delta_s = lse_s + kTile;
+            const unsigned long long sl22 = f2_pack(sl2, sl2);
             const bool diag = a.causal && qt == w.kt;
             const bool tail = q0 + kTile > a.S || k0 + kTile > a.S;
             // P^T (to TMEM) and dS^T (packed, kept in pd) for 32 of this
@@ -1342,14 +1357,26 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 #pragma unroll
               for (int gg = 0; gg < 8; ++gg) {
                 const float4 lv = l4[gg], dv4 = d4[gg];
-                const float ls[4] = {lv.x, lv.y, lv.z, lv.w};
-                const float dl[4] = {dv4.x, dv4.y, dv4.z, dv4.w};
+                // P and dS two query columns per instruction (packed F32 pairs,
+                // the same rounding per element as scalar FMA/sub/mul)
+                const unsigned long long nl2[2] = {f2_pack(lv.x, lv.y), f2_pack(lv.z, lv.w)};
+                const unsigned long long dl2[2] = {f2_pack(dv4.x, dv4.y), f2_pack(dv4.z, dv4.w)};
                 float pe[4], de[4];
 #pragma unroll
+                for (int hp = 0; hp < 2; ++hp) {
+                  const int e = 4 * gg + 2 * hp;
+                  float x0, x1;
+                  f2_unpack(f2_fma(f2_pack(__uint_as_float(vs[e]), __uint_as_float(vs[e + 1])),
+                                   sl22, nl2[hp]), x0, x1);
+                  pe[2 * hp] = ex2_approx(x0);
+                  pe[2 * hp + 1] = ex2_approx(x1);
+                  f2_unpack(f2_mul(f2_pack(pe[2 * hp], pe[2 * hp + 1]),
+                                   f2_sub(f2_pack(__uint_as_float(vd[e]), __uint_as_float(vd[e + 1])),
+                                          dl2[hp])),
+                            de[2 * hp], de[2 * hp + 1]);
+                }
+#pragma unroll
                 for (int uu = 0; uu < 4; ++uu) {
-                  const int e = 4 * gg + uu;
-                  pe[uu] = ex2_approx(fmaf(__uint_as_float(vs[e]), sl2, -ls[uu]));
-                  de[uu] = pe[uu] * (__uint_as_float(vd[e]) - dl[uu]);
                   if (kMasked) {
                     const int qg = q0 + col + 4 * gg + uu;
                     if ((diag && qg < kg) || qg >= a.S || kg >= a.S) pe[uu] = de[uu] = 0.f;
